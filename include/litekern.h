@@ -1,0 +1,174 @@
+/*
+ * litekern.h - C ABI of liblitekern.so, the sm_100a kernels for litevllm's
+ * per-step hot path: paged KV-cache store, paged decode attention, chunked
+ * prefill attention over paged context, and the vocab-wide sampler.
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are device pointers unless stated otherwise. The library
+ *     allocates no device memory; the caller owns every buffer, including the
+ *     workspaces.
+ *   - Calls are asynchronous and stream-ordered on `stream` (a cudaStream_t,
+ *     NULL = legacy default stream). No entry point synchronises the host.
+ *   - The device that owns the buffers must be current on the calling thread.
+ *   - Return value: LK_OK (0) or a negative LK_ERR_* code; lk_status_string()
+ *     turns it into text. Invalid arguments are rejected before any launch.
+ *   - dtype codes: LK_DTYPE_F32 / LK_DTYPE_F16 / LK_DTYPE_BF16.
+ *   - Tensor layouts follow litevllm (reference paths relative to the
+ *     lxy-alexander/lite-vllm project root):
+ *       k_cache / v_cache : [num_blocks, block_size, num_kv_heads, head_dim],
+ *                           contiguous (litevllm/cache/kv_cache.py:41-47)
+ *       slot_mapping      : int64 [num_tokens]  (engine/model_runner.py:237)
+ *       block_tables      : int32 [B, max_blocks], zero padded
+ *                           (engine/model_runner.py:243-247)
+ *       context_lens      : int32 [B], including the token written this step
+ *                           (engine/model_runner.py:230, :248-250)
+ */
+#ifndef LITEKERN_H
+#define LITEKERN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LK_OK 0
+#define LK_ERR_INVALID_ARG (-1)
+#define LK_ERR_UNSUPPORTED (-2)
+#define LK_ERR_ALIGNMENT (-3)
+#define LK_ERR_WORKSPACE (-4)
+#define LK_ERR_CUDA (-5)
+#define LK_ERR_DRIVER (-6)
+
+#define LK_DTYPE_F32 0
+#define LK_DTYPE_F16 1
+#define LK_DTYPE_BF16 2
+
+/* Bits the kernels OR into a caller-provided device status word. */
+#define LK_STATUS_SLOT_OOB 1       /* slot_mapping entry >= num_slots or < -1 */
+#define LK_STATUS_BLOCK_OOB 2      /* block table entry outside [0, num_blocks) */
+#define LK_STATUS_WAIT_TIMEOUT 4   /* a bounded mbarrier wait gave up */
+#define LK_STATUS_CTX_OOB 8        /* context_len larger than the block table */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int lk_version(void);
+
+/* Human-readable text for an LK_* return code. Never NULL. */
+const char* lk_status_string(int code);
+
+/*
+ * KV-cache store. Replaces the advanced-index scatter in
+ * litevllm/layers/attention.py:79-84 (Attention.forward) and its twin
+ * PagedAttention.write_to_cache, litevllm/layers/attention.py:18-33:
+ *     key_cache[slot // bs, slot % bs] = key[t];  value_cache[...] = value[t]
+ * key/value: [num_tokens, num_kv_heads, head_dim] with head stride head_dim,
+ * unit element stride and a token stride given in elements. A slot of -1 is
+ * skipped (padding); any other slot outside [0, num_slots) is skipped and
+ * flagged with LK_STATUS_SLOT_OOB in *status (status may be NULL).
+ * Bit-exact copy; duplicate slots in one call are unspecified (as in torch).
+ */
+int lk_store_kv(const void* key, const void* value, void* k_cache, void* v_cache,
+                const int64_t* slot_mapping, int32_t num_tokens,
+                int32_t num_kv_heads, int32_t head_dim,
+                int64_t key_token_stride, int64_t value_token_stride,
+                int64_t num_slots, int32_t dtype, int32_t* status, void* stream);
+
+/*
+ * Paged decode attention. Replaces Attention._decode_fast,
+ * litevllm/layers/attention.py:91-139:
+ *   out[b,h,:] = softmax_s(scale * q[b,h] . k[b,s,h/G]) @ v[b,s,h/G],
+ *   s < context_lens[b], G = H / H_kv.
+ * q / out: [B, H, D] (token stride q_token_stride / out_token_stride elements,
+ * head stride D). dtype F16 or BF16; D = 128; block_size a multiple of 16;
+ * G <= 8. A context_len of 0 yields NaN rows, like the reference's softmax
+ * over an all -inf row.
+ * num_splits: split-KV factor (0 = choose automatically with
+ * lk_paged_decode_num_splits). workspace: at least
+ * lk_paged_decode_workspace_bytes(B, H, H_kv, D, num_splits) bytes, 256-byte
+ * aligned, zero-filled before its first use; every completed call leaves its
+ * counter region zero again, so one workspace serves consecutive calls on one
+ * stream. Calls that overlap on the GPU must not share a workspace.
+ */
+int lk_paged_decode_num_splits(int32_t B, int32_t H_kv, int32_t max_blocks_per_seq,
+                               int32_t block_size);
+size_t lk_paged_decode_workspace_bytes(int32_t B, int32_t H, int32_t H_kv, int32_t D,
+                                       int32_t num_splits);
+int lk_paged_decode(void* out, int64_t out_token_stride,
+                    const void* q, int64_t q_token_stride,
+                    const void* k_cache, const void* v_cache, int64_t num_blocks,
+                    const int32_t* block_tables, int64_t block_table_stride,
+                    const int32_t* context_lens,
+                    int32_t B, int32_t H, int32_t H_kv, int32_t D,
+                    int32_t block_size, int32_t max_blocks_per_seq, float scale,
+                    int32_t num_splits, void* workspace, size_t workspace_bytes,
+                    int32_t dtype, void* stream);
+
+/*
+ * Read back the status word the last decode call left in its workspace
+ * (host copy; synchronises `stream`). Returns LK_STATUS_* bits or a negative
+ * LK_ERR_* code.
+ */
+int lk_paged_decode_status(const void* workspace, void* stream);
+
+/*
+ * Chunked-prefill attention over prior paged context. The reference only has
+ * Attention._prefill (litevllm/layers/attention.py:141-151: causal SDPA over
+ * the new tokens, one sequence per call); this generalises it. Sequence b has
+ * q_len = cu_seqlens_q[b+1] - cu_seqlens_q[b] query tokens (rows
+ * cu_seqlens_q[b].. of q/out, [T, H, D]) at absolute positions
+ * prior .. prior+q_len-1, prior = context_lens[b] - q_len; query i attends key
+ * positions j <= prior + i. With block_tables != NULL, keys and values (prior
+ * and the chunk's own, already stored) come from the paged cache. With
+ * block_tables == NULL, k_cache / v_cache are the contiguous [T, H_kv, D] keys
+ * and values of the chunk (context_lens may then be NULL, meaning prior = 0):
+ * this is exactly the reference's _prefill. dtype F16 or BF16; D = 128;
+ * G in {1,2,4,8}; block_size a multiple of 16 in paged mode.
+ * status (may be NULL) receives LK_STATUS_* bits.
+ */
+int lk_paged_prefill(void* out, const void* q, int64_t q_token_stride,
+                     const void* k_cache, const void* v_cache, int64_t num_blocks,
+                     const int32_t* block_tables, int64_t block_table_stride,
+                     const int32_t* cu_seqlens_q, const int32_t* context_lens,
+                     int32_t num_seqs, int32_t max_q_len,
+                     int32_t H, int32_t H_kv, int32_t D, int32_t block_size,
+                     float scale, int32_t dtype, int32_t* status, void* stream);
+
+/*
+ * Vocab-wide sampler. Replaces Sampler.sample's greedy path
+ * (litevllm/layers/sampler.py:174-175 -> _argmax_kernel :60-84) and its
+ * temperature path (:178, :187: softmax(logits / T) then torch.multinomial)
+ * with a single pass per row:
+ *   temperatures[b] == 0 (or temperatures == NULL): argmax_v float(logits[b,v])
+ *   otherwise: argmax_v  float(logits[b,v]) / T_b + g[b,v]   (Gumbel-max)
+ * with IEEE fp32 division and addition; ties go to the lowest index; a NaN key
+ * beats every number (torch.argmax semantics). g is read from `noise`
+ * ([B, noise_ld] fp32) when non-NULL, else generated in-kernel as
+ * g = -log(-log(u)), u from Philox4x32-10 keyed by (seed, offset, b, v);
+ * noise_dump ([B, V] fp32, optional) receives the generated g.
+ * logits: [B, V] with row stride ld elements, dtype F32, F16 or BF16.
+ * out_ids: int64 [B]. workspace: lk_sample_workspace_bytes(B, V) bytes,
+ * 256-byte aligned, zero-filled before first use (the call leaves its counter
+ * region zero again).
+ */
+size_t lk_sample_workspace_bytes(int32_t B, int32_t V);
+int lk_sample(int64_t* out_ids, const void* logits, int32_t B, int32_t V, int64_t ld,
+              const float* temperatures, const float* noise, int64_t noise_ld,
+              uint64_t seed, uint64_t offset, float* noise_dump,
+              void* workspace, size_t workspace_bytes, int32_t dtype, void* stream);
+
+/*
+ * probs[b, :] = softmax(float(logits[b, :]) / temperatures[b]) in fp32, for the
+ * top-k / top-p path of Sampler.sample (replaces _triton_softmax_temp,
+ * litevllm/layers/sampler.py:127-144, including vocabularies > 65536 where the
+ * reference falls back to F.softmax).
+ */
+int lk_softmax_temp(float* probs, int64_t probs_ld, const void* logits, int32_t B,
+                    int32_t V, int64_t ld, const float* temperatures, int32_t dtype,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LITEKERN_H */

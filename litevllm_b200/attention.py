@@ -1,0 +1,140 @@
+"""Drop-in replacements for litevllm.layers.attention (Attention, PagedAttention).
+
+Same constructor and forward signature as the reference
+(litevllm/layers/attention.py:68-89), so Qwen3Attention / LlamaAttention
+(models/qwen3.py:87-92, models/llama.py:90-97) call it unchanged. Every path
+runs the liblitekern CUDA kernels; there is no PyTorch or CPU fallback.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from . import ops
+
+
+class PagedAttention:
+    """Static helpers with the reference's names (attention.py:14-65)."""
+
+    @staticmethod
+    def write_to_cache(
+        key: torch.Tensor,
+        value: torch.Tensor,
+        key_cache: torch.Tensor,
+        value_cache: torch.Tensor,
+        slot_mapping: torch.Tensor,
+    ) -> None:
+        """key_cache[slot // bs, slot % bs] = key (attention.py:18-33)."""
+        ops.store_kvcache(key, value, key_cache, value_cache, slot_mapping)
+
+    # north-star alias
+    store_kvcache = write_to_cache
+
+
+def store_kvcache(key, value, key_cache, value_cache, slot_mapping) -> None:
+    """Module-level alias of the KV store (north-star name)."""
+    ops.store_kvcache(key, value, key_cache, value_cache, slot_mapping)
+
+
+class Attention(nn.Module):
+    """Attention over the paged KV cache (reference: attention.py:68-151)."""
+
+    def __init__(self, num_heads, head_dim, num_kv_heads, scale=None):
+        super().__init__()
+        self.num_heads = num_heads
+        self.head_dim = head_dim
+        self.num_kv_heads = num_kv_heads
+        self.num_kv_groups = num_heads // num_kv_heads
+        self.scale = scale or (1.0 / (head_dim**0.5))
+
+    def forward(
+        self,
+        query,
+        key,
+        value,
+        key_cache,
+        value_cache,
+        block_table,
+        slot_mapping,
+        context_lens,
+        is_prefill=True,
+        cu_seqlens_q: Optional[torch.Tensor] = None,
+        max_q_len: Optional[int] = None,
+    ):
+        """Store the new K/V, then prefill or decode attention.
+
+        Reference semantics (attention.py:77-89): the store runs when
+        slot_mapping is given; prefill with block_table None attends the new
+        tokens only, causally (one sequence, _prefill); decode reads the
+        paged history (_decode_fast). Extension: prefill with block_table,
+        context_lens and cu_seqlens_q attends prior paged context plus the
+        chunk, for several sequences at once.
+        """
+        if slot_mapping is not None and key_cache is not None:
+            ops.store_kvcache(key, value, key_cache, value_cache, slot_mapping)
+
+        if is_prefill:
+            if block_table is None:
+                S = query.shape[0]
+                cu = torch.tensor([0, S], dtype=torch.int32, device=query.device)
+                # SDPA's default scale 1/sqrt(D), as the reference's _prefill uses.
+                return ops.paged_prefill(
+                    query, key, value, cu, S, 1.0 / (self.head_dim**0.5)
+                )
+            if cu_seqlens_q is None:
+                # one sequence whose chunk is the whole query
+                S = query.shape[0]
+                cu_seqlens_q = torch.tensor([0, S], dtype=torch.int32, device=query.device)
+                max_q_len = S
+            if max_q_len is None:
+                max_q_len = int((cu_seqlens_q[1:] - cu_seqlens_q[:-1]).max().item())
+            return ops.paged_prefill(
+                query, key_cache, value_cache, cu_seqlens_q, max_q_len, self.scale,
+                block_tables=block_table, context_lens=context_lens,
+            )
+
+        return ops.paged_decode(
+            query, key_cache, value_cache, block_table, context_lens, self.scale
+        )
+
+    def forward_mixed(
+        self,
+        query: torch.Tensor,
+        key: torch.Tensor,
+        value: torch.Tensor,
+        key_cache: torch.Tensor,
+        value_cache: torch.Tensor,
+        block_table: torch.Tensor,
+        slot_mapping: torch.Tensor,
+        context_lens: torch.Tensor,
+        cu_seqlens_q: torch.Tensor,
+        num_prefill_seqs: int,
+        num_prefill_tokens: int,
+        max_q_len: int,
+    ) -> torch.Tensor:
+        """One mixed chunked-prefill + decode step.
+
+        Rows [0, num_prefill_tokens) of query belong to the first
+        num_prefill_seqs sequences (chunks, packed by cu_seqlens_q); the
+        remaining rows are one decode token per sequence. All K/V are stored
+        first, then the prefill kernel and the decode kernel run back to back
+        on the same stream.
+        """
+        if slot_mapping is not None:
+            ops.store_kvcache(key, value, key_cache, value_cache, slot_mapping)
+        out = torch.empty_like(query)
+        P, TP = num_prefill_seqs, num_prefill_tokens
+        if P > 0:
+            ops.paged_prefill(
+                query[:TP], key_cache, value_cache, cu_seqlens_q[: P + 1], max_q_len, self.scale,
+                block_tables=block_table[:P], context_lens=context_lens[:P], out=out[:TP],
+            )
+        if query.shape[0] > TP:
+            ops.paged_decode(
+                query[TP:], key_cache, value_cache, block_table[P:], context_lens[P:], self.scale,
+                out=out[TP:],
+            )
+        return out

@@ -1,0 +1,355 @@
+// Chunked-prefill attention over prior paged context.
+//
+// The reference only has Attention._prefill (litevllm/layers/attention.py:141-151):
+// causal SDPA over the new tokens of one sequence, with query head h reading
+// KV head h / G (repeat_interleave, :147-149) and the default 1/sqrt(D) scale.
+// This kernel generalises it to a chunk that sits on top of `prior` tokens
+// already in the paged cache: query i (absolute position prior + i) attends
+// keys j <= prior + i, gathered through the block table exactly as
+// _decode_fast gathers them (attention.py:105-119). With prior = 0 and
+// contiguous keys it is _prefill.
+//
+// B200 design (flash-attention style, tensor cores for QK^T and PV):
+//  * CTA = (128-row query tile, KV head, sequence). The 128 rows are
+//    BQ = 128 / G positions x the G query heads of the KV head, so each K/V
+//    tile read from HBM serves all G heads. 8 consumer warps own 16 rows each
+//    (warp w: query head w % G, positions (w / G) * 16 ..); a 9th warp issues
+//    TMA loads of 64-token K and V tiles (four 16-token boxes each, gathered
+//    through the block table) into a 3-stage shared-memory ring.
+//  * Per tile each warp runs S = Q K^T (16 x 64) and O += P V (16 x 128) with
+//    mma.sync m16n8k16, fp32 accumulation, and an online softmax in registers;
+//    the S accumulators are re-packed as the A operand of PV without shuffles.
+#include "lk_common.cuh"
+#include "lk_host.h"
+
+namespace {
+
+constexpr int kD = 128;
+constexpr int kRows = 128;        // query rows (position x head) per CTA
+constexpr int kKT = 64;           // keys per tile
+constexpr int kNST = 3;           // pipeline stages
+constexpr int kCW = 8;            // consumer warps
+constexpr int kThreads = (kCW + 1) * 32;
+constexpr int kBoxBytes = 16 * 128;                  // 16 slots x 64 values (one head)
+constexpr int kHalfBytes = kKT * 128;                // 64 tokens x 64 values
+constexpr int kTileBytes = 2 * kHalfBytes;           // one of K or V, both d halves
+constexpr int kStageBytes = 2 * kTileBytes;          // K and V
+constexpr int kSmem = kNST * kStageBytes + 1024;
+
+struct PrefillParams {
+  void* out;
+  const void* q;
+  int64_t q_stride;     // elements between tokens of q (out is [T, H, D] contiguous)
+  const int32_t* block_tables;  // NULL: contiguous keys, slot = cu_seqlens_q[b] + pos
+  int64_t bt_stride;
+  const int32_t* cu_seqlens_q;
+  const int32_t* context_lens;  // may be NULL in contiguous mode (prior = 0)
+  int64_t num_slots;
+  int64_t num_blocks;
+  int H, G, bs, BQ;
+  float scale_log2;
+  int32_t* status;
+};
+
+template <typename T>
+LK_DEVINL void store2(T* p, float a, float b) {
+  *reinterpret_cast<uint32_t*>(p) = lk::pack2<T>(a, b);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+paged_prefill_kernel(const __grid_constant__ CUtensorMap kmap,
+                     const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[kNST];
+  __shared__ __align__(8) uint64_t empty_bar[kNST];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+  const int qt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.G, BQ = p.BQ;
+  const int q_start = p.cu_seqlens_q[b];
+  const int q_len = p.cu_seqlens_q[b + 1] - q_start;
+  const int pos0 = qt * BQ;
+  if (pos0 >= q_len) return;
+  int prior = 0;
+  if (p.block_tables != nullptr && p.context_lens != nullptr) {
+    prior = p.context_lens[b] - q_len;
+    if (prior < 0) {
+      if (threadIdx.x == 0 && p.status) atomicOr(p.status, LK_STATUS_CTX_OOB);
+      prior = 0;
+    }
+  }
+  const int kv_end = prior + min(q_len, pos0 + BQ);  // keys [0, kv_end) feed this tile
+  const int ntiles = (kv_end + kKT - 1) / kKT;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < kNST; ++s) {
+      lk::mbar_init(&full_bar[s], 1);
+      lk::mbar_init(&empty_bar[s], kCW);
+    }
+    lk::fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kCW) {
+    // ------------------------------------------------------- producer ---
+    if (lane == 0) {
+      lk::prefetch_tensormap(&kmap);
+      lk::prefetch_tensormap(&vmap);
+      const int32_t* bt =
+          p.block_tables ? p.block_tables + static_cast<int64_t>(b) * p.bt_stride : nullptr;
+      const int oob = static_cast<int>(p.num_slots < 0x7fffffffLL ? p.num_slots : 0x7fffffffLL);
+      for (int kt = 0; kt < ntiles; ++kt) {
+        const int s = kt % kNST;
+        if (!lk::mbar_wait(&empty_bar[s], ((kt / kNST) & 1) ^ 1)) {
+          if (p.status) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
+          break;
+        }
+        lk::mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+        uint8_t* dst = smem + s * kStageBytes;
+#pragma unroll
+        for (int tb = 0; tb < 4; ++tb) {
+          const int tok = kt * kKT + tb * 16;
+          int slot = oob;  // boxes past the needed keys read zeros
+          if (tok < kv_end) {
+            if (bt) {
+              const int blk = bt[tok / p.bs];
+              if (blk < 0 || blk >= p.num_blocks) {
+                if (p.status) atomicOr(p.status, LK_STATUS_BLOCK_OOB);
+              } else {
+                slot = blk * p.bs + tok % p.bs;
+              }
+            } else {
+              slot = q_start + tok;
+            }
+          }
+#pragma unroll
+          for (int dh = 0; dh < 2; ++dh) {
+            lk::tma_load_3d(dst + dh * kHalfBytes + tb * kBoxBytes, &kmap, &full_bar[s], dh * 64,
+                            slot, kvh);
+            lk::tma_load_3d(dst + kTileBytes + dh * kHalfBytes + tb * kBoxBytes, &vmap,
+                            &full_bar[s], dh * 64, slot, kvh);
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  // --------------------------------------------------------- consumers ---
+  const int g = lane >> 2, c = lane & 3;
+  const int qhead = kvh * G + warp % G;
+  const int prow = pos0 + (warp / G) * 16;  // first position of this warp's 16 rows
+  const int r0 = prow + g, r1 = prow + g + 8;
+  const int H = p.H;
+
+  uint32_t qa[8][4];
+  {
+    const T* base = static_cast<const T*>(p.q) + static_cast<int64_t>(qhead) * kD;
+    const T* q0 = base + static_cast<int64_t>(q_start + r0) * p.q_stride;
+    const T* q1 = base + static_cast<int64_t>(q_start + r1) * p.q_stride;
+    const bool v0 = r0 < q_len, v1 = r1 < q_len;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int k0 = ks * 16 + 2 * c;
+      qa[ks][0] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + k0) : 0u;
+      qa[ks][1] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + k0) : 0u;
+      qa[ks][2] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + k0 + 8) : 0u;
+      qa[ks][3] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + k0 + 8) : 0u;
+    }
+  }
+  float o[16][4];
+#pragma unroll
+  for (int dt = 0; dt < 16; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const float sl2 = p.scale_log2;
+  // Keys this warp can see: up to prior + (its last valid row).
+  const int warp_kv_end = prior + min(prow + 15, q_len - 1) + 1;
+  const uint32_t sbase = lk::smem_u32(smem);
+  const int j = lane >> 3;
+
+  for (int kt = 0; kt < ntiles; ++kt) {
+    const int s = kt % kNST;
+    if (!lk::mbar_wait(&full_bar[s], (kt / kNST) & 1)) {
+      if (lane == 0 && p.status) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
+      break;
+    }
+    if (kt * kKT < warp_kv_end) {
+      const uint32_t kb = sbase + s * kStageBytes;
+      const uint32_t vb = kb + kTileBytes;
+      float sc[8][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+        for (int nt = 0; nt < 8; nt += 2) {
+          const uint32_t tok = (nt + (j >> 1)) * 8 + (lane & 7);
+          const uint32_t chunk = ((ks & 3) << 1) + (j & 1);
+          uint32_t r[4];
+          lk::ldsm_x4(kb + (ks >> 2) * kHalfBytes + lk::swz128(tok, chunk), r[0], r[1], r[2],
+                      r[3]);
+          lk::mma16816<T>(sc[nt], qa[ks], r[0], r[1]);
+          lk::mma16816<T>(sc[nt + 1], qa[ks], r[2], r[3]);
+        }
+      }
+      // causal mask: key j visible to row i iff j <= prior + i
+      const bool need_mask = kt * kKT + kKT - 1 > prior + prow;
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = kt * kKT + nt * 8 + 2 * c + e;
+          float x0 = sc[nt][e] * sl2, x1 = sc[nt][2 + e] * sl2;
+          if (need_mask) {
+            if (key > prior + r0) x0 = -INFINITY;
+            if (key > prior + r1) x1 = -INFINITY;
+          }
+          sc[nt][e] = x0;
+          sc[nt][2 + e] = x1;
+          mx0 = fmaxf(mx0, x0);
+          mx1 = fmaxf(mx1, x1);
+        }
+      }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float ms0 = mn0 == -INFINITY ? 0.f : mn0, ms1 = mn1 == -INFINITY ? 0.f : mn1;
+      const float al0 = exp2f(m0 - ms0), al1 = exp2f(m1 - ms1);
+      m0 = mn0;
+      m1 = mn1;
+      float ps0 = 0.f, ps1 = 0.f;
+      uint32_t pa[4][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const float e0 = exp2f(sc[nt][0] - ms0), e1 = exp2f(sc[nt][1] - ms0);
+        const float e2 = exp2f(sc[nt][2] - ms1), e3 = exp2f(sc[nt][3] - ms1);
+        ps0 += e0 + e1;
+        ps1 += e2 + e3;
+        pa[nt >> 1][(nt & 1) * 2 + 0] = lk::pack2<T>(e0, e1);
+        pa[nt >> 1][(nt & 1) * 2 + 1] = lk::pack2<T>(e2, e3);
+      }
+      l0 = l0 * al0 + ps0;
+      l1 = l1 * al1 + ps1;
+#pragma unroll
+      for (int dt = 0; dt < 16; ++dt) {
+        o[dt][0] *= al0;
+        o[dt][1] *= al0;
+        o[dt][2] *= al1;
+        o[dt][3] *= al1;
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+        for (int dt = 0; dt < 16; dt += 2) {
+          const uint32_t tok = kk * 16 + (j & 1) * 8 + (lane & 7);
+          const uint32_t dchunk = dt + (j >> 1);
+          uint32_t r[4];
+          lk::ldsm_x4_t(vb + (dchunk >> 3) * kHalfBytes + lk::swz128(tok, dchunk & 7), r[0],
+                        r[1], r[2], r[3]);
+          lk::mma16816<T>(o[dt], pa[kk], r[0], r[1]);
+          lk::mma16816<T>(o[dt + 1], pa[kk], r[2], r[3]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) lk::mbar_arrive(&empty_bar[s]);
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float i0 = 1.f / l0, i1 = 1.f / l1;
+  T* out = static_cast<T*>(p.out) + static_cast<int64_t>(qhead) * kD + 2 * c;
+  const int64_t ostride = static_cast<int64_t>(H) * kD;
+  if (r0 < q_len) {
+    T* o0 = out + static_cast<int64_t>(q_start + r0) * ostride;
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) store2<T>(o0 + dt * 8, o[dt][0] * i0, o[dt][1] * i0);
+  }
+  if (r1 < q_len) {
+    T* o1 = out + static_cast<int64_t>(q_start + r1) * ostride;
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) store2<T>(o1 + dt * 8, o[dt][2] * i1, o[dt][3] * i1);
+  }
+}
+
+template <typename T>
+int launch_prefill(const CUtensorMap& km, const CUtensorMap& vm, const PrefillParams& p,
+                   int num_seqs, int max_q_len, int H_kv, cudaStream_t s) {
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(paged_prefill_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmem) != cudaSuccess)
+      return LK_ERR_CUDA;
+    configured[dev] = 1;
+  }
+  dim3 grid((max_q_len + p.BQ - 1) / p.BQ, H_kv, num_seqs);
+  paged_prefill_kernel<T><<<grid, kThreads, kSmem, s>>>(km, vm, p);
+  return lk::check_launch();
+}
+
+}  // namespace
+
+extern "C" int lk_paged_prefill(void* out, const void* q, int64_t q_token_stride,
+                                const void* k_cache, const void* v_cache, int64_t num_blocks,
+                                const int32_t* block_tables, int64_t block_table_stride,
+                                const int32_t* cu_seqlens_q, const int32_t* context_lens,
+                                int32_t num_seqs, int32_t max_q_len, int32_t H, int32_t H_kv,
+                                int32_t D, int32_t block_size, float scale, int32_t dtype,
+                                int32_t* status, void* stream) {
+  if (num_seqs < 0 || max_q_len < 0 || H <= 0 || H_kv <= 0 || H % H_kv != 0 || num_blocks <= 0)
+    return LK_ERR_INVALID_ARG;
+  if (num_seqs == 0 || max_q_len == 0) return LK_OK;
+  if (!out || !q || !k_cache || !v_cache || !cu_seqlens_q) return LK_ERR_INVALID_ARG;
+  if (dtype != LK_DTYPE_BF16 && dtype != LK_DTYPE_F16) return LK_ERR_UNSUPPORTED;
+  const int G = H / H_kv;
+  if (D != kD || (G != 1 && G != 2 && G != 4 && G != 8)) return LK_ERR_UNSUPPORTED;
+  if (num_seqs > 65535 || H_kv > 65535) return LK_ERR_INVALID_ARG;
+  // Paged mode: num_blocks blocks of block_size slots. Contiguous mode: the
+  // key tensor holds num_blocks tokens (block_size is ignored).
+  int64_t num_slots;
+  if (block_tables) {
+    if (block_size <= 0 || block_size % 16 != 0) return LK_ERR_UNSUPPORTED;
+    num_slots = num_blocks * block_size;
+  } else {
+    num_slots = num_blocks;
+  }
+  if (num_slots > 0x7fffffffLL) return LK_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(q) & 3u) || (q_token_stride & 1) ||
+      (reinterpret_cast<uintptr_t>(out) & 3u))
+    return LK_ERR_ALIGNMENT;
+  CUtensorMap km, vm;
+  int rc = lk::get_kv_tensor_map(&km, k_cache, num_slots, H_kv, D, dtype, 16, 1);
+  if (rc != LK_OK) return rc;
+  rc = lk::get_kv_tensor_map(&vm, v_cache, num_slots, H_kv, D, dtype, 16, 1);
+  if (rc != LK_OK) return rc;
+  PrefillParams p;
+  p.out = out;
+  p.q = q;
+  p.q_stride = q_token_stride;
+  p.block_tables = block_tables;
+  p.bt_stride = block_table_stride;
+  p.cu_seqlens_q = cu_seqlens_q;
+  p.context_lens = context_lens;
+  p.num_slots = num_slots;
+  p.num_blocks = block_tables ? num_blocks : 1;
+  p.H = H;
+  p.G = G;
+  p.bs = block_tables ? block_size : 16;
+  p.BQ = kRows / G;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.status = status;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == LK_DTYPE_BF16)
+    return launch_prefill<__nv_bfloat16>(km, vm, p, num_seqs, max_q_len, H_kv, s);
+  return launch_prefill<__half>(km, vm, p, num_seqs, max_q_len, H_kv, s);
+}

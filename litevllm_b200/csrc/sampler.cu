@@ -1,0 +1,447 @@
+// Vocab-wide sampler: one pass over each logits row picks
+//   greedy rows (T == 0):  argmax_v float(x[v])
+//   sampled rows (T > 0):  argmax_v float(x[v]) / T + g[v]     (Gumbel-max)
+// Restates Sampler.sample, litevllm/layers/sampler.py:147-187: the greedy
+// branch (_triton_argmax / _argmax_kernel, :60-84, :111-124: fp32 compare,
+// first index wins ties) and the temperature branch (:178, :187,
+// softmax(x / T) then a categorical draw). Gumbel-max draws from exactly
+// softmax(x / T); the draw is a pure function of the noise g, so it is
+// reproducible from a noise tensor, which torch.multinomial's is not.
+//
+// B200 design: the vocabulary of each row is cut into chunks, one CTA per
+// (chunk, row), so that even a handful of rows covers every SM. Each thread
+// streams 16-byte vectors (8 bf16 logits) with several loads in flight, keeps
+// a running (key, index) best, and the CTA reduces with warp shuffles then
+// shared memory. The last CTA of a row to finish (atomic counter, no
+// waiting) reduces the per-chunk winners and writes the int64 token id.
+//
+// In-kernel noise: u = ((r >> 9) + 0.5) * 2^-23 with r from Philox4x32-10
+// (Salmon, Moraes, Dror, Shaw, "Parallel Random Numbers: As Easy as 1, 2, 3",
+// SC'11) keyed by the 64-bit seed, counter (v / 4, b, offset_lo, offset_hi);
+// word v % 4 of the block feeds element v. g = -log(-log(u)) with CUDA logf.
+#include "lk_common.cuh"
+#include "lk_host.h"
+
+#include <type_traits>
+
+namespace {
+
+constexpr int kSampThreads = 256;
+constexpr int kVec = 8;  // elements per 16-byte vector of 16-bit logits
+
+struct SampleParams {
+  const void* logits;
+  int64_t ld;
+  int V;
+  int chunk;      // elements per CTA (multiple of kVec)
+  int nchunks;
+  const float* temps;
+  const float* noise;
+  int64_t noise_ld;
+  uint32_t seed_lo, seed_hi, off_lo, off_hi;
+  float* noise_dump;
+  int64_t* out;
+  float* part_key;   // [B][nchunks]
+  int32_t* part_idx; // [B][nchunks]
+  int32_t* counters; // [B]
+};
+
+// ------------------------------------------------------------- Philox ---
+struct U4 { uint32_t x, y, z, w; };
+
+LK_DEVINL U4 philox4x32_10(U4 c, uint32_t k0, uint32_t k1) {
+  constexpr uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u;
+  constexpr uint32_t W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t hi0 = __umulhi(M0, c.x), lo0 = M0 * c.x;
+    const uint32_t hi1 = __umulhi(M1, c.z), lo1 = M1 * c.z;
+    c = U4{hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0};
+    k0 += W0;
+    k1 += W1;
+  }
+  return c;
+}
+
+LK_DEVINL float gumbel_from_bits(uint32_t r) {
+  const float u = (static_cast<float>(r >> 9) + 0.5f) * 1.1920928955078125e-07f;  // 2^-23
+  return -logf(-logf(u));
+}
+
+// ---------------------------------------------------------- comparisons ---
+// a beats the current best (b) if it is larger, or NaN where b is not; the
+// caller visits indices in increasing order so equal keys keep the earlier.
+LK_DEVINL bool beats_later(float a, float b) {
+  return a > b || (a != a && b == b);
+}
+// Full comparison for merging two candidates with explicit indices.
+LK_DEVINL bool beats(float ka, int ia, float kb, int ib) {
+  const bool na = ka != ka, nb = kb != kb;
+  if (na != nb) return na;
+  if (na) return ia < ib;
+  return ka > kb || (ka == kb && ia < ib);
+}
+
+template <typename T> struct Load16;
+template <> struct Load16<__nv_bfloat16> {
+  LK_DEVINL static void cvt(const uint4& v, float (&f)[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+};
+template <> struct Load16<__half> {
+  LK_DEVINL static void cvt(const uint4& v, float (&f)[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+      float2 t = __half22float2(h);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  }
+};
+template <> struct Load16<float> {};
+
+template <typename T, bool VEC, int MODE>  // MODE 0 greedy, 1 noise tensor, 2 in-kernel RNG
+LK_DEVINL void scan_chunk(const SampleParams& p, int b, int v0, int v1, float temp, float& best,
+                          int& besti) {
+  const T* row = static_cast<const T*>(p.logits) + static_cast<int64_t>(b) * p.ld;
+  const float* nrow = MODE == 1 ? p.noise + static_cast<int64_t>(b) * p.noise_ld : nullptr;
+  float* drow = (MODE == 2 && p.noise_dump) ? p.noise_dump + static_cast<int64_t>(b) * p.V : nullptr;
+
+  auto visit = [&](float x, int v, float g) {
+    float key;
+    if constexpr (MODE == 0) key = x;
+    else key = __fadd_rn(__fdiv_rn(x, temp), g);
+    if (beats_later(key, best)) {
+      best = key;
+      besti = v;
+    }
+  };
+
+  int vs = v0;
+  if constexpr (VEC && !std::is_same<T, float>::value) {
+    const int vend = v0 + ((min(v1, p.V) - v0) / kVec) * kVec;
+    constexpr int kU = 4;
+    int v = v0 + threadIdx.x * kVec;
+    for (; v + (kU - 1) * kSampThreads * kVec < vend; v += kU * kSampThreads * kVec) {
+      uint4 raw[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        raw[u] = __ldcs(reinterpret_cast<const uint4*>(row + v + u * kSampThreads * kVec));
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        float f[8];
+        Load16<T>::cvt(raw[u], f);
+        const int vv = v + u * kSampThreads * kVec;
+        float g[8];
+        if constexpr (MODE == 1) {
+          const float4 a = __ldcs(reinterpret_cast<const float4*>(nrow + vv));
+          const float4 c = __ldcs(reinterpret_cast<const float4*>(nrow + vv + 4));
+          g[0] = a.x; g[1] = a.y; g[2] = a.z; g[3] = a.w;
+          g[4] = c.x; g[5] = c.y; g[6] = c.z; g[7] = c.w;
+        } else if constexpr (MODE == 2) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const U4 r = philox4x32_10(U4{static_cast<uint32_t>((vv >> 2) + h),
+                                          static_cast<uint32_t>(b), p.off_lo, p.off_hi},
+                                       p.seed_lo, p.seed_hi);
+            g[4 * h + 0] = gumbel_from_bits(r.x);
+            g[4 * h + 1] = gumbel_from_bits(r.y);
+            g[4 * h + 2] = gumbel_from_bits(r.z);
+            g[4 * h + 3] = gumbel_from_bits(r.w);
+          }
+          if (drow) {
+            reinterpret_cast<float4*>(drow + vv)[0] = make_float4(g[0], g[1], g[2], g[3]);
+            reinterpret_cast<float4*>(drow + vv)[1] = make_float4(g[4], g[5], g[6], g[7]);
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) visit(f[e], vv + e, MODE == 0 ? 0.f : g[e]);
+      }
+    }
+    for (; v < vend; v += kSampThreads * kVec) {
+      const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(row + v));
+      float f[8];
+      Load16<T>::cvt(raw, f);
+      float g[8];
+      if constexpr (MODE == 1) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) g[e] = nrow[v + e];
+      } else if constexpr (MODE == 2) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const U4 r = philox4x32_10(U4{static_cast<uint32_t>((v >> 2) + h),
+                                        static_cast<uint32_t>(b), p.off_lo, p.off_hi},
+                                     p.seed_lo, p.seed_hi);
+          g[4 * h + 0] = gumbel_from_bits(r.x);
+          g[4 * h + 1] = gumbel_from_bits(r.y);
+          g[4 * h + 2] = gumbel_from_bits(r.z);
+          g[4 * h + 3] = gumbel_from_bits(r.w);
+        }
+        if (drow) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) drow[v + e] = g[e];
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) visit(f[e], v + e, MODE == 0 ? 0.f : g[e]);
+    }
+    vs = vend;
+  }
+  // Scalar path: unaligned rows, fp32 logits, and the ragged tail.
+  const int vend = min(v1, p.V);
+  for (int v = vs + threadIdx.x; v < vend; v += kSampThreads) {
+    const float x = lk::Elem<T>::to_f(row[v]);
+    float g = 0.f;
+    if constexpr (MODE == 1) {
+      g = nrow[v];
+    } else if constexpr (MODE == 2) {
+      const U4 r = philox4x32_10(U4{static_cast<uint32_t>(v >> 2), static_cast<uint32_t>(b),
+                                    p.off_lo, p.off_hi},
+                                 p.seed_lo, p.seed_hi);
+      const uint32_t w = (v & 3) == 0 ? r.x : (v & 3) == 1 ? r.y : (v & 3) == 2 ? r.z : r.w;
+      g = gumbel_from_bits(w);
+      if (drow) drow[v] = g;
+    }
+    visit(x, v, g);
+  }
+}
+
+LK_DEVINL void reduce_pair(float& k, int& i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float k2 = __shfl_xor_sync(0xffffffffu, k, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, i, o);
+    if (beats(k2, i2, k, i)) {
+      k = k2;
+      i = i2;
+    }
+  }
+}
+
+// Block-wide (key, index) reduction; result valid in thread 0.
+LK_DEVINL void block_reduce(float& k, int& i) {
+  __shared__ float sk[kSampThreads / 32];
+  __shared__ int si[kSampThreads / 32];
+  reduce_pair(k, i);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    sk[w] = k;
+    si[w] = i;
+  }
+  __syncthreads();
+  if (w == 0) {
+    k = l < kSampThreads / 32 ? sk[l] : -INFINITY;
+    i = l < kSampThreads / 32 ? si[l] : 0x7fffffff;
+    reduce_pair(k, i);
+  }
+}
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(kSampThreads) sample_kernel(const SampleParams p) {
+  const int ch = blockIdx.x, b = blockIdx.y;
+  const float temp = p.temps ? p.temps[b] : 0.f;
+  const int v0 = ch * p.chunk, v1 = min(p.V, v0 + p.chunk);
+  float best = -INFINITY;
+  int besti = 0x7fffffff;
+  if (!(temp > 0.f)) scan_chunk<T, VEC, 0>(p, b, v0, v1, temp, best, besti);
+  else if (p.noise) scan_chunk<T, VEC, 1>(p, b, v0, v1, temp, best, besti);
+  else scan_chunk<T, VEC, 2>(p, b, v0, v1, temp, best, besti);
+  block_reduce(best, besti);
+  if (p.nchunks == 1) {
+    if (threadIdx.x == 0) p.out[b] = besti == 0x7fffffff ? 0 : besti;
+    return;
+  }
+  __shared__ int s_last;
+  if (threadIdx.x == 0) {
+    p.part_key[static_cast<int64_t>(b) * p.nchunks + ch] = best;
+    p.part_idx[static_cast<int64_t>(b) * p.nchunks + ch] = besti;
+    __threadfence();
+    const int prev = atomicAdd(p.counters + b, 1);
+    s_last = prev == p.nchunks - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  float k = -INFINITY;
+  int i = 0x7fffffff;
+  for (int c = threadIdx.x; c < p.nchunks; c += kSampThreads) {
+    const float k2 = __ldcg(p.part_key + static_cast<int64_t>(b) * p.nchunks + c);
+    const int i2 = __ldcg(p.part_idx + static_cast<int64_t>(b) * p.nchunks + c);
+    if (beats(k2, i2, k, i)) {
+      k = k2;
+      i = i2;
+    }
+  }
+  block_reduce(k, i);
+  if (threadIdx.x == 0) {
+    p.out[b] = i == 0x7fffffff ? 0 : i;
+    p.counters[b] = 0;
+  }
+}
+
+// ---------------------------------------------------- softmax(x / T) ---
+template <typename T>
+__global__ void __launch_bounds__(kSampThreads)
+softmax_temp_kernel(float* __restrict__ probs, int64_t probs_ld, const T* __restrict__ logits,
+                    int V, int64_t ld, const float* __restrict__ temps) {
+  const int b = blockIdx.x;
+  const T* row = logits + static_cast<int64_t>(b) * ld;
+  const float t = temps ? temps[b] : 1.f;
+  float m = -INFINITY, s = 0.f;
+  for (int v = threadIdx.x; v < V; v += kSampThreads) {
+    const float x = __fdiv_rn(lk::Elem<T>::to_f(row[v]), t);
+    if (x > m) {
+      s = s * __expf(m - x) + 1.f;
+      m = x;
+    } else {
+      s += __expf(x - m);
+    }
+  }
+  __shared__ float sm[kSampThreads / 32], ss[kSampThreads / 32];
+  __shared__ float gm, gs;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    const float mm = fmaxf(m, m2);
+    s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
+    m = mm;
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sm[threadIdx.x >> 5] = m;
+    ss[threadIdx.x >> 5] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float M = -INFINITY;
+    for (int w = 0; w < kSampThreads / 32; ++w) M = fmaxf(M, sm[w]);
+    float S = 0.f;
+    for (int w = 0; w < kSampThreads / 32; ++w)
+      S += sm[w] == -INFINITY ? 0.f : ss[w] * __expf(sm[w] - M);
+    gm = M;
+    gs = S;
+  }
+  __syncthreads();
+  const float M = gm, inv = 1.f / gs;
+  float* prow = probs + static_cast<int64_t>(b) * probs_ld;
+  for (int v = threadIdx.x; v < V; v += kSampThreads)
+    prow[v] = __expf(__fdiv_rn(lk::Elem<T>::to_f(row[v]), t) - M) * inv;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+int choose_chunks(int B, int V) {
+  // ~4 CTAs per SM over the whole batch, chunks of at least 4096 elements.
+  const int64_t target = 4LL * lk::num_sms();
+  int64_t n = (target + B - 1) / B;
+  const int64_t maxn = (V + 4095) / 4096;
+  if (n > maxn) n = maxn;
+  if (n < 1) n = 1;
+  if (n > 1024) n = 1024;
+  return static_cast<int>(n);
+}
+
+template <typename T>
+int launch_sample(const SampleParams& p, int B, bool vec, cudaStream_t s) {
+  dim3 grid(p.nchunks, B);
+  if (vec) sample_kernel<T, true><<<grid, kSampThreads, 0, s>>>(p);
+  else sample_kernel<T, false><<<grid, kSampThreads, 0, s>>>(p);
+  return lk::check_launch();
+}
+
+}  // namespace
+
+extern "C" size_t lk_sample_workspace_bytes(int32_t B, int32_t V) {
+  if (B <= 0 || V <= 0) return 0;
+  const int n = choose_chunks(B, V);
+  return align256(static_cast<size_t>(B) * 4) + 2 * align256(static_cast<size_t>(B) * n * 4);
+}
+
+extern "C" int lk_sample(int64_t* out_ids, const void* logits, int32_t B, int32_t V, int64_t ld,
+                         const float* temperatures, const float* noise, int64_t noise_ld,
+                         uint64_t seed, uint64_t offset, float* noise_dump, void* workspace,
+                         size_t workspace_bytes, int32_t dtype, void* stream) {
+  if (B < 0 || V <= 0 || ld < V) return LK_ERR_INVALID_ARG;
+  if (B == 0) return LK_OK;
+  if (!out_ids || !logits || B > 65535) return LK_ERR_INVALID_ARG;
+  if (noise && noise_ld < V) return LK_ERR_INVALID_ARG;
+  if (dtype != LK_DTYPE_F32 && dtype != LK_DTYPE_F16 && dtype != LK_DTYPE_BF16)
+    return LK_ERR_UNSUPPORTED;
+  SampleParams p;
+  p.logits = logits;
+  p.ld = ld;
+  p.V = V;
+  p.nchunks = choose_chunks(B, V);
+  const int64_t per = (static_cast<int64_t>(V) + p.nchunks - 1) / p.nchunks;
+  p.chunk = static_cast<int>(((per + kVec - 1) / kVec) * kVec);
+  p.nchunks = static_cast<int>((V + static_cast<int64_t>(p.chunk) - 1) / p.chunk);
+  p.temps = temperatures;
+  p.noise = noise;
+  p.noise_ld = noise_ld;
+  p.seed_lo = static_cast<uint32_t>(seed);
+  p.seed_hi = static_cast<uint32_t>(seed >> 32);
+  p.off_lo = static_cast<uint32_t>(offset);
+  p.off_hi = static_cast<uint32_t>(offset >> 32);
+  p.noise_dump = noise_dump;
+  p.out = out_ids;
+  if (p.nchunks > 1) {
+    const size_t need = lk_sample_workspace_bytes(B, V);
+    if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+      return LK_ERR_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    p.counters = reinterpret_cast<int32_t*>(ws);
+    const size_t cb = align256(static_cast<size_t>(B) * 4);
+    const size_t kb = align256(static_cast<size_t>(B) * choose_chunks(B, V) * 4);
+    p.part_key = reinterpret_cast<float*>(ws + cb);
+    p.part_idx = reinterpret_cast<int32_t*>(ws + cb + kb);
+  } else {
+    p.counters = nullptr;
+    p.part_key = nullptr;
+    p.part_idx = nullptr;
+  }
+  const int esz = lk::dtype_size(dtype);
+  const bool vec = dtype != LK_DTYPE_F32 &&
+                   (reinterpret_cast<uintptr_t>(logits) & 15u) == 0 && ((ld * esz) & 15) == 0 &&
+                   (!noise || (((reinterpret_cast<uintptr_t>(noise) & 15u) == 0) &&
+                               ((noise_ld * 4) & 15) == 0)) &&
+                   (!noise_dump || ((reinterpret_cast<uintptr_t>(noise_dump) & 15u) == 0 &&
+                                    ((static_cast<int64_t>(V) * 4) & 15) == 0));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case LK_DTYPE_BF16: return launch_sample<__nv_bfloat16>(p, B, vec, s);
+    case LK_DTYPE_F16: return launch_sample<__half>(p, B, vec, s);
+    default: return launch_sample<float>(p, B, false, s);
+  }
+}
+
+extern "C" int lk_softmax_temp(float* probs, int64_t probs_ld, const void* logits, int32_t B,
+                               int32_t V, int64_t ld, const float* temperatures, int32_t dtype,
+                               void* stream) {
+  if (B < 0 || V <= 0 || ld < V || probs_ld < V) return LK_ERR_INVALID_ARG;
+  if (B == 0) return LK_OK;
+  if (!probs || !logits) return LK_ERR_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case LK_DTYPE_BF16:
+      softmax_temp_kernel<__nv_bfloat16><<<B, kSampThreads, 0, s>>>(
+          probs, probs_ld, static_cast<const __nv_bfloat16*>(logits), V, ld, temperatures);
+      break;
+    case LK_DTYPE_F16:
+      softmax_temp_kernel<__half><<<B, kSampThreads, 0, s>>>(
+          probs, probs_ld, static_cast<const __half*>(logits), V, ld, temperatures);
+      break;
+    case LK_DTYPE_F32:
+      softmax_temp_kernel<float><<<B, kSampThreads, 0, s>>>(
+          probs, probs_ld, static_cast<const float*>(logits), V, ld, temperatures);
+      break;
+    default: return LK_ERR_UNSUPPORTED;
+  }
+  return lk::check_launch();
+}

@@ -1,0 +1,347 @@
+"""PyTorch-facing wrappers of the liblitekern C ABI.
+
+Every function validates dtype / device / layout, then calls one C entry
+point on the current CUDA stream of the tensors' device. Nothing here
+computes on the host: a CPU tensor or a missing library raises.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from ._lib import LK_DTYPE_BF16, LK_DTYPE_F16, LK_DTYPE_F32, check, lib
+
+_DTYPES = {torch.float32: LK_DTYPE_F32, torch.float16: LK_DTYPE_F16, torch.bfloat16: LK_DTYPE_BF16}
+
+
+def _dtype_code(t: torch.Tensor, allowed=(torch.float16, torch.bfloat16)) -> int:
+    if t.dtype not in allowed:
+        raise TypeError(f"dtype {t.dtype} not supported here (allowed: {allowed})")
+    return _DTYPES[t.dtype]
+
+
+def _cuda(*ts: Optional[torch.Tensor]) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("litevllm_b200 kernels run on CUDA tensors only (no CPU fallback)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} vs {t.device}")
+    assert dev is not None
+    return dev
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+class _Workspaces:
+    """Zero-initialised scratch buffers, one per (device, purpose).
+
+    The kernels leave their counter regions zero after every call, so a
+    buffer is reused across calls on one stream without re-clearing.
+    """
+
+    def __init__(self) -> None:
+        self._bufs: dict[tuple, torch.Tensor] = {}
+
+    def get(self, dev: torch.device, name: str, nbytes: int) -> torch.Tensor:
+        key = (dev.index, name)
+        buf = self._bufs.get(key)
+        if buf is None or buf.numel() < nbytes:
+            size = max(nbytes, 1 << 16)
+            if buf is not None:
+                size = max(size, buf.numel() * 2)
+            buf = torch.zeros(size, dtype=torch.uint8, device=dev)
+            self._bufs[key] = buf
+        return buf
+
+
+WORKSPACES = _Workspaces()
+
+
+# --------------------------------------------------------------- KV store ---
+def store_kvcache(
+    key: torch.Tensor,
+    value: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    status: Optional[torch.Tensor] = None,
+) -> None:
+    """key_cache[slot // bs, slot % bs] = key[t] (and value), for every t.
+
+    key/value: [T, H_kv, D]; caches [num_blocks, bs, H_kv, D] contiguous;
+    slot_mapping int64 [T]. Mirrors litevllm/layers/attention.py:79-84.
+    """
+    dev = _cuda(key, value, key_cache, value_cache, slot_mapping, status)
+    if key.dim() != 3 or value.shape != key.shape:
+        raise ValueError("key/value must be [T, H_kv, D] with equal shapes")
+    T, H_kv, D = key.shape
+    if key_cache.dim() != 4 or key_cache.shape[2:] != (H_kv, D) or value_cache.shape != key_cache.shape:
+        raise ValueError("caches must be [num_blocks, block_size, H_kv, D]")
+    if not (key_cache.is_contiguous() and value_cache.is_contiguous()):
+        raise ValueError("caches must be contiguous")
+    for t in (key, value):
+        if t.stride(2) != 1 or t.stride(1) != D:
+            raise ValueError("key/value must have unit d-stride and head stride D")
+    if key.dtype != key_cache.dtype or value.dtype != key_cache.dtype:
+        raise TypeError("key/value dtype must match the cache dtype")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.numel() != T:
+        raise TypeError("slot_mapping must be int64 [T]")
+    slot_mapping = slot_mapping.contiguous()
+    code = _dtype_code(key_cache, (torch.float32, torch.float16, torch.bfloat16))
+    num_slots = key_cache.shape[0] * key_cache.shape[1]
+    with torch.cuda.device(dev):
+        check(
+            lib().lk_store_kv(
+                key.data_ptr(), value.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
+                slot_mapping.data_ptr(), T, H_kv, D, key.stride(0), value.stride(0), num_slots,
+                code, _ptr(status), _stream(dev),
+            )
+        )
+
+
+# ----------------------------------------------------------- paged decode ---
+def decode_num_splits(B: int, H_kv: int, max_blocks: int, block_size: int) -> int:
+    return int(lib().lk_paged_decode_num_splits(B, H_kv, max_blocks, block_size))
+
+
+def decode_workspace_bytes(B: int, H: int, H_kv: int, D: int, num_splits: int) -> int:
+    return int(lib().lk_paged_decode_workspace_bytes(B, H, H_kv, D, num_splits))
+
+
+def paged_decode(
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    context_lens: torch.Tensor,
+    scale: float,
+    num_splits: int = 0,
+    out: Optional[torch.Tensor] = None,
+    workspace: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """Single-token paged attention; mirrors Attention._decode_fast
+    (litevllm/layers/attention.py:91-139). query [B, H, D] -> [B, H, D]."""
+    dev = _cuda(query, key_cache, value_cache, block_tables, context_lens, out, workspace)
+    if query.dim() != 3:
+        raise ValueError("query must be [B, H, D]")
+    B, H, D = query.shape
+    nb, bs, H_kv, Dk = key_cache.shape
+    if Dk != D or value_cache.shape != key_cache.shape:
+        raise ValueError("cache shape mismatch")
+    if not (key_cache.is_contiguous() and value_cache.is_contiguous()):
+        raise ValueError("caches must be contiguous")
+    if query.dtype != key_cache.dtype:
+        raise TypeError("query dtype must match the cache dtype")
+    if query.stride(2) != 1 or query.stride(1) != D:
+        raise ValueError("query must have unit d-stride and head stride D")
+    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or block_tables.shape[0] != B:
+        raise TypeError("block_tables must be int32 [B, max_blocks]")
+    if block_tables.stride(1) != 1:
+        block_tables = block_tables.contiguous()
+    if context_lens.dtype != torch.int32 or context_lens.numel() != B:
+        raise TypeError("context_lens must be int32 [B]")
+    context_lens = context_lens.contiguous()
+    code = _dtype_code(query)
+    if out is None:
+        out = torch.empty((B, H, D), dtype=query.dtype, device=dev)
+    elif out.shape != (B, H, D) or out.dtype != query.dtype or out.stride(2) != 1 or out.stride(1) != D:
+        raise ValueError("bad out tensor")
+    if B == 0:
+        return out
+    max_blocks = block_tables.shape[1]
+    if num_splits <= 0:
+        num_splits = decode_num_splits(B, H_kv, max_blocks, bs)
+    need = decode_workspace_bytes(B, H, H_kv, D, num_splits)
+    if workspace is None:
+        workspace = WORKSPACES.get(dev, "decode", need)
+    elif workspace.numel() * workspace.element_size() < need:
+        raise ValueError(f"workspace too small: need {need} bytes")
+    with torch.cuda.device(dev):
+        check(
+            lib().lk_paged_decode(
+                out.data_ptr(), out.stride(0), query.data_ptr(), query.stride(0),
+                key_cache.data_ptr(), value_cache.data_ptr(), nb, block_tables.data_ptr(),
+                block_tables.stride(0), context_lens.data_ptr(), B, H, H_kv, D, bs, max_blocks,
+                float(scale), num_splits, workspace.data_ptr(),
+                workspace.numel() * workspace.element_size(), code, _stream(dev),
+            )
+        )
+    return out
+
+
+def decode_status(workspace: Optional[torch.Tensor] = None, device=None) -> int:
+    """Read (and clear) the LK_STATUS_* bits the decode kernels left in their
+    workspace. Synchronises the current stream."""
+    if workspace is None:
+        dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        workspace = WORKSPACES.get(dev, "decode", 256)
+    v = int(workspace[:4].view(torch.int32).item())
+    workspace[:4].zero_()
+    return v
+
+
+# --------------------------------------------------------- paged prefill ---
+def paged_prefill(
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    cu_seqlens_q: torch.Tensor,
+    max_q_len: int,
+    scale: float,
+    block_tables: Optional[torch.Tensor] = None,
+    context_lens: Optional[torch.Tensor] = None,
+    out: Optional[torch.Tensor] = None,
+    status: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """Causal attention for prefill chunks over prior paged context.
+
+    query [T, H, D] packed by cu_seqlens_q (int32 [S+1]). Paged mode
+    (block_tables given): caches [num_blocks, bs, H_kv, D], context_lens =
+    prior + chunk length per sequence. Contiguous mode (block_tables None):
+    key_cache/value_cache are the chunk's own [T, H_kv, D] keys/values and
+    every sequence starts at position 0 (Attention._prefill,
+    litevllm/layers/attention.py:141-151).
+    """
+    dev = _cuda(query, key_cache, value_cache, cu_seqlens_q, block_tables, context_lens, out, status)
+    if query.dim() != 3:
+        raise ValueError("query must be [T, H, D]")
+    T, H, D = query.shape
+    if query.stride(2) != 1 or query.stride(1) != D:
+        raise ValueError("query must have unit d-stride and head stride D")
+    if block_tables is not None:
+        nb, bs, H_kv, Dk = key_cache.shape
+        if not (key_cache.is_contiguous() and value_cache.is_contiguous()):
+            raise ValueError("caches must be contiguous")
+        if block_tables.dtype != torch.int32 or block_tables.stride(1) != 1:
+            raise TypeError("block_tables must be int32 with unit column stride")
+        if context_lens is None or context_lens.dtype != torch.int32:
+            raise TypeError("context_lens must be int32 in paged mode")
+        context_lens = context_lens.contiguous()
+        bt_stride = block_tables.stride(0)
+        num = nb
+    else:
+        if key_cache.dim() != 3:
+            raise ValueError("contiguous mode wants key/value [T, H_kv, D]")
+        key_cache = key_cache.contiguous()
+        value_cache = value_cache.contiguous()
+        Tk, H_kv, Dk = key_cache.shape
+        bs, bt_stride, num = 16, 0, Tk
+        context_lens = None
+    if Dk != D or value_cache.shape != key_cache.shape:
+        raise ValueError("key/value shape mismatch")
+    if query.dtype != key_cache.dtype:
+        raise TypeError("query dtype must match the cache dtype")
+    if cu_seqlens_q.dtype != torch.int32:
+        raise TypeError("cu_seqlens_q must be int32")
+    cu_seqlens_q = cu_seqlens_q.contiguous()
+    S = cu_seqlens_q.numel() - 1
+    code = _dtype_code(query)
+    if out is None:
+        out = torch.empty((T, H, D), dtype=query.dtype, device=dev)
+    elif out.shape != (T, H, D) or not out.is_contiguous():
+        raise ValueError("bad out tensor")
+    if S <= 0 or T == 0:
+        return out
+    with torch.cuda.device(dev):
+        check(
+            lib().lk_paged_prefill(
+                out.data_ptr(), query.data_ptr(), query.stride(0), key_cache.data_ptr(),
+                value_cache.data_ptr(), num, _ptr(block_tables), bt_stride,
+                cu_seqlens_q.data_ptr(), _ptr(context_lens), S, int(max_q_len), H, H_kv, D, bs,
+                float(scale), code, _ptr(status), _stream(dev),
+            )
+        )
+    return out
+
+
+# ---------------------------------------------------------------- sampler ---
+def sample(
+    logits: torch.Tensor,
+    temperatures: Optional[torch.Tensor] = None,
+    noise: Optional[torch.Tensor] = None,
+    seed: int = 0,
+    offset: int = 0,
+    noise_dump: Optional[torch.Tensor] = None,
+    out: Optional[torch.Tensor] = None,
+    workspace: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """Greedy / Gumbel-max token ids, int64 [B].
+
+    temperatures: fp32 [B] (0 = greedy row) or None (all greedy).
+    noise: fp32 [B, >=V] Gumbel noise, or None for in-kernel Philox noise
+    keyed by (seed, offset); noise_dump (fp32 [B, V]) receives that noise.
+    """
+    if logits.dim() == 1:
+        logits = logits.unsqueeze(0)
+    dev = _cuda(logits, temperatures, noise, noise_dump, out, workspace)
+    B, V = logits.shape
+    if logits.stride(1) != 1:
+        logits = logits.contiguous()
+    code = _dtype_code(logits, (torch.float32, torch.float16, torch.bfloat16))
+    if temperatures is not None:
+        if temperatures.dtype != torch.float32 or temperatures.numel() != B:
+            raise TypeError("temperatures must be fp32 [B]")
+        temperatures = temperatures.contiguous()
+    noise_ld = 0
+    if noise is not None:
+        if noise.dtype != torch.float32 or noise.shape[0] != B or noise.shape[1] < V or noise.stride(1) != 1:
+            raise TypeError("noise must be fp32 [B, >=V] with unit column stride")
+        noise_ld = noise.stride(0)
+    if noise_dump is not None:
+        if noise_dump.dtype != torch.float32 or noise_dump.shape != (B, V) or not noise_dump.is_contiguous():
+            raise TypeError("noise_dump must be contiguous fp32 [B, V]")
+    if out is None:
+        out = torch.empty(B, dtype=torch.int64, device=dev)
+    if B == 0:
+        return out
+    need = int(lib().lk_sample_workspace_bytes(B, V))
+    if workspace is None:
+        workspace = WORKSPACES.get(dev, "sample", need)
+    with torch.cuda.device(dev):
+        check(
+            lib().lk_sample(
+                out.data_ptr(), logits.data_ptr(), B, V, logits.stride(0), _ptr(temperatures),
+                _ptr(noise), noise_ld, seed & (2**64 - 1), offset & (2**64 - 1), _ptr(noise_dump),
+                workspace.data_ptr(), workspace.numel() * workspace.element_size(), code,
+                _stream(dev),
+            )
+        )
+    return out
+
+
+def softmax_temp(logits: torch.Tensor, temperatures: torch.Tensor) -> torch.Tensor:
+    """fp32 softmax(logits / T) per row (the top-k / top-p path)."""
+    if logits.dim() == 1:
+        logits = logits.unsqueeze(0)
+    dev = _cuda(logits, temperatures)
+    B, V = logits.shape
+    logits = logits.contiguous()
+    code = _dtype_code(logits, (torch.float32, torch.float16, torch.bfloat16))
+    temperatures = temperatures.to(torch.float32).contiguous()
+    probs = torch.empty((B, V), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        check(
+            lib().lk_softmax_temp(
+                probs.data_ptr(), V, logits.data_ptr(), B, V, V, temperatures.data_ptr(), code,
+                _stream(dev),
+            )
+        )
+    return probs
+
+
+def default_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

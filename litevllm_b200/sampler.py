@@ -1,0 +1,116 @@
+"""Drop-in replacement for litevllm.layers.sampler.Sampler.
+
+`Sampler.sample(logits, sampling_params, past_token_ids=None)` keeps the
+reference signature (litevllm/layers/sampler.py:147-187):
+
+* repetition penalty -> same arithmetic as the reference (:190-201), torch ops
+  on the GPU;
+* temperature 0 -> liblitekern greedy argmax (replaces _argmax_kernel);
+* top-k / top-p -> liblitekern softmax(x / T), the reference's top-k / top-p
+  masking (:204-225), torch.multinomial;
+* otherwise -> liblitekern Gumbel-max with in-kernel Philox noise: one pass,
+  no probability tensor. The seed is drawn from torch's CPU generator, so
+  torch.manual_seed makes it reproducible; sampling_params.seed, when set,
+  is used instead.
+
+`Sampler.sample_batch` is the batched, per-row-temperature entry the engine
+calls once per step.
+"""
+
+from __future__ import annotations
+
+import threading
+from typing import Optional
+
+import torch
+
+from . import ops
+
+
+def _apply_repetition_penalty(logits, past_token_ids, penalty):
+    for i in range(logits.shape[0]):
+        unique_ids = past_token_ids[i].unique()
+        score = logits[i, unique_ids]
+        logits[i, unique_ids] = torch.where(score > 0, score / penalty, score * penalty)
+    return logits
+
+
+def _apply_top_k_top_p(probs, top_k, top_p):
+    if top_k > 0:
+        k = min(top_k, probs.size(-1))
+        kth = torch.topk(probs, k, dim=-1).values[..., -1, None]
+        probs = torch.where(probs < kth, torch.zeros_like(probs), probs)
+    if top_p < 1.0:
+        sp, si = torch.sort(probs, descending=True, dim=-1)
+        cum = torch.cumsum(sp, dim=-1)
+        sp = torch.where(cum - sp > top_p, torch.zeros_like(sp), sp)
+        probs = torch.zeros_like(probs).scatter_(-1, si, sp)
+    return probs / probs.sum(dim=-1, keepdim=True).clamp_min(1e-9)
+
+
+class Sampler:
+    """Stateless (apart from an RNG call counter) sampler."""
+
+    _offset = 0
+    _lock = threading.Lock()
+
+    @classmethod
+    def _next_offset(cls) -> int:
+        with cls._lock:
+            cls._offset += 1
+            return cls._offset
+
+    @staticmethod
+    def _seed(sampling_params=None) -> int:
+        s = getattr(sampling_params, "seed", None)
+        if s is not None:
+            return int(s)
+        return int(torch.randint(0, 2**62, (1,)).item())
+
+    @staticmethod
+    def sample(logits: torch.Tensor, sampling_params, past_token_ids: Optional[torch.Tensor] = None):
+        if logits.dim() == 1:
+            logits = logits.unsqueeze(0)
+        if past_token_ids is not None and sampling_params.repetition_penalty != 1.0:
+            logits = _apply_repetition_penalty(
+                logits.clone(), past_token_ids, sampling_params.repetition_penalty
+            )
+        B = logits.shape[0]
+        T = float(sampling_params.temperature)
+        if T == 0.0:
+            return ops.sample(logits)
+        temps = torch.full((B,), T, dtype=torch.float32, device=logits.device)
+        if sampling_params.top_k > 0 or sampling_params.top_p < 1.0:
+            probs = ops.softmax_temp(logits, temps)
+            probs = _apply_top_k_top_p(probs, sampling_params.top_k, sampling_params.top_p)
+            return torch.multinomial(probs, num_samples=1).squeeze(-1)
+        return ops.sample(
+            logits, temps, seed=Sampler._seed(sampling_params), offset=Sampler._next_offset()
+        )
+
+    # north-star alias
+    forward = sample
+
+    @staticmethod
+    def sample_batch(
+        logits: torch.Tensor,
+        temperatures: Optional[torch.Tensor] = None,
+        noise: Optional[torch.Tensor] = None,
+        seed: Optional[int] = None,
+        offset: Optional[int] = None,
+        noise_dump: Optional[torch.Tensor] = None,
+        out: Optional[torch.Tensor] = None,
+    ) -> torch.Tensor:
+        """One sampler launch for a whole step: rows with temperature 0 are
+        greedy, the others Gumbel-max at their own temperature."""
+        if temperatures is not None and temperatures.dtype != torch.float32:
+            temperatures = temperatures.float()
+        return ops.sample(
+            logits,
+            temperatures,
+            noise=noise,
+            seed=Sampler._seed() if seed is None else seed,
+            offset=Sampler._next_offset() if offset is None else offset,
+            noise_dump=noise_dump,
+            out=out,
+        )

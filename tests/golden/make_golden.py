@@ -1,0 +1,123 @@
+"""Generate tests/golden/*.npz by running the REFERENCE implementation on CPU.
+
+    python tests/golden/make_golden.py /path/to/lite-vllm-checkout
+
+Imports litevllm from the given checkout (read only) and records, for small
+seeded inputs, what its own functions return:
+
+  store_decode.npz   Attention.forward(..., is_prefill=False)   (store + _decode_fast,
+                     litevllm/layers/attention.py:77-139), config-1 head shapes
+                     (16 Q / 8 KV heads, D=128, bs=16), context lengths 1, 15, 16,
+                     17, 40, 100 (one block, block edges, partial last block).
+  decode_g4.npz      same, 32 Q / 8 KV heads (Llama-3-8B GQA ratio 4).
+  prefill.npz        Attention.forward(..., is_prefill=True)    (store + _prefill,
+                     :141-151) for G=2 and G=4.
+  sampler.npz        Sampler.sample greedy ids (litevllm/layers/sampler.py:151-175)
+                     with planted ties, and the temperature softmax the reference
+                     computes before its multinomial draw (:178 / :133-135).
+
+Inputs are stored next to outputs (bf16 inputs as uint16 bit patterns), so
+the fixtures do not depend on any random generator.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+
+
+def bf16_bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def main(ref_root: str) -> None:
+    sys.path.insert(0, ref_root)
+    from litevllm.config import SamplingParams
+    from litevllm.layers.attention import Attention
+    from litevllm.layers.sampler import Sampler, _triton_softmax_temp
+
+    torch.manual_seed(1234)
+    g = torch.Generator().manual_seed(20260101)
+
+    def decode_case(name, H, H_kv, ctx):
+        D, bs = 128, 16
+        B = len(ctx)
+        nblk = [max(1, -(-c // bs)) for c in ctx]
+        pool = sum(nblk) + 1
+        perm = torch.randperm(pool, generator=g)
+        mb = max(nblk)
+        bt = torch.zeros((B, mb), dtype=torch.int32)
+        off = 0
+        for i, n in enumerate(nblk):
+            bt[i, :n] = perm[off : off + n].int()
+            off += n
+        slots = torch.tensor([int(bt[i, (c - 1) // bs]) * bs + (c - 1) % bs for i, c in enumerate(ctx)])
+        kc = torch.randn((pool, bs, H_kv, D), generator=g).bfloat16()
+        vc = torch.randn((pool, bs, H_kv, D), generator=g).bfloat16()
+        q = torch.randn((B, H, D), generator=g).bfloat16()
+        k = torch.randn((B, H_kv, D), generator=g).bfloat16()
+        v = torch.randn((B, H_kv, D), generator=g).bfloat16()
+        kc32, vc32 = kc.float().clone(), vc.float().clone()
+        attn = Attention(H, D, H_kv)
+        out = attn.forward(q.float(), k.float(), v.float(), kc32, vc32, bt, slots,
+                           torch.tensor(ctx, dtype=torch.int32), is_prefill=False)
+        np.savez_compressed(
+            HERE / name,
+            H=H, H_kv=H_kv, D=D, bs=bs, scale=attn.scale,
+            ctx=np.array(ctx, dtype=np.int32), block_tables=bt.numpy(), slot_mapping=slots.numpy(),
+            key_cache=bf16_bits(kc), value_cache=bf16_bits(vc), query=bf16_bits(q),
+            key=bf16_bits(k), value=bf16_bits(v),
+            # the rows the store wrote, read back from the reference's cache
+            stored_k=bf16_bits(kc32.view(-1, H_kv, D)[slots].bfloat16()),
+            stored_v=bf16_bits(vc32.view(-1, H_kv, D)[slots].bfloat16()),
+            untouched_equal=np.array(bool(
+                torch.equal(kc32.view(-1, H_kv, D)[[i for i in range(pool * bs) if i not in set(slots.tolist())]],
+                            kc.float().view(-1, H_kv, D)[[i for i in range(pool * bs) if i not in set(slots.tolist())]]))),
+            out=out.float().numpy(),
+        )
+
+    decode_case("store_decode.npz", 16, 8, [1, 15, 16, 17, 40, 100])
+    decode_case("decode_g4.npz", 32, 8, [3, 64, 129])
+
+    # prefill: reference _prefill over the new tokens only
+    pre = {}
+    for tag, H, H_kv, S in (("g2", 16, 8, 37), ("g4", 32, 8, 33)):
+        D = 128
+        q = torch.randn((S, H, D), generator=g).bfloat16()
+        k = torch.randn((S, H_kv, D), generator=g).bfloat16()
+        v = torch.randn((S, H_kv, D), generator=g).bfloat16()
+        attn = Attention(H, D, H_kv)
+        out = attn.forward(q.float(), k.float(), v.float(), None, None, None, None, None,
+                           is_prefill=True)
+        pre.update({f"{tag}_q": bf16_bits(q), f"{tag}_k": bf16_bits(k), f"{tag}_v": bf16_bits(v),
+                    f"{tag}_out": out.float().contiguous().numpy(), f"{tag}_shape": np.array([S, H, H_kv, D])})
+    np.savez_compressed(HERE / "prefill.npz", **pre)
+
+    # sampler: greedy with planted ties + the temperature softmax
+    V = 4096
+    logits = torch.randn((6, V), generator=g) * 2.0
+    logits[1, 100] = logits[1, 3000] = 50.0          # tie: lowest index wins
+    logits[2, :] = 1.0                               # all equal -> index 0
+    logits[3, V - 1] = 60.0                          # max at the last index
+    logits[4, 0] = 70.0                              # max at the first index
+    logits[5, 17] = logits[5, 18] = logits[5, 4000] = 55.0
+    greedy = Sampler.sample(logits, SamplingParams(temperature=0.0, max_tokens=8))
+    probs07 = _triton_softmax_temp(logits[:2], 0.7)
+    # the four vectors of the reference's own tests/test_sampler.py
+    ref_vec = torch.tensor([[1.0, 5.0, 3.0, 0.5], [4.0, 0.0, 2.0, 1.0]])
+    ref_vec_out = Sampler.sample(ref_vec, SamplingParams(temperature=0.0, max_tokens=8))
+    np.savez_compressed(
+        HERE / "sampler.npz",
+        logits=logits.numpy(), greedy=greedy.numpy(), probs07=probs07.numpy(),
+        ref_vec=ref_vec.numpy(), ref_vec_out=ref_vec_out.numpy(),
+    )
+    print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

@@ -1,0 +1,109 @@
+"""C-ABI checks that need no GPU: the library loads, exports every entry point
+include/litekern.h declares, and rejects bad arguments before any launch."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from litevllm_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "litekern.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(lk_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    for s in ("lk_store_kv", "lk_paged_decode", "lk_paged_prefill", "lk_sample", "lk_softmax_temp"):
+        assert s in syms
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    for s in declared_symbols():
+        assert hasattr(lib, s), s
+    assert set(declared_symbols()) <= set(_lib.SIGNATURES), "ctypes prototypes missing"
+
+
+def test_status_strings():
+    lib = _lib.lib()
+    assert lib.lk_version() >= 100
+    assert lib.lk_status_string(0) == b"ok"
+    for code in (-1, -2, -3, -4, -5, -6, -99):
+        assert lib.lk_status_string(code).startswith(b"litekern")
+
+
+def test_argument_validation_without_launch():
+    lib = _lib.lib()
+    # zero tokens is a no-op
+    assert lib.lk_store_kv(None, None, None, None, None, 0, 8, 128, 1024, 1024, 16, 2, None, None) == 0
+    # bad dtype
+    assert lib.lk_store_kv(1, 1, 1, 1, 1, 4, 8, 128, 1024, 1024, 16, 7, None, None) == -2
+    # null pointers
+    assert lib.lk_store_kv(None, 1, 1, 1, 1, 4, 8, 128, 1024, 1024, 16, 2, None, None) == -1
+    # decode: H not a multiple of H_kv
+    assert lib.lk_paged_decode(1, 0, 1, 0, 1, 1, 10, 1, 4, 1, 2, 12, 8, 128, 16, 4, 0.1, 1,
+                               1, 1 << 20, 2, None) == -1
+    # decode: D != 128 unsupported
+    assert lib.lk_paged_decode(1, 0, 1, 0, 1, 1, 10, 1, 4, 1, 2, 16, 8, 64, 16, 4, 0.1, 1,
+                               1, 1 << 20, 2, None) == -2
+    # decode: G > 8 unsupported
+    assert lib.lk_paged_decode(1, 0, 1, 0, 1, 1, 10, 1, 4, 1, 2, 32, 2, 128, 16, 4, 0.1, 1,
+                               1, 1 << 20, 2, None) == -2
+    # decode: fp32 unsupported on the tensor-core path
+    assert lib.lk_paged_decode(1, 0, 1, 0, 1, 1, 10, 1, 4, 1, 2, 16, 8, 128, 16, 4, 0.1, 1,
+                               1, 1 << 20, 0, None) == -2
+    # decode: workspace missing
+    assert lib.lk_paged_decode(16, 4096, 16, 4096, 256, 256, 10, 16, 4, 16, 2, 32, 8, 128, 16, 4,
+                               0.1, 2, None, 0, 2, None) == -4
+    # prefill: G = 3 unsupported
+    assert lib.lk_paged_prefill(16, 16, 0, 16, 16, 10, None, 0, 16, None, 1, 8, 24, 8, 128, 16,
+                                0.1, 2, None, None) == -2
+    # sampler: ld < V
+    assert lib.lk_sample(1, 1, 2, 100, 50, None, None, 0, 0, 0, None, None, 0, 2, None) == -1
+    # sampler: B = 0 no-op
+    assert lib.lk_sample(None, None, 0, 100, 100, None, None, 0, 0, 0, None, None, 0, 2, None) == 0
+
+
+def test_workspace_sizes_and_split_plan():
+    lib = _lib.lib()
+    assert lib.lk_paged_decode_workspace_bytes(256, 32, 8, 128, 1) == 256 + 1024
+    w4 = lib.lk_paged_decode_workspace_bytes(256, 32, 8, 128, 4)
+    assert w4 >= 256 * 4 * 32 * (128 + 2) * 4
+    # long contexts split; a single short sequence per SM-wave does not over-split
+    assert lib.lk_paged_decode_num_splits(8, 8, 8192, 16) >= 32
+    assert lib.lk_paged_decode_num_splits(256, 8, 4, 16) == 1
+    n = lib.lk_paged_decode_num_splits(256, 8, 256, 16)
+    assert 1 <= n <= 256
+    assert lib.lk_sample_workspace_bytes(8, 151936) > 0
+
+
+def test_ops_refuse_cpu_tensors():
+    """No CPU fallback: host tensors are rejected loudly."""
+    from litevllm_b200 import ops
+
+    q = torch.zeros(2, 32, 128, dtype=torch.bfloat16)
+    kc = torch.zeros(4, 16, 8, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.paged_decode(q, kc, kc, torch.zeros(2, 1, dtype=torch.int32),
+                         torch.ones(2, dtype=torch.int32), 0.1)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.sample(torch.zeros(2, 10))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.store_kvcache(torch.zeros(1, 8, 128, dtype=torch.bfloat16),
+                          torch.zeros(1, 8, 128, dtype=torch.bfloat16), kc, kc,
+                          torch.zeros(1, dtype=torch.int64))
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "absent.so")
+    with pytest.raises(_lib.LiteKernError, match="no fallback"):
+        _lib.lib()

@@ -1,0 +1,128 @@
+"""Paged decode attention on the GPU vs the reference (golden) and the fp32 oracle."""
+
+import math
+
+import pytest
+import torch
+
+from litevllm_b200 import ops, workloads
+from litevllm_b200.attention import Attention
+from oracle import paged_attention as pa
+from tests import golden_io
+from tests.tolerance import assert_attn_close
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name", ["store_decode.npz", "decode_g4.npz"])
+def test_decode_matches_reference_golden(cuda, name):
+    """Store + decode through the drop-in Attention.forward, as the reference's
+    Attention.forward(..., is_prefill=False) ran them."""
+    d = golden_io.decode_case(name)
+    attn = Attention(int(d["H"]), int(d["D"]), int(d["H_kv"]))
+    kc, vc = d["key_cache"].to(cuda), d["value_cache"].to(cuda)
+    out = attn.forward(d["query"].to(cuda), d["key"].to(cuda), d["value"].to(cuda), kc, vc,
+                       d["block_tables"].to(cuda), d["slot_mapping"].to(cuda),
+                       d["context_lens"].to(cuda), is_prefill=False)
+    assert out.dtype == torch.bfloat16 and out.shape == d["out"].shape
+    assert_attn_close(out, d["out"])
+
+
+def _check(b, rows=None, num_splits=0, dtype=torch.bfloat16):
+    out = ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables, b.context_lens,
+                           b.scale, num_splits=num_splits)
+    ref = pa.decode(b.query.float(), b.key_cache.float(), b.value_cache.float(), b.block_tables,
+                    b.context_lens, b.scale, rows=rows)
+    got = out if rows is None else out[list(rows)]
+    assert_attn_close(got, ref)
+    return out
+
+
+@pytest.mark.parametrize("ctx", [[1], [15], [16], [17], [1, 2, 3, 31, 32, 33, 255, 256, 257]])
+def test_decode_edge_lengths(cuda, ctx):
+    b = workloads.make_decode_batch(1, len(ctx), seed=5, ctx=ctx, H=16, H_kv=8, device=cuda)
+    _check(b)
+
+
+@pytest.mark.parametrize("H,H_kv", [(8, 8), (16, 8), (32, 8), (64, 8), (32, 4), (8, 2), (4, 1), (16, 16)])
+def test_decode_gqa_ratios_and_head_groups(cuda, H, H_kv):
+    b = workloads.make_decode_batch(2, 6, seed=H * 7 + H_kv, H=H, H_kv=H_kv, device=cuda,
+                                    ctx=[5, 100, 333, 1024, 16, 700])
+    _check(b)
+
+
+@pytest.mark.parametrize("num_splits", [1, 2, 3, 7, 64])
+def test_decode_split_kv_consistent(cuda, num_splits):
+    b = workloads.make_decode_batch(2, 5, seed=11, device=cuda, ctx=[4096, 1, 2000, 17, 1023])
+    _check(b, num_splits=num_splits)
+
+
+def test_decode_repeated_calls_reuse_workspace(cuda):
+    """Counters reset after each call: many back-to-back split calls agree."""
+    b = workloads.make_decode_batch(2, 16, seed=12, device=cuda)
+    first = ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables, b.context_lens,
+                             b.scale, num_splits=8)
+    for _ in range(5):
+        again = ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables,
+                                 b.context_lens, b.scale, num_splits=8)
+        assert torch.equal(first, again)
+    assert ops.decode_status() == 0
+
+
+def test_decode_fp16(cuda):
+    b = workloads.make_decode_batch(2, 8, seed=13, dtype=torch.float16, device=cuda)
+    _check(b)
+
+
+def test_decode_block_size_32(cuda):
+    b = workloads.make_decode_batch(2, 6, seed=14, bs=32, device=cuda, ctx=[1, 31, 32, 33, 500, 64])
+    _check(b)
+
+
+def test_decode_zero_context_is_nan_like_reference(cuda):
+    """The reference's softmax over an all -inf row yields NaN (attention.py:132-135)."""
+    b = workloads.make_decode_batch(2, 3, seed=15, device=cuda, ctx=[5, 1, 9])
+    b.context_lens[1] = 0
+    out = ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables, b.context_lens,
+                           b.scale)
+    assert torch.isnan(out[1]).all() and not torch.isnan(out[[0, 2]]).any()
+    lit = pa.decode_batched_reference(b.query.float().cpu(), b.key_cache.float().cpu(),
+                                      b.value_cache.float().cpu(), b.block_tables.cpu(),
+                                      b.context_lens.cpu(), b.scale)
+    assert torch.isnan(lit[1]).all()
+
+
+def test_decode_custom_scale_and_strided_query(cuda):
+    b = workloads.make_decode_batch(2, 4, seed=16, device=cuda)
+    big = torch.randn((4, 3, 32, 128), device=cuda).bfloat16()
+    big[:, 1] = b.query
+    q = big[:, 1]  # token stride 3*32*128
+    out = ops.paged_decode(q, b.key_cache, b.value_cache, b.block_tables, b.context_lens, 0.05)
+    ref = pa.decode(b.query.float(), b.key_cache.float(), b.value_cache.float(), b.block_tables,
+                    b.context_lens, 0.05)
+    assert_attn_close(out, ref)
+
+
+def test_decode_config2_full_batch_sampled_rows(cuda):
+    """Config 2 at full size (B=256); the oracle checks 24 rows incl. the longest."""
+    b = workloads.make_decode_batch(2, 256, seed=0, device=cuda)
+    longest = max(range(256), key=lambda i: b.ctx[i])
+    rows = sorted(set(list(range(0, 256, 12)) + [longest]))
+    _check(b, rows=rows)
+
+
+def test_decode_config5_long_context_subset(cuda):
+    """Config 5 shapes (32K-128K tokens, split-KV mandatory) on 2 sequences."""
+    ctx = [workloads.context_len(5, 0, 0), 131072]
+    b = workloads.make_decode_batch(5, 2, seed=0, device=cuda, ctx=ctx)
+    _check(b)
+
+
+def test_decode_out_of_range_block_flags_status(cuda):
+    b = workloads.make_decode_batch(2, 2, seed=17, device=cuda, ctx=[40, 40])
+    nb = b.key_cache.shape[0]
+    b.block_tables[1, 1] = nb + 5
+    ws = torch.zeros(1 << 20, dtype=torch.uint8, device=cuda)
+    ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables, b.context_lens, b.scale,
+                     workspace=ws)
+    assert ops.decode_status(ws) & 2

@@ -1,0 +1,82 @@
+"""Chunked-prefill attention on the GPU vs the reference's _prefill (golden)
+and the fp32 prior-context oracle."""
+
+import pytest
+import torch
+
+from litevllm_b200 import ops, workloads
+from litevllm_b200.attention import Attention
+from oracle import paged_attention as pa
+from tests import golden_io
+from tests.tolerance import assert_attn_close
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("tag", ["g2", "g4"])
+def test_prefill_matches_reference_golden(cuda, tag):
+    """The reference path: Attention.forward(is_prefill=True) with no block
+    table attends the new tokens only (attention.py:141-151)."""
+    d = golden_io.load("prefill.npz")
+    S, H, H_kv, D = (int(x) for x in d[f"{tag}_shape"])
+    q, k, v = (golden_io.bf16(d[f"{tag}_{x}"]).to(cuda) for x in "qkv")
+    attn = Attention(H, D, H_kv)
+    out = attn.forward(q, k, v, None, None, None, None, None, is_prefill=True)
+    assert_attn_close(out, torch.from_numpy(d[f"{tag}_out"]))
+
+
+def _paged_case(cuda, q_lens, prior, H=32, H_kv=8, seed=0, dtype=torch.bfloat16):
+    b = workloads.make_prefill_batch(q_lens, prior, seed=seed, H=H, H_kv=H_kv, dtype=dtype,
+                                     device=cuda)
+    ops.store_kvcache(b.key, b.value, b.key_cache, b.value_cache, b.slot_mapping)
+    out = ops.paged_prefill(b.query, b.key_cache, b.value_cache, b.cu_seqlens_q, max(q_lens),
+                            b.scale, block_tables=b.block_tables, context_lens=b.context_lens)
+    ref = pa.prefill(b.query.float(), b.key_cache.float(), b.value_cache.float(), b.block_tables,
+                     b.context_lens, b.cu_seqlens_q, b.scale)
+    assert_attn_close(out, ref)
+    return b, out
+
+
+@pytest.mark.parametrize("q_lens,prior", [
+    ([1], [0]), ([16], [0]), ([17], [5]), ([64], [64]), ([200], [1000]),
+    ([1, 33, 128, 7], [0, 15, 2000, 3]),
+])
+def test_prefill_paged_prior_context(cuda, q_lens, prior):
+    _paged_case(cuda, q_lens, prior)
+
+
+@pytest.mark.parametrize("H,H_kv", [(8, 8), (16, 8), (32, 8), (64, 8)])
+def test_prefill_gqa_ratios(cuda, H, H_kv):
+    _paged_case(cuda, [40, 130], [70, 0], H=H, H_kv=H_kv, seed=H)
+
+
+def test_prefill_fp16(cuda):
+    _paged_case(cuda, [90], [33], dtype=torch.float16, seed=3)
+
+
+def test_prefill_prior_zero_equals_contiguous(cuda):
+    """With no prior context the paged path equals the reference's _prefill path."""
+    b, out = _paged_case(cuda, [77], [0], seed=4)
+    cu = torch.tensor([0, 77], dtype=torch.int32, device=cuda)
+    out2 = ops.paged_prefill(b.query, b.key, b.value, cu, 77, b.scale)
+    assert_attn_close(out2, out.float(), max_abs=1e-2, mean_rel=5e-3)
+
+
+def test_prefill_config3_chunks(cuda):
+    """Config 3's four 512-token chunks on top of prior context ~U[0,3584]."""
+    prior = [workloads.prefill_prior(0, i) for i in range(4)]
+    _paged_case(cuda, [512] * 4, prior, seed=5)
+
+
+def test_mixed_step_prefill_plus_decode(cuda):
+    """One mixed step through Attention.forward_mixed: 2 chunks + 5 decode rows."""
+    q_lens = [40, 70, 1, 1, 1, 1, 1]
+    prior = [100, 0, 9, 300, 15, 16, 1000]
+    b = workloads.make_prefill_batch(q_lens, prior, seed=6, device=cuda)
+    attn = Attention(32, 128, 8)
+    out = attn.forward_mixed(b.query, b.key, b.value, b.key_cache, b.value_cache,
+                             b.block_tables, b.slot_mapping, b.context_lens, b.cu_seqlens_q,
+                             num_prefill_seqs=2, num_prefill_tokens=110, max_q_len=70)
+    ref = pa.prefill(b.query.float(), b.key_cache.float(), b.value_cache.float(), b.block_tables,
+                     b.context_lens, b.cu_seqlens_q, b.scale)
+    assert_attn_close(out, ref)

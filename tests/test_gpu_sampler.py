@@ -1,0 +1,137 @@
+"""Sampler on the GPU vs the reference (golden, its own test vectors) and the
+oracle: greedy and noise-given ids bit-exact, in-kernel noise reproducible."""
+
+import numpy as np
+import pytest
+import torch
+
+from litevllm_b200 import ops, workloads
+from litevllm_b200.sampler import Sampler
+from oracle import sampler as osamp
+from tests import golden_io
+
+pytestmark = pytest.mark.gpu
+
+
+class SP:
+    """Minimal stand-in with the reference SamplingParams fields the sampler reads
+    (litevllm/config/config.py:159-170)."""
+
+    def __init__(self, temperature=1.0, top_p=1.0, top_k=-1, repetition_penalty=1.0, seed=None):
+        self.temperature, self.top_p, self.top_k = temperature, top_p, top_k
+        self.repetition_penalty, self.seed = repetition_penalty, seed
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_greedy_matches_reference_golden(cuda, dtype):
+    d = golden_io.load("sampler.npz")
+    x = torch.from_numpy(d["logits"]).to(dtype)
+    got = ops.sample(x.to(cuda)).cpu().numpy()
+    want = osamp.greedy(x.float().numpy())
+    assert np.array_equal(got, want)
+    if dtype == torch.float32:
+        assert np.array_equal(got, d["greedy"])
+
+
+def test_reference_test_sampler_vectors(cuda):
+    """litevllm tests/test_sampler.py, through the drop-in Sampler on the GPU."""
+    logits = torch.tensor([[1.0, 5.0, 3.0, 0.5], [4.0, 0.0, 2.0, 1.0]], device=cuda)
+    assert Sampler.sample(logits, SP(temperature=0.0)).tolist() == [1, 0]
+    torch.manual_seed(0)
+    out = Sampler.sample(torch.randn(4, 32, device=cuda), SP(temperature=1.0))
+    assert out.shape == (4,) and (out >= 0).all() and (out < 32).all()
+    logits = torch.zeros(1, 8, device=cuda)
+    logits[0, 3] = 100.0
+    assert Sampler.sample(logits, SP(temperature=1.0, top_k=1)).tolist() == [3]
+    logits = torch.tensor([[10.0, 9.5, -100.0, -100.0]], device=cuda)
+    assert Sampler.sample(logits, SP(temperature=1.0, top_p=0.9)).tolist()[0] in (0, 1)
+
+
+def test_softmax_temp_matches_reference_golden(cuda):
+    d = golden_io.load("sampler.npz")
+    x = torch.from_numpy(d["logits"][:2]).to(cuda)
+    p = ops.softmax_temp(x, torch.full((2,), 0.7, device=cuda))
+    torch.testing.assert_close(p.cpu(), torch.from_numpy(d["probs07"]), atol=1e-6, rtol=1e-4)
+
+
+@pytest.mark.parametrize("B,V", [(1, 7), (3, 1000), (8, 151936), (64, 128256), (5, 151937)])
+def test_greedy_ties_across_chunks(cuda, B, V):
+    g = torch.Generator().manual_seed(B * 7 + V)
+    x = torch.randn((B, V), generator=g).bfloat16()
+    # plant exact ties in far-apart chunks; the lower index must win
+    for b in range(B):
+        i, j = sorted(torch.randint(0, V, (2,), generator=g).tolist())
+        x[b, j] = 30.0
+        x[b, i] = 30.0
+    got = ops.sample(x.to(cuda)).cpu().numpy()
+    assert np.array_equal(got, osamp.greedy(x.float().numpy()))
+
+
+def test_greedy_unaligned_row_stride(cuda):
+    x = torch.randn((6, 1001), device=cuda).bfloat16()
+    view = x[:, :999]  # row stride 1001 elements: not 16-byte aligned
+    got = ops.sample(view).cpu().numpy()
+    assert np.array_equal(got, osamp.greedy(view.float().cpu().numpy()))
+
+
+def test_greedy_nan_wins_like_torch_argmax(cuda):
+    x = torch.randn((2, 5000), device=cuda)
+    x[1, 4321] = float("nan")
+    x[1, 4400] = float("nan")
+    got = ops.sample(x).tolist()
+    assert got[1] == 4321 == int(torch.argmax(x[1].cpu()))
+
+
+@pytest.mark.parametrize("cfg", [1, 4, 5])
+def test_gumbel_noise_given_bit_exact(cuda, cfg):
+    B, V = (8, 151936) if cfg == 1 else (16, 151936)
+    x = workloads.make_logits(cfg, B, V, seed=cfg, dtype=torch.bfloat16)
+    t = workloads.temperatures_for(cfg, B)
+    n = workloads.gumbel_noise(B, V, seed=cfg)
+    got = ops.sample(x.to(cuda), t.to(cuda), noise=n.to(cuda)).cpu().numpy()
+    want = osamp.gumbel(x.float().numpy(), t.numpy(), n.numpy())
+    assert np.array_equal(got, want)
+
+
+def test_in_kernel_noise_dump_and_philox(cuda):
+    """In-kernel noise: the dumped noise reproduces the ids bit-exactly, its
+    uniforms are the oracle's Philox4x32-10 stream, and the same (seed, offset)
+    gives the same ids."""
+    B, V = 4, 50000
+    x = torch.randn((B, V)).bfloat16()
+    t = torch.tensor([0.7, 1.0, 0.0, 1.3])
+    dump = torch.zeros((B, V), device=cuda)
+    seed, offset = 0x1234_5678_9ABC, 77
+    ids = ops.sample(x.to(cuda), t.to(cuda), seed=seed, offset=offset, noise_dump=dump)
+    dump_np = dump.cpu().numpy()
+    assert np.array_equal(ids.cpu().numpy(), osamp.gumbel(x.float().numpy(), t.numpy(), dump_np))
+    for b in (0, 1, 3):
+        g = osamp.gumbel_from_u(osamp.philox_uniforms(b, V, seed, offset))
+        np.testing.assert_allclose(dump_np[b], g, rtol=2e-6, atol=2e-6)
+    again = ops.sample(x.to(cuda), t.to(cuda), seed=seed, offset=offset)
+    assert torch.equal(ids, again)
+
+
+def test_gumbel_in_kernel_distribution_chi_square(cuda):
+    """Histogram of in-kernel Gumbel-max draws vs the reference's softmax(x / T)."""
+    V, N, T = 32, 60_000, 0.7
+    x = torch.randn(V, generator=torch.Generator().manual_seed(9)) * 2
+    logits = x.repeat(N, 1).to(cuda)
+    ids = ops.sample(logits, torch.full((N,), T, device=cuda), seed=2024, offset=1).cpu()
+    counts = torch.bincount(ids, minlength=V).double()
+    p = torch.softmax(x.double() / T, 0)
+    exp = p * N
+    keep = exp > 5
+    chi2 = (((counts - exp) ** 2) / exp)[keep].sum().item()
+    dof = int(keep.sum()) - 1
+    # 99.9th percentile of chi-square is below dof + 4.5 sqrt(2 dof) for these dof
+    assert chi2 < dof + 4.5 * (2 * dof) ** 0.5, (chi2, dof)
+
+
+def test_sample_batch_mixed_rows(cuda):
+    """One launch, per-row temperatures: greedy rows equal argmax."""
+    x = workloads.make_logits(1, 8, 151936, seed=1, dtype=torch.float32).to(cuda)
+    t = workloads.temperatures_for(1, 8).to(cuda)
+    ids = Sampler.sample_batch(x, t, seed=5, offset=9).cpu().numpy()
+    assert np.array_equal(ids[:4], osamp.greedy(x[:4].cpu().numpy()))
+    assert ((ids >= 0) & (ids < 151936)).all()
