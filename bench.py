@@ -1,0 +1,438 @@
+"""Benchmark of litevllm's per-step hot path on B200: KV store -> paged decode
+attention -> greedy sampler, config 2 of the baseline (Llama-3-8B attention
+shapes, 256 sequences per GPU, log-normal contexts, V = 128256).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (one process per GPU)
+
+Sequences are sharded by request: GPU r owns global sequences
+r*B .. r*B+B-1, its own KV pool and inputs; no collective touches the data
+path (weak scaling). torch.distributed is used only for the start/stop
+barrier and the max-over-ranks time. Rank 0 prints one JSON line.
+
+--impl reference times the reference algorithm on the host CPU (the CPU
+restatement of litevllm's Attention.forward store + _decode_fast and the greedy
+Sampler, run with every host thread) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "paged-decode attn HBM GB/s (% of peak); sampled tok/s at 1/2/4/8 B200"
+CFG = 2
+B_PER_GPU = 256
+H, H_KV, D, BS, V = 32, 8, 128, 16, 128256
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=1, help="attention layers per step")
+    ap.add_argument("--num-splits", type=int, default=0, help="decode split-KV override (0=auto)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------- algorithmic bytes ---
+def decode_bytes(ctx, B, elem=2):
+    kv = sum(ctx) * 2 * H_KV * D * elem
+    qo = B * H * D * elem * 2
+    meta = sum(-(-c // BS) for c in ctx) * 4 + B * 4
+    return kv + qo + meta
+
+
+def store_bytes(B, elem=2):
+    return B * 2 * H_KV * D * elem * 2 + B * 8
+
+
+def sampler_bytes(B, elem=2):
+    return B * V * elem + B * 8
+
+
+# ---------------------------------------------------------------- environment ---
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return ws, rank, local
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic():
+    """Per-launch DRAM bytes of the decode kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "paged_decode_cfg2.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(float(line.split(":", 1)[1].strip().split()[0]))
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """Polls NVML clocks and throttle reasons on a thread during the timed region."""
+
+    REASONS = {
+        "hw_slowdown": 0x0000000000000008,
+        "sw_thermal_slowdown": 0x0000000000000020,
+        "hw_thermal_slowdown": 0x0000000000000040,
+        "sw_power_cap": 0x0000000000000004,
+        "hw_power_brake_slowdown": 0x0000000000000080,
+    }
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.ok = False
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------ our arm ---
+def run_ours(args, ws, rank, local):
+    from litevllm_b200 import ops, workloads
+    from litevllm_b200.attention import Attention
+    from litevllm_b200.sampler import Sampler
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B = B_PER_GPU
+    first = rank * B
+    batch = workloads.make_decode_batch(CFG, B, seed=0, first_seq=first, device=dev)
+    # L layers: separate KV pools per layer would multiply memory; the layers
+    # share the block tables and read distinct pools (layer 0 reuses batch's).
+    pools = [(batch.key_cache, batch.value_cache)]
+    for li in range(1, args.layers):
+        pools.append((torch.randn_like(batch.key_cache), torch.randn_like(batch.value_cache)))
+    logits = [workloads.make_logits(CFG, B, V, seed=s, first_seq=first, device=dev) for s in (0, 1)]
+    temps = workloads.temperatures_for(CFG, B, device=dev)  # all greedy for config 2
+    ids = torch.empty(B, dtype=torch.int64, device=dev)
+    out = torch.empty_like(batch.query)
+    max_blocks = batch.block_tables.shape[1]
+    nsplit = args.num_splits or ops.decode_num_splits(B, H_KV, max_blocks, BS)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i, ev=None):
+        for li, (kc, vc) in enumerate(pools):
+            ops.store_kvcache(batch.key, batch.value, kc, vc, batch.slot_mapping)
+            if ev is not None and li == 0:
+                ev[0].record(stream)
+            ops.paged_decode(batch.query, kc, vc, batch.block_tables, batch.context_lens,
+                             batch.scale, num_splits=nsplit, out=out)
+            if ev is not None and li == 0:
+                ev[1].record(stream)
+        ops.sample(logits[i & 1], temps, seed=1, offset=i, out=ids)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+
+    K = args.steps
+    dec_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(K)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        t0.record(stream)
+        for i in range(K):
+            step(i, dec_ev[i])
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    if ws > 1:
+        torch.distributed.barrier()
+    ms = t0.elapsed_time(t1) / K
+    dec_ms = sum(a.elapsed_time(b) for a, b in dec_ev) / K
+    status = ops.decode_status()
+    if status:
+        raise RuntimeError(f"decode kernel status bits {status}")
+
+    # ---- e2e through the public API: host inputs in, token ids out, every step
+    e2e = None
+    if not args.no_e2e:
+        attn = Attention(H, D, H_KV)
+        pin = lambda t: t.detach().cpu().pin_memory()
+        h_q, h_k, h_v = pin(batch.query), pin(batch.key), pin(batch.value)
+        h_slot, h_bt, h_ctx = pin(batch.slot_mapping), pin(batch.block_tables), pin(batch.context_lens)
+        h_logits = [pin(x) for x in logits]
+        h_ids = torch.empty(B, dtype=torch.int64).pin_memory()
+        kc, vc = pools[0]
+
+        def e2e_step(i):
+            q = h_q.to(dev, non_blocking=True)
+            k = h_k.to(dev, non_blocking=True)
+            v = h_v.to(dev, non_blocking=True)
+            slot = h_slot.to(dev, non_blocking=True)
+            bt = h_bt.to(dev, non_blocking=True)
+            ctx = h_ctx.to(dev, non_blocking=True)
+            lg = h_logits[i & 1].to(dev, non_blocking=True)
+            o = attn.forward(q, k, v, kc, vc, bt, slot, ctx, is_prefill=False)
+            for li in range(1, args.layers):
+                o = attn.forward(q, k, v, pools[li][0], pools[li][1], bt, slot, ctx, is_prefill=False)
+            tok = Sampler.sample_batch(lg, None, seed=1, offset=i)
+            h_ids.copy_(tok, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+            return o
+
+        for i in range(max(3, args.warmup)):
+            e2e_step(i)
+        if ws > 1:
+            torch.distributed.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(K):
+            e2e_step(i)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        e2e_ms = e0.elapsed_time(e1) / K
+        if ws > 1:
+            t = torch.tensor([e2e_ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        h2d = sum(x.numel() * x.element_size() for x in (h_q, h_k, h_v, h_slot, h_bt, h_ctx, h_logits[0]))
+        e2e = dict(ms=e2e_ms, h2d=h2d, d2h=B * 8)
+
+    if ws > 1:
+        t = torch.tensor([ms, dec_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, dec_ms = float(t[0]), float(t[1])
+    return dict(ms=ms, dec_ms=dec_ms, ctx=batch.ctx, B=B, e2e=e2e, clocks=clk.summary(),
+                nsplit=nsplit, K=K)
+
+
+# -------------------------------------------------------- CPU (reference) arm ---
+def cpu_reference_sample(n_seqs: int, seed_offset: int = 0):
+    """Time the reference algorithm on the host for n_seqs config-2 sequences:
+    store + _decode_fast (literal restatement, padded gather) + greedy argmax,
+    fp32, all host threads. Returns (seconds, algorithmic bytes, tokens)."""
+    from litevllm_b200 import workloads
+    from oracle import paged_attention as pa
+    from oracle import sampler as osamp
+    from oracle import store_kv as ostore
+
+    b = workloads.make_decode_batch(CFG, n_seqs, seed=0, first_seq=seed_offset, dtype=torch.float32)
+    lg = workloads.make_logits(CFG, n_seqs, V, seed=0, first_seq=seed_offset, dtype=torch.float32)
+    kc, vc = b.key_cache.numpy(), b.value_cache.numpy()
+    t = time.perf_counter()
+    ostore.store_kv(b.key.numpy(), b.value.numpy(), kc, vc, b.slot_mapping.numpy())
+    pa.decode_batched_reference(b.query, b.key_cache, b.value_cache, b.block_tables,
+                                b.context_lens, b.scale)
+    osamp.greedy(lg.numpy())
+    dt = time.perf_counter() - t
+    nbytes = decode_bytes(b.ctx, n_seqs) + store_bytes(n_seqs) + sampler_bytes(n_seqs)
+    return dt, nbytes, n_seqs
+
+
+def cpu_baseline(budget_s=12.0, n_seqs=8):
+    torch.set_num_threads(os.cpu_count() or 1)
+    cpu_reference_sample(2)  # warm
+    tot_t = tot_b = tot_n = 0.0
+    i = 0
+    while tot_t < budget_s and i < 20:
+        dt, nb, n = cpu_reference_sample(n_seqs, seed_offset=1000 + i * n_seqs)
+        tot_t, tot_b, tot_n = tot_t + dt, tot_b + nb, tot_n + n
+        i += 1
+    return dict(gbs=tot_b / tot_t / 1e9, tok_s=tot_n / tot_t, cores=torch.get_num_threads(),
+                sample=f"{i} x {n_seqs} config-2 sequences (store + _decode_fast restatement + "
+                       f"greedy argmax over {V}), fp32, {tot_t:.1f} s")
+
+
+def workload_config(N):
+    return {
+        "workload": "config 2: bf16 paged decode step, Llama-3-8B attention (32 Q / 8 KV heads, "
+                    "D=128, block 16), 256 sequences per GPU, context lengths "
+                    "clip(lognormal(median 1024, sigma 0.5), 16, 4096); KV store of the 256 new "
+                    "tokens + decode (1 layer) + greedy sampler over [256, 128256] bf16",
+        "global_batch": B_PER_GPU * N,
+        "l2": "inputs larger than L2: KV pool ~1.2 GB per GPU, two rotating 66 MB logits buffers",
+        "parallelism": f"request-sharded x{N} (no collective on the data path)",
+    }
+
+
+def run_reference(args, ws, rank):
+    """CPU arm: the reference algorithm on the host, rank 0 only."""
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    n = 8
+    for i in range(max(1, args.warmup)):
+        cpu_reference_sample(n, seed_offset=5000 + i * n)
+    tt = tb = tn = 0.0
+    for i in range(args.steps):
+        dt, nb, k = cpu_reference_sample(n, seed_offset=i * n)
+        tt, tb, tn = tt + dt, tb + nb, tn + k
+    gbs = tb / tt / 1e9
+    sample = f"{args.steps} steps x {n} config-2 sequences (store + _decode_fast + greedy argmax), fp32"
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(gbs, 3),
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(tt / args.steps * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": workload_config(args.gpus),
+        "sampled_tok_s": round(tn / tt, 2),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    ws, rank, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, ws, rank)
+        return
+    if ws > 1:
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local))
+    r = run_ours(args, ws, rank, local)
+    N = ws
+    ms = r["ms"]
+    B = r["B"]
+    step_bytes = args.layers * (decode_bytes(r["ctx"], B) + store_bytes(B)) + sampler_bytes(B)
+    # value: whole-job hot-path bytes per second; every rank moves its own step_bytes
+    # (per-rank context mixes differ slightly; rank 0's count stands for all)
+    value = step_bytes * N / (ms * 1e-3) / 1e9
+    dec_b = decode_bytes(r["ctx"], B)
+    dec_gbs = dec_b / (r["dec_ms"] * 1e-3) / 1e9
+    peak, peak_kind = measured_peak()
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": N,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": workload_config(N),
+        "sampled_tok_s": round(B * N / (ms * 1e-3), 1),
+        "decode_split_kv": r["nsplit"],
+        "roofline": {
+            "kernel": "paged_decode_kernel",
+            "bound": "hbm",
+            "achieved": round(dec_gbs, 1),
+            "peak": peak,
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
+            "unit": "GB/s",
+            "frac": round(dec_gbs / peak, 4),
+            "traffic": profiled_traffic(),
+            "algorithmic_bytes_per_launch": dec_b,
+        },
+        "gpu_launches": r["K"] * (2 * args.layers + 1),
+        "clocks": r["clocks"],
+    }
+    if r["e2e"]:
+        e = r["e2e"]
+        line["e2e"] = {
+            "value": round(step_bytes * N / (e["ms"] * 1e-3) / 1e9, 2),
+            "unit": "GB/s",
+            "h2d_bytes_per_step": e["h2d"],
+            "d2h_bytes_per_step": e["d2h"],
+            "ms_per_step": round(e["ms"], 4),
+            "sampled_tok_s": round(B * N / (e["ms"] * 1e-3), 1),
+        }
+    if rank == 0 and N == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline()
+        line["cpu_baseline"] = {"value": round(cb["gbs"], 3), "unit": "GB/s", "cores": cb["cores"],
+                                "kind": "port", "sample": cb["sample"],
+                                "sampled_tok_s": round(cb["tok_s"], 2)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
