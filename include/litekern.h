@@ -86,9 +86,10 @@ int lk_store_kv(const void* key, const void* value, void* k_cache, void* v_cache
  * num_splits: split-KV factor (0 = choose automatically with
  * lk_paged_decode_num_splits). workspace: at least
  * lk_paged_decode_workspace_bytes(B, H, H_kv, D, num_splits) bytes, 256-byte
- * aligned, zero-filled before its first use; every completed call leaves its
- * counter region zero again, so one workspace serves consecutive calls on one
- * stream. Calls that overlap on the GPU must not share a workspace.
+ * aligned, zero-filled before its first use; its counter region sits at a
+ * fixed offset and every completed call leaves it zero again, so one
+ * workspace serves consecutive calls of any shape on one stream. Calls that
+ * overlap on the GPU must not share a workspace. B * (H_kv / 8) <= 65536.
  */
 int lk_paged_decode_num_splits(int32_t B, int32_t H_kv, int32_t max_blocks_per_seq,
                                int32_t block_size);
@@ -148,8 +149,8 @@ int lk_paged_prefill(void* out, const void* q, int64_t q_token_stride,
  * noise_dump ([B, V] fp32, optional) receives the generated g.
  * logits: [B, V] with row stride ld elements, dtype F32, F16 or BF16.
  * out_ids: int64 [B]. workspace: lk_sample_workspace_bytes(B, V) bytes,
- * 256-byte aligned, zero-filled before first use (the call leaves its counter
- * region zero again).
+ * 256-byte aligned, zero-filled before first use (the counter region sits at a
+ * fixed offset and every call leaves it zero again, whatever B and V).
  */
 size_t lk_sample_workspace_bytes(int32_t B, int32_t V);
 int lk_sample(int64_t* out_ids, const void* logits, int32_t B, int32_t V, int64_t ld,

@@ -325,8 +325,11 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
   if (threadIdx.x == 0) p.counters[b * p.num_groups + hg] = 0;
 }
 
-// Workspace layout: [status: int32, padded to 256 B][counters: B*groups int32,
-// padded to 256 B][part_ml: B*splits*H*2 f32][part_o: B*splits*H*D f32]
+// Workspace layout: [status: int32, padded to 256 B][counters: kMaxCounters
+// int32, a fixed region so that calls with different B find it where the
+// previous call left it zeroed][part_ml: B*splits*H*2 f32][part_o: B*splits*H*D f32]
+constexpr int64_t kMaxCounters = 65536;
+constexpr size_t kHeadBytes = 256 + kMaxCounters * 4;
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 int heads_per_cta(int H_kv) {
@@ -389,7 +392,8 @@ extern "C" size_t lk_paged_decode_workspace_bytes(int32_t B, int32_t H, int32_t 
                                                   int32_t num_splits) {
   if (B <= 0 || H <= 0 || H_kv <= 0 || D <= 0) return 0;
   const int groups = H_kv / heads_per_cta(H_kv);
-  size_t bytes = align256(static_cast<size_t>(B) * groups * 4) + 256;
+  (void)groups;
+  size_t bytes = kHeadBytes;
   if (num_splits > 1) {
     bytes += align256(static_cast<size_t>(B) * num_splits * H * 2 * 4);
     bytes += align256(static_cast<size_t>(B) * num_splits * H * D * 4);
@@ -414,6 +418,8 @@ extern "C" int lk_paged_decode(void* out, int64_t out_token_stride, const void* 
   if (dtype != LK_DTYPE_BF16 && dtype != LK_DTYPE_F16) return LK_ERR_UNSUPPORTED;
   if (D != kD || block_size % kTok != 0 || H / H_kv > 8) return LK_ERR_UNSUPPORTED;
   if (B > 65535 || max_blocks_per_seq == 0) return LK_ERR_INVALID_ARG;
+  if (static_cast<int64_t>(B) * (H_kv / heads_per_cta(H_kv)) > kMaxCounters)
+    return LK_ERR_UNSUPPORTED;
   if (num_blocks * block_size > 0x7fffffffLL) return LK_ERR_UNSUPPORTED;
   if (((reinterpret_cast<uintptr_t>(q) & 3u) != 0) || (q_token_stride & 1) != 0)
     return LK_ERR_ALIGNMENT;
@@ -450,7 +456,7 @@ extern "C" int lk_paged_decode(void* out, int64_t out_token_stride, const void* 
   p.stages_per_split = static_cast<int>((max_stages + num_splits - 1) / num_splits);
   p.num_groups = H_kv / hpc;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  const size_t cnt_bytes = 256 + align256(static_cast<size_t>(B) * p.num_groups * 4);
+  const size_t cnt_bytes = kHeadBytes;
   p.status = reinterpret_cast<int32_t*>(ws);
   p.counters = reinterpret_cast<int32_t*>(ws + 256);
   p.part_ml = reinterpret_cast<float*>(ws + cnt_bytes);

@@ -337,6 +337,11 @@ softmax_temp_kernel(float* __restrict__ probs, int64_t probs_ld, const T* __rest
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
+// Workspace layout: [counters: 65536 int32 — a fixed region, so that calls
+// with different B find it where the previous call left it zeroed]
+// [part_key: B*chunks f32][part_idx: B*chunks int32]
+constexpr size_t kCounterBytes = 65536 * 4;
+
 int choose_chunks(int B, int V) {
   // ~4 CTAs per SM over the whole batch, chunks of at least 4096 elements.
   const int64_t target = 4LL * lk::num_sms();
@@ -361,7 +366,7 @@ int launch_sample(const SampleParams& p, int B, bool vec, cudaStream_t s) {
 extern "C" size_t lk_sample_workspace_bytes(int32_t B, int32_t V) {
   if (B <= 0 || V <= 0) return 0;
   const int n = choose_chunks(B, V);
-  return align256(static_cast<size_t>(B) * 4) + 2 * align256(static_cast<size_t>(B) * n * 4);
+  return kCounterBytes + 2 * align256(static_cast<size_t>(B) * n * 4);
 }
 
 extern "C" int lk_sample(int64_t* out_ids, const void* logits, int32_t B, int32_t V, int64_t ld,
@@ -397,7 +402,7 @@ extern "C" int lk_sample(int64_t* out_ids, const void* logits, int32_t B, int32_
       return LK_ERR_WORKSPACE;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     p.counters = reinterpret_cast<int32_t*>(ws);
-    const size_t cb = align256(static_cast<size_t>(B) * 4);
+    const size_t cb = kCounterBytes;
     const size_t kb = align256(static_cast<size_t>(B) * choose_chunks(B, V) * 4);
     p.part_key = reinterpret_cast<float*>(ws + cb);
     p.part_idx = reinterpret_cast<int32_t*>(ws + cb + kb);
@@ -445,3 +450,4 @@ extern "C" int lk_softmax_temp(float* probs, int64_t probs_ld, const void* logit
   }
   return lk::check_launch();
 }
+

@@ -74,7 +74,7 @@ def test_argument_validation_without_launch():
 
 def test_workspace_sizes_and_split_plan():
     lib = _lib.lib()
-    assert lib.lk_paged_decode_workspace_bytes(256, 32, 8, 128, 1) == 256 + 1024
+    assert lib.lk_paged_decode_workspace_bytes(256, 32, 8, 128, 1) == 256 + 65536 * 4
     w4 = lib.lk_paged_decode_workspace_bytes(256, 32, 8, 128, 4)
     assert w4 >= 256 * 4 * 32 * (128 + 2) * 4
     # long contexts split; a single short sequence per SM-wave does not over-split

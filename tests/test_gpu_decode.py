@@ -126,3 +126,9 @@ def test_decode_out_of_range_block_flags_status(cuda):
     ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables, b.context_lens, b.scale,
                      workspace=ws)
     assert ops.decode_status(ws) & 2
+
+
+def test_decode_workspace_reused_across_batch_shapes(cuda):
+    for B, splits in [(3, 5), (40, 7), (5, 64), (40, 7)]:
+        b = workloads.make_decode_batch(2, B, seed=B, device=cuda)
+        _check(b, num_splits=splits)

@@ -135,3 +135,12 @@ def test_sample_batch_mixed_rows(cuda):
     ids = Sampler.sample_batch(x, t, seed=5, offset=9).cpu().numpy()
     assert np.array_equal(ids[:4], osamp.greedy(x[:4].cpu().numpy()))
     assert ((ids >= 0) & (ids < 151936)).all()
+
+
+def test_workspace_reused_across_batch_shapes(cuda):
+    """Calls with different B / V share one workspace; each must find the
+    counters zeroed whatever the previous call's layout was."""
+    for B, V in [(8, 151936), (256, 128256), (3, 50000), (64, 151936), (256, 128256)]:
+        x = torch.randn((B, V), device=cuda).bfloat16()
+        got = ops.sample(x).cpu().numpy()
+        assert np.array_equal(got, osamp.greedy(x.float().cpu().numpy())), (B, V)
