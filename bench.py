@@ -170,8 +170,11 @@ def run_ours(args, ws, rank, local):
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    B = B_PER_GPU
-    first = rank * B
+    from litevllm_b200.sharding import shard
+
+    mine = shard(B_PER_GPU * ws, ws, rank)
+    B = len(mine)
+    first = mine.start
     batch = workloads.make_decode_batch(CFG, B, seed=0, first_seq=first, device=dev)
     # L layers: separate KV pools per layer would multiply memory; the layers
     # share the block tables and read distinct pools (layer 0 reuses batch's).

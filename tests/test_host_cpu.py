@@ -1,0 +1,101 @@
+"""Host-side logic on CPU: workload keying, request sharding (2 gloo ranks),
+and the drop-in install into the reference package."""
+
+import os
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from litevllm_b200 import sharding, workloads
+
+REF = Path("/root/reference")
+
+
+def test_shards_partition_the_batch():
+    for G in (1, 7, 64, 256, 257):
+        for W in (1, 2, 3, 8):
+            got = [i for r in range(W) for i in sharding.shard(G, W, r)]
+            assert got == list(range(G))
+
+
+def test_context_lengths_keyed_by_global_index():
+    full = [workloads.context_len(2, 0, i) for i in range(64)]
+    assert all(16 <= c <= 4096 for c in full)
+    assert 700 < sorted(full)[32] < 1500  # median near 1024
+    for W in (2, 4, 8):
+        parts = []
+        for r in range(W):
+            parts += [workloads.context_len(2, 0, i) for i in sharding.shard(64, W, r)]
+        assert parts == full
+    c5 = [workloads.context_len(5, 0, i) for i in range(16)]
+    assert all(32768 <= c <= 131072 for c in c5)
+
+
+def test_decode_batch_tables_are_disjoint():
+    b = workloads.make_decode_batch(2, 32, seed=1, device="cpu", dtype=torch.float32)
+    used = []
+    for i, c in enumerate(b.ctx):
+        n = -(-c // 16)
+        used += b.block_tables[i, :n].tolist()
+        assert (b.block_tables[i, n:] == 0).all()
+        assert b.slot_mapping[i] == b.block_tables[i, (c - 1) // 16] * 16 + (c - 1) % 16
+    assert len(used) == len(set(used))
+
+
+def _rank_main(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        mine = list(sharding.shard(10, world, rank))
+        ctx = [workloads.context_len(2, 0, i) for i in mine]
+        # rank-dependent "step time": the max over ranks must come back everywhere
+        m = sharding.max_over_ranks([1.0 + rank, 5.0 - rank])
+        out = [None] * world
+        torch.distributed.all_gather_object(out, (mine, ctx))
+        q.put((rank, m, out))
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+def test_two_rank_gloo_sharding_and_max_timing():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29600 + os.getpid() % 1000
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, m, out in res:
+        assert m == [2.0, 5.0]
+        idx = out[0][0] + out[1][0]
+        assert idx == list(range(10))
+        assert out[0][1] + out[1][1] == [workloads.context_len(2, 0, i) for i in range(10)]
+
+
+@pytest.mark.skipif(not (REF / "litevllm").exists(), reason="reference checkout not present")
+def test_install_patches_reference_namespace():
+    sys.path.insert(0, str(REF))
+    try:
+        import litevllm.layers as L
+        import litevllm.layers.attention as LA
+        import litevllm.layers.sampler as LS
+
+        from litevllm_b200 import install
+        from litevllm_b200.attention import Attention
+        from litevllm_b200.sampler import Sampler
+
+        sites = install()
+        assert LA.Attention is Attention and L.Attention is Attention
+        assert LS.Sampler is Sampler
+        assert "litevllm.layers.attention.Attention" in sites
+        import litevllm.models.qwen3 as Q
+
+        assert Q.Attention is Attention
+    finally:
+        sys.path.remove(str(REF))
