@@ -40,6 +40,7 @@ extern "C" {
 #define LK_ERR_WORKSPACE (-4)
 #define LK_ERR_CUDA (-5)
 #define LK_ERR_DRIVER (-6)
+#define LK_ERR_TOO_LARGE (-7)
 
 #define LK_DTYPE_F32 0
 #define LK_DTYPE_F16 1
@@ -164,6 +165,30 @@ int lk_sample(int64_t* out_ids, const void* logits, int32_t B, int32_t V, int64_
  * litevllm/layers/sampler.py:127-144, including vocabularies > 65536 where the
  * reference falls back to F.softmax).
  */
+/*
+ * Allocation-free variant of lk_sample. It has no counterpart in the
+ * reference. It is for callers that cannot call cudaMalloc at the point where
+ * they sample: code running while another component owns the allocator
+ * (a caching allocator mid-reconfiguration, an arena that must not grow),
+ * hosts that forbid device allocation after start-up, and plugins handed only
+ * input and output buffers. Instead of a caller workspace it uses a
+ * file-scope 160 KiB __device__ scratch array that every GPU which loads this
+ * library holds until the process exits; the call itself allocates and frees
+ * nothing. Limits: B <= 8192 rows and B * chunks <= 16384, where chunks is
+ * the vocabulary split lk_sample would use (at most ceil(4 * SMs / B), and 1
+ * for V <= 4096); larger problems return LK_ERR_TOO_LARGE before any launch.
+ * The first call on each device looks up the array's device address with
+ * that device current (cudaGetSymbolAddress); make that first call before
+ * any stream capture. Every call shares the one array: calls that overlap on
+ * the GPU (other streams, other threads) race and must be serialised by the
+ * caller. Each call clears the counters it uses, so an earlier aborted call
+ * leaves nothing behind. Arguments and results are those of lk_sample.
+ */
+int lk_sample_noalloc(int64_t* out_ids, const void* logits, int32_t B, int32_t V, int64_t ld,
+                      const float* temperatures, const float* noise, int64_t noise_ld,
+                      uint64_t seed, uint64_t offset, float* noise_dump, int32_t dtype,
+                      void* stream);
+
 int lk_softmax_temp(float* probs, int64_t probs_ld, const void* logits, int32_t B,
                     int32_t V, int64_t ld, const float* temperatures, int32_t dtype,
                     void* stream);

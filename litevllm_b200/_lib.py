@@ -51,6 +51,11 @@ SIGNATURES: dict[str, tuple] = {
         [c_void_p, c_void_p, c_int32, c_int32, c_int64, c_void_p, c_void_p, c_int64, c_uint64,
          c_uint64, c_void_p, c_void_p, c_size_t, c_int32, c_void_p],
     ),
+    "lk_sample_noalloc": (
+        c_int32,
+        [c_void_p, c_void_p, c_int32, c_int32, c_int64, c_void_p, c_void_p, c_int64, c_uint64,
+         c_uint64, c_void_p, c_int32, c_void_p],
+    ),
     "lk_softmax_temp": (
         c_int32,
         [c_void_p, c_int64, c_void_p, c_int32, c_int32, c_int64, c_void_p, c_int32, c_void_p],

@@ -120,6 +120,8 @@ extern "C" const char* lk_status_string(int code) {
     case LK_ERR_WORKSPACE: return "litekern: workspace missing, misaligned or too small";
     case LK_ERR_CUDA: return "litekern: CUDA launch error";
     case LK_ERR_DRIVER: return "litekern: tensor-map creation failed in the CUDA driver";
+    case LK_ERR_TOO_LARGE:
+      return "litekern: problem exceeds the static scratch of the allocation-free entry point";
     default: return "litekern: unknown status";
   }
 }

@@ -22,6 +22,7 @@
 #include "lk_common.cuh"
 #include "lk_host.h"
 
+#include <mutex>
 #include <type_traits>
 
 namespace {
@@ -451,3 +452,96 @@ extern "C" int lk_softmax_temp(float* probs, int64_t probs_ld, const void* logit
   return lk::check_launch();
 }
 
+// ------------------------------------------------ allocation-free variant ---
+// lk_sample_noalloc: the same kernel, with its cross-CTA scratch (per-row
+// counters and per-chunk winners) in a file-scope __device__ array instead of
+// a caller workspace, for callers that cannot allocate device memory.
+namespace {
+
+constexpr int kNoAllocMaxRows = 8192;
+constexpr int kNoAllocMaxPartials = 16384;
+constexpr size_t kNoAllocCounterBytes = kNoAllocMaxRows * 4;
+constexpr size_t kNoAllocBytes = kNoAllocCounterBytes + 2 * kNoAllocMaxPartials * 4;  // 160 KiB
+
+static __device__ __align__(256) unsigned char g_sample_scratch[kNoAllocBytes];
+
+// Device address of g_sample_scratch per device, looked up once with that
+// device current. In host code the symbol is only a host-side stand-in.
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[64] = {nullptr};
+
+int scratch_address(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LK_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_sample_scratch) != cudaSuccess || p == nullptr)
+      return LK_ERR_CUDA;
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return LK_OK;
+}
+
+}  // namespace
+
+extern "C" int lk_sample_noalloc(int64_t* out_ids, const void* logits, int32_t B, int32_t V,
+                                 int64_t ld, const float* temperatures, const float* noise,
+                                 int64_t noise_ld, uint64_t seed, uint64_t offset,
+                                 float* noise_dump, int32_t dtype, void* stream) {
+  if (B < 0 || V <= 0 || ld < V) return LK_ERR_INVALID_ARG;
+  if (B == 0) return LK_OK;
+  if (!out_ids || !logits || B > 65535) return LK_ERR_INVALID_ARG;
+  if (noise && noise_ld < V) return LK_ERR_INVALID_ARG;
+  if (dtype != LK_DTYPE_F32 && dtype != LK_DTYPE_F16 && dtype != LK_DTYPE_BF16)
+    return LK_ERR_UNSUPPORTED;
+  SampleParams p;
+  p.logits = logits;
+  p.ld = ld;
+  p.V = V;
+  p.nchunks = choose_chunks(B, V);
+  const int64_t per = (static_cast<int64_t>(V) + p.nchunks - 1) / p.nchunks;
+  p.chunk = static_cast<int>(((per + kVec - 1) / kVec) * kVec);
+  p.nchunks = static_cast<int>((V + static_cast<int64_t>(p.chunk) - 1) / p.chunk);
+  if (B > kNoAllocMaxRows || static_cast<int64_t>(B) * p.nchunks > kNoAllocMaxPartials)
+    return LK_ERR_TOO_LARGE;
+  p.temps = temperatures;
+  p.noise = noise;
+  p.noise_ld = noise_ld;
+  p.seed_lo = static_cast<uint32_t>(seed);
+  p.seed_hi = static_cast<uint32_t>(seed >> 32);
+  p.off_lo = static_cast<uint32_t>(offset);
+  p.off_hi = static_cast<uint32_t>(offset >> 32);
+  p.noise_dump = noise_dump;
+  p.out = out_ids;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p.nchunks > 1) {
+    void* base = nullptr;
+    const int rc = scratch_address(&base);
+    if (rc != LK_OK) return rc;
+    uint8_t* ws = static_cast<uint8_t*>(base);
+    p.counters = reinterpret_cast<int32_t*>(ws);
+    p.part_key = reinterpret_cast<float*>(ws + kNoAllocCounterBytes);
+    p.part_idx = reinterpret_cast<int32_t*>(ws + kNoAllocCounterBytes + kNoAllocMaxPartials * 4);
+    // The counters must start at zero; clear the rows this call uses.
+    if (cudaMemsetAsync(p.counters, 0, static_cast<size_t>(B) * 4, s) != cudaSuccess)
+      return LK_ERR_CUDA;
+  } else {
+    p.counters = nullptr;
+    p.part_key = nullptr;
+    p.part_idx = nullptr;
+  }
+  const int esz = lk::dtype_size(dtype);
+  const bool vec = dtype != LK_DTYPE_F32 &&
+                   (reinterpret_cast<uintptr_t>(logits) & 15u) == 0 && ((ld * esz) & 15) == 0 &&
+                   (!noise || (((reinterpret_cast<uintptr_t>(noise) & 15u) == 0) &&
+                               ((noise_ld * 4) & 15) == 0)) &&
+                   (!noise_dump || ((reinterpret_cast<uintptr_t>(noise_dump) & 15u) == 0 &&
+                                    ((static_cast<int64_t>(V) * 4) & 15) == 0));
+  switch (dtype) {
+    case LK_DTYPE_BF16: return launch_sample<__nv_bfloat16>(p, B, vec, s);
+    case LK_DTYPE_F16: return launch_sample<__half>(p, B, vec, s);
+    default: return launch_sample<float>(p, B, false, s);
+  }
+}
