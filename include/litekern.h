@@ -84,8 +84,11 @@ int lk_store_kv(const void* key, const void* value, void* k_cache, void* v_cache
  * head stride D). dtype F16 or BF16; D = 128; block_size a multiple of 16;
  * G <= 8. A context_len of 0 yields NaN rows, like the reference's softmax
  * over an all -inf row.
- * num_splits: split-KV factor (0 = choose automatically with
- * lk_paged_decode_num_splits). workspace: at least
+ * num_splits: a positive value runs the split-KV kernel with that many
+ * splits per sequence; 0 picks the split count lk_paged_decode_num_splits
+ * returns; -1 runs the persistent stage-balanced kernel (one CTA per SM, the
+ * (sequence, 16-token stage) space cut into equal contiguous ranges, partial
+ * sequences merged by the last CTA to finish them). workspace: at least
  * lk_paged_decode_workspace_bytes(B, H, H_kv, D, num_splits) bytes, 256-byte
  * aligned, zero-filled before its first use; its counter region sits at a
  * fixed offset and every completed call leaves it zero again, so one

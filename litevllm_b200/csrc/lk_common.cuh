@@ -123,6 +123,26 @@ LK_DEVINL void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar
       : "memory");
 }
 
+// 1-D bulk copy global -> shared (both 16-byte aligned, size a multiple of
+// 16), completion signalled on an mbarrier via complete_tx. No multicast.
+LK_DEVINL void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Bulk-tensor prefetch of one box into L2 (no shared memory, no completion
+// signal): used to put more bytes in flight than the shared-memory ring holds.
+LK_DEVINL void tma_prefetch_3d(const CUtensorMap* map, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
 LK_DEVINL void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

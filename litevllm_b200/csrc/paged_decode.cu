@@ -20,6 +20,8 @@
 #include "lk_common.cuh"
 #include "lk_host.h"
 
+#include <stdlib.h>
+
 namespace {
 
 constexpr int kD = 128;          // head_dim
@@ -36,6 +38,7 @@ struct DecodeParams {
   int64_t num_blocks;
   int H, G, bs, max_blocks;
   float scale_log2;       // scale * log2(e)
+  int prefetch;           // stages prefetched into L2 ahead of the ring (0 = off)
   int stages_per_split;
   int num_splits;
   int num_groups;         // H_kv / HPC
@@ -118,34 +121,64 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     const int64_t num_slots = p.num_blocks * p.bs;
     bool ok = true;
     int it = 0;
-    for (int base = st0; base < st1 && ok; base += 32) {
-      // Each lane resolves one stage's starting slot ahead of time so the
-      // block-table reads overlap instead of serialising the TMA issue.
-      int slot0 = 0;
-      const int st = base + lane;
-      if (st < st1) {
-        const int pos = st * kTok;
-        const int blk = __ldg(bt + pos / p.bs);
-        if (blk < 0 || blk >= p.num_blocks) {
-          atomicOr(p.status, LK_STATUS_BLOCK_OOB);
-          slot0 = static_cast<int>(num_slots < 0x7fffffffLL ? num_slots : 0x7fffffffLL);  // past the end: TMA reads zeros
-        } else {
-          slot0 = blk * p.bs + (pos % p.bs);
+    // Each lane resolves one stage's starting slot ahead of time so the
+    // block-table reads overlap instead of serialising the TMA issue; the
+    // next 32 stages are resolved one batch early so that L2 prefetches can
+    // run `prefetch` stages ahead of the shared-memory ring.
+    const int oob = static_cast<int>(num_slots < 0x7fffffffLL ? num_slots : 0x7fffffffLL);
+    auto lookup = [&](int st) -> int {
+      if (st >= st1) return -1;
+      const int pos = st * kTok;
+      const int blk = __ldg(bt + pos / p.bs);
+      if (blk < 0 || blk >= p.num_blocks) {
+        atomicOr(p.status, LK_STATUS_BLOCK_OOB);
+        return oob;  // past the end: TMA reads zeros
+      }
+      return blk * p.bs + (pos % p.bs);
+    };
+    const int PF = p.prefetch;
+    const int h0 = hg * HPC;
+    int nxt = lookup(st0 + lane);
+    {
+      // warm-up prefetches for the first PF stages
+      for (int i = 0; i < PF && i < 32; ++i) {
+        const int sl = __shfl_sync(0xffffffffu, nxt, i);
+        if (lane == 0 && sl >= 0) {
+          lk::tma_prefetch_3d(&kmap, 0, sl, h0);
+          lk::tma_prefetch_3d(&kmap, 64, sl, h0);
+          lk::tma_prefetch_3d(&vmap, 0, sl, h0);
+          lk::tma_prefetch_3d(&vmap, 64, sl, h0);
         }
       }
+    }
+    for (int base = st0; base < st1 && ok; base += 32) {
+      const int cur = nxt;
+      nxt = lookup(base + 32 + lane);
       const int n = min(32, st1 - base);
       for (int i = 0; i < n; ++i, ++it) {
-        const int slot = __shfl_sync(0xffffffffu, slot0, i);
+        const int slot = __shfl_sync(0xffffffffu, cur, i);
+        int pslot = -1;
+        if (PF > 0) {
+          const int j = i + PF;
+          const int a = __shfl_sync(0xffffffffu, cur, j & 31);
+          const int c = __shfl_sync(0xffffffffu, nxt, j & 31);
+          pslot = j < 32 ? a : c;
+        }
         if (lane == 0) {
           const int s = it % NST;
           const uint32_t ph = ((it / NST) & 1) ^ 1;
+          if (pslot >= 0) {
+            lk::tma_prefetch_3d(&kmap, 0, pslot, h0);
+            lk::tma_prefetch_3d(&kmap, 64, pslot, h0);
+            lk::tma_prefetch_3d(&vmap, 0, pslot, h0);
+            lk::tma_prefetch_3d(&vmap, 64, pslot, h0);
+          }
           if (!lk::mbar_wait(&empty_bar[s], ph)) {
             atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
             ok = false;
           } else {
             lk::mbar_arrive_expect_tx(&full_bar[s], Shape::kStageBytes);
             uint8_t* dst = smem + s * Shape::kStageBytes;
-            const int h0 = hg * HPC;
             lk::tma_load_3d(dst, &kmap, &full_bar[s], 0, slot, h0);
             lk::tma_load_3d(dst + Shape::kBoxBytes, &kmap, &full_bar[s], 64, slot, h0);
             lk::tma_load_3d(dst + 2 * Shape::kBoxBytes, &vmap, &full_bar[s], 0, slot, h0);
@@ -325,6 +358,401 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
   if (threadIdx.x == 0) p.counters[b * p.num_groups + hg] = 0;
 }
 
+// ------------------------------------------------------------------------
+// Persistent, stage-balanced decode.
+//
+// The (unit, stage) space — unit u = b * groups + hg, nst(u) = ceil(ctx_b/16)
+// stages of 16 tokens — is flattened in unit order and cut into gridDim.x
+// equal contiguous ranges, one per CTA (grid = number of SMs, one CTA per
+// SM). The producer streams TMA loads across unit boundaries without
+// draining the ring; every stage carries a small descriptor (unit, stage,
+// flags) in shared memory. A unit split across CTAs (at most two partial
+// segments per CTA: its first and its last) writes (m, l, o) partials into
+// slot (cta, 0|1); each consumer warp counts the segments of its own
+// (sequence, KV head) with an atomic and the last one merges. No CTA ever
+// waits on another.
+struct DecodeState {
+  float o[8][4];
+  float m0, m1, l0, l1;
+};
+
+template <typename T, int kBoxBytes>
+LK_DEVINL void decode_stage(DecodeState& st, const uint32_t (&qb)[8][2], uint32_t kb,
+                            uint32_t vb, int pos0, int ctx, float sl2, int lane) {
+  const int g = lane >> 2, j = lane >> 3;
+  float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const uint32_t row = (lane & 7) + ((j & 1) << 3);
+    const uint32_t chunk = ((ks & 3) << 1) + (j >> 1);
+    uint32_t a[4];
+    lk::ldsm_x4(kb + (ks >> 2) * kBoxBytes + lk::swz128(row, chunk), a[0], a[1], a[2], a[3]);
+    lk::mma16816<T>(sc, a, qb[ks][0], qb[ks][1]);
+  }
+  const int pos = pos0 + g;
+  float x0 = sc[0] * sl2, x1 = sc[1] * sl2, x2 = sc[2] * sl2, x3 = sc[3] * sl2;
+  if (pos >= ctx) x0 = x1 = -INFINITY;
+  if (pos + 8 >= ctx) x2 = x3 = -INFINITY;
+  float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+  }
+  const float mn0 = fmaxf(st.m0, mx0), mn1 = fmaxf(st.m1, mx1);
+  const float al0 = exp2f(st.m0 - mn0), al1 = exp2f(st.m1 - mn1);
+  const float p0 = exp2f(x0 - mn0), p1 = exp2f(x1 - mn1);
+  const float p2 = exp2f(x2 - mn0), p3 = exp2f(x3 - mn1);
+  st.l0 = st.l0 * al0 + p0 + p2;
+  st.l1 = st.l1 * al1 + p1 + p3;
+  st.m0 = mn0;
+  st.m1 = mn1;
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    st.o[mt][0] *= al0;
+    st.o[mt][1] *= al1;
+    st.o[mt][2] *= al0;
+    st.o[mt][3] *= al1;
+  }
+  const uint32_t pb0 = lk::movmatrix_t(lk::pack2<T>(p0, p1));
+  const uint32_t pb1 = lk::movmatrix_t(lk::pack2<T>(p2, p3));
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    const uint32_t tok = (lane & 7) + ((j >> 1) << 3);
+    const uint32_t chunk = ((mt & 3) << 1) + (j & 1);
+    uint32_t a[4];
+    lk::ldsm_x4_t(vb + (mt >> 2) * kBoxBytes + lk::swz128(tok, chunk), a[0], a[1], a[2], a[3]);
+    lk::mma16816<T>(st.o[mt], a, pb0, pb1);
+  }
+}
+
+// CTA that owns flattened stage s when S stages are cut into n ranges
+// [floor(i*S/n), floor((i+1)*S/n)).
+LK_DEVINL int stage_owner(int64_t s, int64_t S, int n) {
+  return static_cast<int>(((s + 1) * n - 1) / S);
+}
+
+// Whether CTA c's range is non-empty (S < n leaves some CTAs without stages;
+// such CTAs hold no segment of any unit).
+LK_DEVINL bool range_nonempty(int c, int64_t S, int n) {
+  return (S * (c + 1)) / n > (S * c) / n;
+}
+
+constexpr int kFirst = 1, kLast = 2;
+
+template <typename T, int HPC, int NST>
+__global__ void __launch_bounds__((HPC + 1) * 32, 1)
+paged_decode_persistent_kernel(const __grid_constant__ CUtensorMap kmap,
+                               const __grid_constant__ CUtensorMap vmap, const DecodeParams p,
+                               int num_units) {
+  using Shape = DecodeShape<HPC, NST>;
+  constexpr int kThreads = Shape::kThreads;
+  constexpr int kWarps = HPC + 1;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[NST];
+  __shared__ __align__(8) uint64_t empty_bar[NST];
+  __shared__ int meta[NST][6];  // unit, stage-in-unit, ctx, flags, P lo, P hi
+  __shared__ long long s_red[kWarps];
+  __shared__ long long s_scan[kWarps];
+  __shared__ long long s_P0;
+  __shared__ int s_u0;
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int cta = blockIdx.x, nctas = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.G, groups = p.num_groups;
+  const int cap = p.max_blocks * p.bs;
+
+  // ---- pass 1: total stages; NaN rows for empty contexts
+  long long local = 0;
+  for (int u = threadIdx.x; u < num_units; u += kThreads) {
+    const int b = u / groups;
+    int ctx = p.context_lens[b];
+    if (ctx > cap) {
+      if (cta == 0) atomicOr(p.status, LK_STATUS_CTX_OOB);
+      ctx = cap;
+    }
+    const int n = ctx > 0 ? (ctx + kTok - 1) / kTok : 0;
+    local += n;
+    if (n == 0 && (u % nctas) == cta) {
+      // softmax over an all -inf row is NaN in the reference; reproduce it.
+      T* out = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride;
+      const int nq = HPC * G, hg = u % groups;
+      for (int i = 0; i < nq * kD; ++i)
+        store_out<T>(out + (hg * nq) * kD + i, __int_as_float(0x7fc00000));
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) local += __shfl_xor_sync(0xffffffffu, local, off);
+  if (lane == 0) s_red[warp] = local;
+  if (threadIdx.x == 0) s_u0 = -1;
+  __syncthreads();
+  long long S = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) S += s_red[w];
+  const long long start = S * cta / nctas, end = S * (cta + 1) / nctas;
+  if (start >= end) return;
+
+  // ---- pass 2: first unit u0 with P(u0) <= start < P(u0) + nst(u0)
+  long long base = 0;
+  for (int c0 = 0; c0 < num_units; c0 += kThreads) {
+    const int u = c0 + threadIdx.x;
+    int n = 0;
+    if (u < num_units) {
+      const int ctx = min(p.context_lens[u / groups], cap);
+      n = ctx > 0 ? (ctx + kTok - 1) / kTok : 0;
+    }
+    long long incl = n;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const long long v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
+    }
+    if (lane == 31) s_scan[warp] = incl;
+    __syncthreads();
+    long long woff = 0, tot = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      if (w < warp) woff += s_scan[w];
+      tot += s_scan[w];
+    }
+    const long long P = base + woff + incl - n;
+    if (n > 0 && P <= start && start < P + n) {
+      s_u0 = u;
+      s_P0 = P;
+    }
+    __syncthreads();
+    if (s_u0 >= 0) break;
+    base += tot;
+  }
+  const int u0 = s_u0;
+  const long long P0 = s_P0;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < NST; ++s) {
+      lk::mbar_init(&full_bar[s], 1);
+      lk::mbar_init(&empty_bar[s], HPC);
+    }
+    lk::fence_barrier_init();
+  }
+  __syncthreads();
+  const int total = static_cast<int>(end - start);
+
+  if (warp == HPC) {
+    // ------------------------------------------------------- producer ---
+    if (lane == 0) {
+      lk::prefetch_tensormap(&kmap);
+      lk::prefetch_tensormap(&vmap);
+    }
+    const int64_t num_slots = p.num_blocks * p.bs;
+    const int oob = static_cast<int>(num_slots < 0x7fffffffLL ? num_slots : 0x7fffffffLL);
+    bool ok = true;
+    int it = 0;
+    long long P = P0;
+    for (int u = u0; u < num_units && P < end && ok; ++u) {
+      const int b = u / groups, hg = u % groups;
+      const int ctx = min(p.context_lens[b], cap);
+      const int n = ctx > 0 ? (ctx + kTok - 1) / kTok : 0;
+      const int lo = static_cast<int>((start > P ? start : P) - P);
+      const int hi = static_cast<int>(((P + n) < end ? (P + n) : end) - P);
+      const int32_t* bt = p.block_tables + static_cast<int64_t>(b) * p.bt_stride;
+      const int h0 = hg * HPC;
+      const int PF = p.prefetch;
+      auto lookup = [&](int t) -> int {
+        if (t >= hi) return -1;
+        const int pos = t * kTok;
+        const int blk = __ldg(bt + pos / p.bs);
+        if (blk < 0 || blk >= p.num_blocks) {
+          atomicOr(p.status, LK_STATUS_BLOCK_OOB);
+          return oob;
+        }
+        return blk * p.bs + (pos % p.bs);
+      };
+      int nxt = lookup(lo + lane);
+      for (int i = 0; i < PF && i < 32; ++i) {
+        const int sl = __shfl_sync(0xffffffffu, nxt, i);
+        if (lane == 0 && sl >= 0) {
+          lk::tma_prefetch_3d(&kmap, 0, sl, h0);
+          lk::tma_prefetch_3d(&kmap, 64, sl, h0);
+          lk::tma_prefetch_3d(&vmap, 0, sl, h0);
+          lk::tma_prefetch_3d(&vmap, 64, sl, h0);
+        }
+      }
+      for (int t0 = lo; t0 < hi && ok; t0 += 32) {
+        const int cur = nxt;
+        nxt = lookup(t0 + 32 + lane);
+        const int cnt = min(32, hi - t0);
+        for (int i = 0; i < cnt; ++i, ++it) {
+          const int slot = __shfl_sync(0xffffffffu, cur, i);
+          int pslot = -1;
+          if (PF > 0) {
+            const int j = i + PF;
+            const int a = __shfl_sync(0xffffffffu, cur, j & 31);
+            const int c = __shfl_sync(0xffffffffu, nxt, j & 31);
+            pslot = j < 32 ? a : c;
+          }
+          if (lane == 0) {
+            const int s = it % NST;
+            if (pslot >= 0) {
+              lk::tma_prefetch_3d(&kmap, 0, pslot, h0);
+              lk::tma_prefetch_3d(&kmap, 64, pslot, h0);
+              lk::tma_prefetch_3d(&vmap, 0, pslot, h0);
+              lk::tma_prefetch_3d(&vmap, 64, pslot, h0);
+            }
+            if (!lk::mbar_wait(&empty_bar[s], ((it / NST) & 1) ^ 1)) {
+              atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
+              ok = false;
+            } else {
+              const int tt = t0 + i;
+              meta[s][0] = u;
+              meta[s][1] = tt;
+              meta[s][2] = ctx;
+              meta[s][3] = (tt == lo ? kFirst : 0) | (tt == hi - 1 ? kLast : 0);
+              meta[s][4] = static_cast<int>(P & 0xffffffffLL);
+              meta[s][5] = static_cast<int>(P >> 32);
+              lk::mbar_arrive_expect_tx(&full_bar[s], Shape::kStageBytes);
+              uint8_t* dst = smem + s * Shape::kStageBytes;
+              lk::tma_load_3d(dst, &kmap, &full_bar[s], 0, slot, h0);
+              lk::tma_load_3d(dst + Shape::kBoxBytes, &kmap, &full_bar[s], 64, slot, h0);
+              lk::tma_load_3d(dst + 2 * Shape::kBoxBytes, &vmap, &full_bar[s], 0, slot, h0);
+              lk::tma_load_3d(dst + 3 * Shape::kBoxBytes, &vmap, &full_bar[s], 64, slot, h0);
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+          if (!ok) break;
+        }
+      }
+      P += n;
+    }
+    return;
+  }
+
+  // --------------------------------------------------------- consumers ---
+  const int g = lane >> 2, c = lane & 3;
+  const int n0 = 2 * c, n1 = 2 * c + 1;
+  const float sl2 = p.scale_log2;
+  const uint32_t smem_base = lk::smem_u32(smem) + warp * (kTok * 128);
+  DecodeState st;
+  uint32_t qb[8][2];
+  for (int it = 0; it < total; ++it) {
+    const int s = it % NST;
+    if (!lk::mbar_wait(&full_bar[s], (it / NST) & 1)) {
+      if (lane == 0) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
+      break;
+    }
+    const int u = meta[s][0], t = meta[s][1], ctx = meta[s][2], flags = meta[s][3];
+    const long long P = (static_cast<long long>(meta[s][5]) << 32) |
+                        static_cast<unsigned int>(meta[s][4]);
+    const int b = u / groups, hg = u % groups;
+    const int kvh = hg * HPC + warp;
+    const int qh0 = kvh * G;
+    if (flags & kFirst) {
+      const T* qrow = static_cast<const T*>(p.q) + static_cast<int64_t>(b) * p.q_stride +
+                      static_cast<int64_t>(qh0 + g) * kD;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        qb[ks][0] = g < G ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * c) : 0u;
+        qb[ks][1] = g < G ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * c) : 0u;
+      }
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) st.o[mt][0] = st.o[mt][1] = st.o[mt][2] = st.o[mt][3] = 0.f;
+      st.m0 = st.m1 = -INFINITY;
+      st.l0 = st.l1 = 0.f;
+    }
+    const uint32_t kb = smem_base + s * Shape::kStageBytes;
+    decode_stage<T, Shape::kBoxBytes>(st, qb, kb, kb + 2 * Shape::kBoxBytes, t * kTok, ctx, sl2,
+                                      lane);
+    __syncwarp();
+    if (lane == 0) lk::mbar_arrive(&empty_bar[s]);
+    if (!(flags & kLast)) continue;
+
+    // ---- segment finished: final output, or partial + merge by the last segment
+    float l0 = st.l0, l1 = st.l1;
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    const int nst = (ctx + kTok - 1) / kTok;
+    const int c0 = stage_owner(P, S, nctas), c1 = stage_owner(P + nst - 1, S, nctas);
+    T* out = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride;
+    if (c0 == c1) {
+      const float r0 = 1.f / l0, r1 = 1.f / l1;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int d = mt * 16 + g;
+        if (n0 < G) {
+          store_out<T>(out + (qh0 + n0) * kD + d, st.o[mt][0] * r0);
+          store_out<T>(out + (qh0 + n0) * kD + d + 8, st.o[mt][2] * r0);
+        }
+        if (n1 < G) {
+          store_out<T>(out + (qh0 + n1) * kD + d, st.o[mt][1] * r1);
+          store_out<T>(out + (qh0 + n1) * kD + d + 8, st.o[mt][3] * r1);
+        }
+      }
+      continue;
+    }
+    const int slot = cta * 2 + (cta == c0 ? 1 : 0);
+    const int64_t prow = static_cast<int64_t>(slot) * p.H;
+    float* po = p.part_o + prow * kD;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      const int d = mt * 16 + g;
+      if (n0 < G) {
+        po[(qh0 + n0) * kD + d] = st.o[mt][0];
+        po[(qh0 + n0) * kD + d + 8] = st.o[mt][2];
+      }
+      if (n1 < G) {
+        po[(qh0 + n1) * kD + d] = st.o[mt][1];
+        po[(qh0 + n1) * kD + d + 8] = st.o[mt][3];
+      }
+    }
+    if (g == 0) {
+      float* pml = p.part_ml + prow * 2;
+      if (n0 < G) {
+        pml[(qh0 + n0) * 2] = st.m0;
+        pml[(qh0 + n0) * 2 + 1] = l0;
+      }
+      if (n1 < G) {
+        pml[(qh0 + n1) * 2] = st.m1;
+        pml[(qh0 + n1) * 2 + 1] = l1;
+      }
+    }
+    __threadfence();
+    __syncwarp();
+    int prev = 0;
+    int32_t* counter = p.counters + static_cast<int64_t>(b) * (groups * HPC) + kvh;
+    if (lane == 0) prev = atomicAdd(counter, 1);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    int nseg = 0;
+    for (int cc = c0; cc <= c1; ++cc) nseg += range_nonempty(cc, S, nctas) ? 1 : 0;
+    if (prev != nseg - 1) continue;
+    __threadfence();
+    for (int i = lane; i < G * kD; i += 32) {
+      const int qh = qh0 + i / kD, d = i % kD;
+      float M = -INFINITY;
+      for (int cc = c0; cc <= c1; ++cc) {
+        if (!range_nonempty(cc, S, nctas)) continue;
+        const int sl = cc * 2 + (cc == c0 ? 1 : 0);
+        M = fmaxf(M, __ldcg(p.part_ml + (static_cast<int64_t>(sl) * p.H + qh) * 2));
+      }
+      float L = 0.f, acc = 0.f;
+      for (int cc = c0; cc <= c1; ++cc) {
+        if (!range_nonempty(cc, S, nctas)) continue;
+        const int sl = cc * 2 + (cc == c0 ? 1 : 0);
+        const float* ml = p.part_ml + (static_cast<int64_t>(sl) * p.H + qh) * 2;
+        const float w = exp2f(__ldcg(ml) - M);
+        L += __ldcg(ml + 1) * w;
+        acc += __ldcg(p.part_o + (static_cast<int64_t>(sl) * p.H + qh) * kD + d) * w;
+      }
+      store_out<T>(out + qh * kD + d, acc / L);
+    }
+    __syncwarp();
+    if (lane == 0) *counter = 0;
+  }
+}
+
 // Workspace layout: [status: int32, padded to 256 B][counters: kMaxCounters
 // int32, a fixed region so that calls with different B find it where the
 // previous call left it zeroed][part_ml: B*splits*H*2 f32][part_o: B*splits*H*D f32]
@@ -332,7 +760,23 @@ constexpr int64_t kMaxCounters = 65536;
 constexpr size_t kHeadBytes = 256 + kMaxCounters * 4;
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
+// KV heads per CTA: the largest of 8, 4, 2, 1 that divides H_kv, capped by the
+// LITEKERN_DECODE_HEADS_PER_CTA environment variable (read once; a tuning knob).
+int heads_cap() {
+  static int cap = [] {
+    const char* e = getenv("LITEKERN_DECODE_HEADS_PER_CTA");
+    const int v = e ? atoi(e) : 8;
+    return (v == 1 || v == 2 || v == 4 || v == 8) ? v : 8;
+  }();
+  return cap;
+}
+
 int heads_per_cta(int H_kv) {
+  const int cap = heads_cap();
+  if (cap < 8) {
+    for (int h = cap; h >= 1; h >>= 1)
+      if (H_kv % h == 0) return h;
+  }
   if (H_kv % 8 == 0) return 8;
   if (H_kv % 4 == 0) return 4;
   if (H_kv % 2 == 0) return 2;
@@ -369,6 +813,57 @@ int dispatch_decode(int hpc, const CUtensorMap& km, const CUtensorMap& vm, const
   }
 }
 
+template <typename T, int HPC, int NST>
+int launch_persistent(const CUtensorMap& km, const CUtensorMap& vm, const DecodeParams& p,
+                      int num_units, int grid, cudaStream_t s) {
+  using Shape = DecodeShape<HPC, NST>;
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(paged_decode_persistent_kernel<T, HPC, NST>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Shape::kSmem) != cudaSuccess)
+      return LK_ERR_CUDA;
+    configured[dev] = 1;
+  }
+  paged_decode_persistent_kernel<T, HPC, NST>
+      <<<grid, Shape::kThreads, Shape::kSmem, s>>>(km, vm, p, num_units);
+  return lk::check_launch();
+}
+
+template <typename T>
+int dispatch_persistent(int hpc, const CUtensorMap& km, const CUtensorMap& vm,
+                        const DecodeParams& p, int num_units, int grid, cudaStream_t s) {
+  switch (hpc) {
+    case 8: return launch_persistent<T, 8, 3>(km, vm, p, num_units, grid, s);
+    case 4: return launch_persistent<T, 4, 6>(km, vm, p, num_units, grid, s);
+    case 2: return launch_persistent<T, 2, 12>(km, vm, p, num_units, grid, s);
+    default: return launch_persistent<T, 1, 24>(km, vm, p, num_units, grid, s);
+  }
+}
+
+// Stages the producers prefetch into L2 ahead of the shared-memory ring;
+// LITEKERN_DECODE_PREFETCH (read once, 0..31) overrides the default.
+int prefetch_distance() {
+  static int d = [] {
+    const char* e = getenv("LITEKERN_DECODE_PREFETCH");
+    int v = e ? atoi(e) : 0;
+    return v < 0 ? 0 : (v > 31 ? 31 : v);
+  }();
+  return d;
+}
+
+// CTAs of the persistent kernel: one per SM (its shared-memory ring takes the SM).
+// LITEKERN_DECODE_GRID (read once) overrides it, for tuning.
+int persistent_grid() {
+  static int override_grid = [] {
+    const char* e = getenv("LITEKERN_DECODE_GRID");
+    return e ? atoi(e) : 0;
+  }();
+  return override_grid > 0 ? override_grid : lk::num_sms();
+}
+
 }  // namespace
 
 extern "C" int lk_paged_decode_num_splits(int32_t B, int32_t H_kv, int32_t max_blocks_per_seq,
@@ -377,13 +872,13 @@ extern "C" int lk_paged_decode_num_splits(int32_t B, int32_t H_kv, int32_t max_b
   const int groups = H_kv / heads_per_cta(H_kv);
   const int64_t max_stages = (static_cast<int64_t>(max_blocks_per_seq) * block_size + 15) / 16;
   const int64_t units = static_cast<int64_t>(B) * groups;
-  // Enough CTAs to cover every SM twice even if all sequences were long,
-  // no split shorter than 8 stages (128 tokens), and no split longer than
-  // 32 stages (512 tokens, 2 MiB of bf16 K+V) so that long sequences do not
-  // leave a tail on a few SMs.
-  int64_t splits = (2 * lk::num_sms() + units - 1) / units;
-  splits = std::min<int64_t>(splits, (max_stages + 7) / 8);
-  splits = std::max<int64_t>(splits, (max_stages + 31) / 32);
+  // Measured on B200 (config 2: B=256, contexts <= 4096; config 5: B=8..64,
+  // contexts 32K-128K): fewer, longer CTAs stream faster than many short
+  // ones. A split holds at least 64 stages (1024 tokens) and long contexts
+  // are cut into about 16 splits.
+  (void)units;
+  const int64_t spp = std::max<int64_t>(64, (max_stages + 15) / 16);
+  int64_t splits = (max_stages + spp - 1) / spp;
   splits = std::max<int64_t>(1, std::min<int64_t>(splits, max_stages));
   return static_cast<int>(std::min<int64_t>(splits, 65535));
 }
@@ -394,7 +889,11 @@ extern "C" size_t lk_paged_decode_workspace_bytes(int32_t B, int32_t H, int32_t 
   const int groups = H_kv / heads_per_cta(H_kv);
   (void)groups;
   size_t bytes = kHeadBytes;
-  if (num_splits > 1) {
+  if (num_splits < 0) {  // persistent kernel: two partial slots per CTA
+    const size_t slots = 2 * static_cast<size_t>(persistent_grid());
+    bytes += align256(slots * H * 2 * 4);
+    bytes += align256(slots * H * D * 4);
+  } else if (num_splits > 1) {
     bytes += align256(static_cast<size_t>(B) * num_splits * H * 2 * 4);
     bytes += align256(static_cast<size_t>(B) * num_splits * H * D * 4);
   }
@@ -418,12 +917,11 @@ extern "C" int lk_paged_decode(void* out, int64_t out_token_stride, const void* 
   if (dtype != LK_DTYPE_BF16 && dtype != LK_DTYPE_F16) return LK_ERR_UNSUPPORTED;
   if (D != kD || block_size % kTok != 0 || H / H_kv > 8) return LK_ERR_UNSUPPORTED;
   if (B > 65535 || max_blocks_per_seq == 0) return LK_ERR_INVALID_ARG;
-  if (static_cast<int64_t>(B) * (H_kv / heads_per_cta(H_kv)) > kMaxCounters)
-    return LK_ERR_UNSUPPORTED;
+  if (static_cast<int64_t>(B) * H_kv > kMaxCounters) return LK_ERR_UNSUPPORTED;
   if (num_blocks * block_size > 0x7fffffffLL) return LK_ERR_UNSUPPORTED;
   if (((reinterpret_cast<uintptr_t>(q) & 3u) != 0) || (q_token_stride & 1) != 0)
     return LK_ERR_ALIGNMENT;
-  if (num_splits <= 0)
+  if (num_splits == 0)
     num_splits = lk_paged_decode_num_splits(B, H_kv, max_blocks_per_seq, block_size);
   const size_t need = lk_paged_decode_workspace_bytes(B, H, H_kv, D, num_splits);
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
@@ -452,17 +950,26 @@ extern "C" int lk_paged_decode(void* out, int64_t out_token_stride, const void* 
   p.bs = block_size;
   p.max_blocks = max_blocks_per_seq;
   p.scale_log2 = scale * 1.4426950408889634f;
-  p.num_splits = num_splits;
-  p.stages_per_split = static_cast<int>((max_stages + num_splits - 1) / num_splits);
+  p.prefetch = prefetch_distance();
+  const bool persistent = num_splits < 0;
+  p.num_splits = persistent ? 1 : num_splits;
+  p.stages_per_split = static_cast<int>((max_stages + p.num_splits - 1) / p.num_splits);
   p.num_groups = H_kv / hpc;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const size_t cnt_bytes = kHeadBytes;
   p.status = reinterpret_cast<int32_t*>(ws);
   p.counters = reinterpret_cast<int32_t*>(ws + 256);
   p.part_ml = reinterpret_cast<float*>(ws + cnt_bytes);
-  p.part_o = reinterpret_cast<float*>(
-      ws + cnt_bytes + align256(static_cast<size_t>(B) * num_splits * H * 2 * 4));
+  const size_t ml_rows = persistent ? 2 * static_cast<size_t>(persistent_grid())
+                                    : static_cast<size_t>(B) * num_splits;
+  p.part_o = reinterpret_cast<float*>(ws + cnt_bytes + align256(ml_rows * H * 2 * 4));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (persistent) {
+    const int units = B * p.num_groups;
+    if (dtype == LK_DTYPE_BF16)
+      return dispatch_persistent<__nv_bfloat16>(hpc, km, vm, p, units, persistent_grid(), s);
+    return dispatch_persistent<__half>(hpc, km, vm, p, units, persistent_grid(), s);
+  }
   if (dtype == LK_DTYPE_BF16) return dispatch_decode<__nv_bfloat16>(hpc, km, vm, p, B, s);
   return dispatch_decode<__half>(hpc, km, vm, p, B, s);
 }

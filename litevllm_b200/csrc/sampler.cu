@@ -22,13 +22,19 @@
 #include "lk_common.cuh"
 #include "lk_host.h"
 
+#include <cooperative_groups.h>
+#include <stdlib.h>
+
 #include <mutex>
 #include <type_traits>
+
+namespace cg = cooperative_groups;
 
 namespace {
 
 constexpr int kSampThreads = 256;
 constexpr int kVec = 8;  // elements per 16-byte vector of 16-bit logits
+constexpr int kSampCtasPerSm = 6;
 
 struct SampleParams {
   const void* logits;
@@ -245,7 +251,7 @@ LK_DEVINL void block_reduce(float& k, int& i) {
 }
 
 template <typename T, bool VEC>
-__global__ void __launch_bounds__(kSampThreads) sample_kernel(const SampleParams p) {
+__global__ void __launch_bounds__(kSampThreads, kSampCtasPerSm) sample_kernel(const SampleParams p) {
   const int ch = blockIdx.x, b = blockIdx.y;
   const float temp = p.temps ? p.temps[b] : 0.f;
   const int v0 = ch * p.chunk, v1 = min(p.V, v0 + p.chunk);
@@ -336,6 +342,261 @@ softmax_temp_kernel(float* __restrict__ probs, int64_t probs_ld, const T* __rest
     prow[v] = __expf(__fdiv_rn(lk::Elem<T>::to_f(row[v]), t) - M) * inv;
 }
 
+
+// ---------------------------------------------------- greedy-only kernel ---
+// All rows greedy (temperatures == NULL), 16-bit logits, 16-byte aligned
+// rows: the vector max of 8 values is taken with packed NaN-propagating
+// max instructions, and the first index of that max is searched only when
+// it beats the thread's running best, so the common path is three packed
+// max operations per 8 logits.
+// Packed NaN-propagating max of two 16-bit pairs, and NaN-propagating fp32 max.
+template <typename T> LK_DEVINL uint32_t pmax_nan(uint32_t a, uint32_t b);
+template <> LK_DEVINL uint32_t pmax_nan<__nv_bfloat16>(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+template <> LK_DEVINL uint32_t pmax_nan<__half>(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+LK_DEVINL float fmax_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+template <typename T> LK_DEVINL float half_lo(uint32_t w);
+template <typename T> LK_DEVINL float half_hi(uint32_t w);
+template <> LK_DEVINL float half_lo<__nv_bfloat16>(uint32_t w) { return __uint_as_float(w << 16); }
+template <> LK_DEVINL float half_hi<__nv_bfloat16>(uint32_t w) {
+  return __uint_as_float(w & 0xffff0000u);
+}
+template <> LK_DEVINL float half_lo<__half>(uint32_t w) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xffffu)));
+}
+template <> LK_DEVINL float half_hi<__half>(uint32_t w) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16)));
+}
+
+// Bits of a 16-bit float that compare equal to vm, and the NaN test, in the
+// raw 16-bit encoding (exact: vm came from one of these values).
+template <typename T> LK_DEVINL uint32_t to_bits16(float vm);
+template <> LK_DEVINL uint32_t to_bits16<__nv_bfloat16>(float vm) {
+  return __float_as_uint(vm) >> 16;
+}
+template <> LK_DEVINL uint32_t to_bits16<__half>(float vm) {
+  return __half_as_ushort(__float2half_rn(vm));
+}
+template <typename T> LK_DEVINL bool is_nan16(uint32_t h);
+template <> LK_DEVINL bool is_nan16<__nv_bfloat16>(uint32_t h) { return (h & 0x7fffu) > 0x7f80u; }
+template <> LK_DEVINL bool is_nan16<__half>(uint32_t h) { return (h & 0x7fffu) > 0x7c00u; }
+
+// The vector holds a new running best: index (0..7) of its first occurrence.
+// +0 and -0 compare equal, as in the fp32 comparison.
+template <typename T>
+LK_DEVINL int first_index_of(const uint4& raw, float vm) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  const bool want_nan = vm != vm;
+  const uint32_t hv = to_bits16<T>(vm);
+  int e = 8;
+#pragma unroll
+  for (int k = 7; k >= 0; --k) {
+    const uint32_t h = (k & 1) ? (w[k >> 1] >> 16) : (w[k >> 1] & 0xffffu);
+    const bool hit = want_nan ? is_nan16<T>(h) : (h == hv || ((h | hv) & 0x7fffu) == 0u);
+    e = hit ? k : e;
+  }
+  return e;
+}
+
+template <typename T>
+LK_DEVINL void argmax_vec(const uint4& raw, int base, float& best, int& besti) {
+  const uint32_t m = pmax_nan<T>(pmax_nan<T>(raw.x, raw.y), pmax_nan<T>(raw.z, raw.w));
+  const float vm = fmax_nan(half_lo<T>(m), half_hi<T>(m));
+  if (beats_later(vm, best)) {
+    besti = base + first_index_of<T>(raw, vm);
+    best = vm;
+  }
+}
+
+template <typename T, int kU, int kMinBlocks, bool kCluster>
+__global__ void __launch_bounds__(kSampThreads, kMinBlocks) argmax_kernel(const SampleParams p) {
+  const int ch = blockIdx.x, b = blockIdx.y;
+  const int v0 = ch * p.chunk, v1 = min(p.V, v0 + p.chunk);
+  const T* row = static_cast<const T*>(p.logits) + static_cast<int64_t>(b) * p.ld;
+  float best = -INFINITY;
+  int besti = 0x7fffffff;
+  const int vend = v0 + ((v1 - v0) / kVec) * kVec;
+  constexpr int kStride = kSampThreads * kVec;
+  int v = v0 + threadIdx.x * kVec;
+  for (; v + (kU - 1) * kStride < vend; v += kU * kStride) {
+    uint4 raw[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) raw[u] = __ldcs(reinterpret_cast<const uint4*>(row + v + u * kStride));
+#pragma unroll
+    for (int u = 0; u < kU; ++u) argmax_vec<T>(raw[u], v + u * kStride, best, besti);
+  }
+  for (; v < vend; v += kStride)
+    argmax_vec<T>(__ldcs(reinterpret_cast<const uint4*>(row + v)), v, best, besti);
+  for (int t = vend + threadIdx.x; t < v1; t += kSampThreads) {
+    const float x = lk::Elem<T>::to_f(row[t]);
+    if (beats_later(x, best)) {
+      best = x;
+      besti = t;
+    }
+  }
+  block_reduce(best, besti);
+  if constexpr (kCluster) {
+    // The row's chunks form one thread-block cluster: every CTA publishes
+    // its winner in its own shared memory and rank 0 reads them all through
+    // distributed shared memory. The second cluster barrier keeps each CTA's
+    // shared memory alive until rank 0 has read it.
+    __shared__ float c_key;
+    __shared__ int c_idx;
+    cg::cluster_group cluster = cg::this_cluster();
+    if (threadIdx.x == 0) {
+      c_key = best;
+      c_idx = besti;
+    }
+    cluster.sync();
+    if (cluster.block_rank() == 0 && threadIdx.x < 32) {
+      float k = -INFINITY;
+      int i = 0x7fffffff;
+      for (int r = threadIdx.x; r < static_cast<int>(cluster.num_blocks()); r += 32) {
+        const float k2 = *cluster.map_shared_rank(&c_key, r);
+        const int i2 = *cluster.map_shared_rank(&c_idx, r);
+        if (beats(k2, i2, k, i)) {
+          k = k2;
+          i = i2;
+        }
+      }
+      reduce_pair(k, i);
+      if (threadIdx.x == 0) p.out[b] = i == 0x7fffffff ? 0 : i;
+    }
+    cluster.sync();
+    return;
+  }
+  if (p.nchunks == 1) {
+    if (threadIdx.x == 0) p.out[b] = besti == 0x7fffffff ? 0 : besti;
+    return;
+  }
+  __shared__ int s_last;
+  if (threadIdx.x == 0) {
+    p.part_key[static_cast<int64_t>(b) * p.nchunks + ch] = best;
+    p.part_idx[static_cast<int64_t>(b) * p.nchunks + ch] = besti;
+    __threadfence();
+    s_last = atomicAdd(p.counters + b, 1) == p.nchunks - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  float k = -INFINITY;
+  int i = 0x7fffffff;
+  for (int c = threadIdx.x; c < p.nchunks; c += kSampThreads) {
+    const float k2 = __ldcg(p.part_key + static_cast<int64_t>(b) * p.nchunks + c);
+    const int i2 = __ldcg(p.part_idx + static_cast<int64_t>(b) * p.nchunks + c);
+    if (beats(k2, i2, k, i)) {
+      k = k2;
+      i = i2;
+    }
+  }
+  block_reduce(k, i);
+  if (threadIdx.x == 0) {
+    p.out[b] = i == 0x7fffffff ? 0 : i;
+    p.counters[b] = 0;
+  }
+}
+
+
+// Greedy rows streamed through shared memory: thread 0 keeps a ring of kNS
+// 16 KiB tiles filled with 1-D bulk async copies (the copy engine holds up to
+// kNS * 16 KiB in flight per CTA without tying up registers); all threads
+// reduce each tile from shared memory.
+constexpr int kTileVec = 1024;  // 16-byte vectors per tile (16 KiB)
+constexpr int kNS = 4;
+constexpr int kBulkSmem = kNS * kTileVec * 16;
+
+template <typename T>
+__global__ void __launch_bounds__(kSampThreads) argmax_bulk_kernel(const SampleParams p) {
+  extern __shared__ __align__(128) uint4 ring[];
+  __shared__ __align__(8) uint64_t full[kNS];
+  const int ch = blockIdx.x, b = blockIdx.y;
+  const int v0 = ch * p.chunk, v1 = min(p.V, v0 + p.chunk);
+  const T* row = static_cast<const T*>(p.logits) + static_cast<int64_t>(b) * p.ld;
+  const int vend = v0 + ((v1 - v0) / kVec) * kVec;
+  const int nvec = (vend - v0) / kVec;
+  const int tiles = (nvec + kTileVec - 1) / kTileVec;
+  auto issue = [&](int t, int s) {
+    const int nv = min(kTileVec, nvec - t * kTileVec);
+    const uint32_t bytes = static_cast<uint32_t>(nv) * 16u;
+    lk::mbar_arrive_expect_tx(&full[s], bytes);
+    lk::bulk_load(ring + s * kTileVec, row + v0 + static_cast<int64_t>(t) * kTileVec * kVec, bytes,
+                  &full[s]);
+  };
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < kNS; ++s) lk::mbar_init(&full[s], 1);
+    lk::fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int t = 0; t < kNS && t < tiles; ++t) issue(t, t);
+  float best = -INFINITY;
+  int besti = 0x7fffffff;
+  for (int t = 0; t < tiles; ++t) {
+    const int s = t % kNS;
+    if (!lk::mbar_wait(&full[s], (t / kNS) & 1)) break;  // bounded; never expected
+    const int nv = min(kTileVec, nvec - t * kTileVec);
+    const uint4* tile = ring + s * kTileVec;
+    const int vbase = v0 + t * kTileVec * kVec;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < nv; i += kSampThreads)
+      argmax_vec<T>(tile[i], vbase + i * kVec, best, besti);
+    __syncthreads();
+    if (threadIdx.x == 0 && t + kNS < tiles) {
+      lk::fence_proxy_async();
+      issue(t + kNS, s);
+    }
+  }
+  for (int t = vend + threadIdx.x; t < v1; t += kSampThreads) {
+    const float x = lk::Elem<T>::to_f(row[t]);
+    if (beats_later(x, best)) {
+      best = x;
+      besti = t;
+    }
+  }
+  block_reduce(best, besti);
+  if (p.nchunks == 1) {
+    if (threadIdx.x == 0) p.out[b] = besti == 0x7fffffff ? 0 : besti;
+    return;
+  }
+  __shared__ int s_last;
+  if (threadIdx.x == 0) {
+    p.part_key[static_cast<int64_t>(b) * p.nchunks + ch] = best;
+    p.part_idx[static_cast<int64_t>(b) * p.nchunks + ch] = besti;
+    __threadfence();
+    s_last = atomicAdd(p.counters + b, 1) == p.nchunks - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  float k = -INFINITY;
+  int i = 0x7fffffff;
+  for (int c = threadIdx.x; c < p.nchunks; c += kSampThreads) {
+    const float k2 = __ldcg(p.part_key + static_cast<int64_t>(b) * p.nchunks + c);
+    const int i2 = __ldcg(p.part_idx + static_cast<int64_t>(b) * p.nchunks + c);
+    if (beats(k2, i2, k, i)) {
+      k = k2;
+      i = i2;
+    }
+  }
+  block_reduce(k, i);
+  if (threadIdx.x == 0) {
+    p.out[b] = i == 0x7fffffff ? 0 : i;
+    p.counters[b] = 0;
+  }
+}
+
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 // Workspace layout: [counters: 65536 int32 — a fixed region, so that calls
@@ -343,20 +604,104 @@ size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 // [part_key: B*chunks f32][part_idx: B*chunks int32]
 constexpr size_t kCounterBytes = 65536 * 4;
 
+// Loads in flight per thread of the greedy kernel and the CTAs per SM that
+// its registers allow: 4 -> 6, 8 -> 4, 16 -> 2. LITEKERN_SAMPLE_UNROLL (read
+// once) selects one; the grid is sized for one full wave of it.
+int sample_unroll() {
+  static int u = [] {
+    const char* e = getenv("LITEKERN_SAMPLE_UNROLL");
+    const int v = e ? atoi(e) : 8;
+    return (v == 0 || v == 4 || v == 8 || v == 16) ? v : 8;
+  }();
+  return u;
+}
+int ctas_per_sm() {
+  switch (sample_unroll()) {
+    case 4: return 6;
+    case 8: return 4;
+    case 16: return 2;
+    default: return 3;  // bulk kernel: 64 KiB ring per CTA
+  }
+}
+
+int chunk_override() {
+  static int c = [] {
+    const char* e = getenv("LITEKERN_SAMPLE_CHUNKS");
+    return e ? atoi(e) : 0;
+  }();
+  return c;
+}
+
 int choose_chunks(int B, int V) {
-  // ~4 CTAs per SM over the whole batch, chunks of at least 4096 elements.
-  const int64_t target = 4LL * lk::num_sms();
-  int64_t n = (target + B - 1) / B;
-  const int64_t maxn = (V + 4095) / 4096;
+  if (chunk_override() > 0) return chunk_override();
+  // One full wave: kSampCtasPerSm CTAs per SM over the whole batch (rounded
+  // down so the grid never spills into a second wave), chunks of at least
+  // 2048 elements.
+  const int64_t target = static_cast<int64_t>(ctas_per_sm()) * lk::num_sms();
+  int64_t n = target / B;
+  const int64_t maxn = (V + 2047) / 2048;
   if (n > maxn) n = maxn;
   if (n < 1) n = 1;
   if (n > 1024) n = 1024;
   return static_cast<int>(n);
 }
 
+constexpr int kMaxCluster = 8;  // portable cluster size
+
+template <typename K>
+cudaError_t launch_cluster(K kernel, const cudaLaunchConfig_t& cfg, const SampleParams& p) {
+  return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
 template <typename T>
 int launch_sample(const SampleParams& p, int B, bool vec, cudaStream_t s) {
   dim3 grid(p.nchunks, B);
+  if constexpr (!std::is_same<T, float>::value) {
+    if (vec && p.temps == nullptr && sample_unroll() != 0) {
+      if (p.nchunks > 1 && p.nchunks <= kMaxCluster) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(kSampThreads);
+        cfg.dynamicSmemBytes = 0;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = p.nchunks;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e;
+        switch (sample_unroll()) {
+          case 4: e = launch_cluster(argmax_kernel<T, 4, 6, true>, cfg, p); break;
+          case 16: e = launch_cluster(argmax_kernel<T, 16, 2, true>, cfg, p); break;
+          default: e = launch_cluster(argmax_kernel<T, 8, 4, true>, cfg, p); break;
+        }
+        return e == cudaSuccess ? LK_OK : LK_ERR_CUDA;
+      }
+      switch (sample_unroll()) {
+        case 4: argmax_kernel<T, 4, 6, false><<<grid, kSampThreads, 0, s>>>(p); break;
+        case 16: argmax_kernel<T, 16, 2, false><<<grid, kSampThreads, 0, s>>>(p); break;
+        default: argmax_kernel<T, 8, 4, false><<<grid, kSampThreads, 0, s>>>(p); break;
+      }
+      return lk::check_launch();
+    }
+  }
+  if constexpr (!std::is_same<T, float>::value) {
+    if (vec && p.temps == nullptr) {
+      static int configured[64] = {0};
+      int dev = 0;
+      cudaGetDevice(&dev);
+      if (dev >= 0 && dev < 64 && !configured[dev]) {
+        if (cudaFuncSetAttribute(argmax_bulk_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kBulkSmem) != cudaSuccess)
+          return LK_ERR_CUDA;
+        configured[dev] = 1;
+      }
+      argmax_bulk_kernel<T><<<grid, kSampThreads, kBulkSmem, s>>>(p);
+      return lk::check_launch();
+    }
+  }
   if (vec) sample_kernel<T, true><<<grid, kSampThreads, 0, s>>>(p);
   else sample_kernel<T, false><<<grid, kSampThreads, 0, s>>>(p);
   return lk::check_launch();
@@ -385,6 +730,11 @@ extern "C" int lk_sample(int64_t* out_ids, const void* logits, int32_t B, int32_
   p.ld = ld;
   p.V = V;
   p.nchunks = choose_chunks(B, V);
+  // All-greedy 16-bit rows reduce their chunks inside one cluster: at most
+  // kMaxCluster chunks per row.
+  if (temperatures == nullptr && dtype != LK_DTYPE_F32 && sample_unroll() != 0 &&
+      chunk_override() == 0 && p.nchunks > kMaxCluster)
+    p.nchunks = kMaxCluster;
   const int64_t per = (static_cast<int64_t>(V) + p.nchunks - 1) / p.nchunks;
   p.chunk = static_cast<int>(((per + kVec - 1) / kVec) * kVec);
   p.nchunks = static_cast<int>((V + static_cast<int64_t>(p.chunk) - 1) / p.chunk);
@@ -501,6 +851,11 @@ extern "C" int lk_sample_noalloc(int64_t* out_ids, const void* logits, int32_t B
   p.ld = ld;
   p.V = V;
   p.nchunks = choose_chunks(B, V);
+  // All-greedy 16-bit rows reduce their chunks inside one cluster: at most
+  // kMaxCluster chunks per row.
+  if (temperatures == nullptr && dtype != LK_DTYPE_F32 && sample_unroll() != 0 &&
+      chunk_override() == 0 && p.nchunks > kMaxCluster)
+    p.nchunks = kMaxCluster;
   const int64_t per = (static_cast<int64_t>(V) + p.nchunks - 1) / p.nchunks;
   p.chunk = static_cast<int>(((per + kVec - 1) / kVec) * kVec);
   p.nchunks = static_cast<int>((V + static_cast<int64_t>(p.chunk) - 1) / p.chunk);

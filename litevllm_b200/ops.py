@@ -7,6 +7,7 @@ computes on the host: a CPU tensor or a missing library raises.
 
 from __future__ import annotations
 
+import contextlib
 import math
 from typing import Optional
 
@@ -44,6 +45,14 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 
 def _stream(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
+
+
+_NULL = contextlib.nullcontext()
+
+
+def _on(dev: torch.device):
+    """Make dev current for the call (a no-op when it already is)."""
+    return _NULL if dev.index == torch.cuda.current_device() else torch.cuda.device(dev)
 
 
 class _Workspaces:
@@ -103,7 +112,7 @@ def store_kvcache(
     slot_mapping = slot_mapping.contiguous()
     code = _dtype_code(key_cache, (torch.float32, torch.float16, torch.bfloat16))
     num_slots = key_cache.shape[0] * key_cache.shape[1]
-    with torch.cuda.device(dev):
+    with _on(dev):
         check(
             lib().lk_store_kv(
                 key.data_ptr(), value.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
@@ -163,14 +172,15 @@ def paged_decode(
     if B == 0:
         return out
     max_blocks = block_tables.shape[1]
-    if num_splits <= 0:
+    num_splits = int(num_splits)
+    if num_splits == 0:  # auto split count; -1 selects the persistent kernel
         num_splits = decode_num_splits(B, H_kv, max_blocks, bs)
     need = decode_workspace_bytes(B, H, H_kv, D, num_splits)
     if workspace is None:
         workspace = WORKSPACES.get(dev, "decode", need)
     elif workspace.numel() * workspace.element_size() < need:
         raise ValueError(f"workspace too small: need {need} bytes")
-    with torch.cuda.device(dev):
+    with _on(dev):
         check(
             lib().lk_paged_decode(
                 out.data_ptr(), out.stride(0), query.data_ptr(), query.stride(0),
@@ -256,7 +266,7 @@ def paged_prefill(
         raise ValueError("bad out tensor")
     if S <= 0 or T == 0:
         return out
-    with torch.cuda.device(dev):
+    with _on(dev):
         check(
             lib().lk_paged_prefill(
                 out.data_ptr(), query.data_ptr(), query.stride(0), key_cache.data_ptr(),
@@ -311,7 +321,7 @@ def sample(
     need = int(lib().lk_sample_workspace_bytes(B, V))
     if workspace is None:
         workspace = WORKSPACES.get(dev, "sample", need)
-    with torch.cuda.device(dev):
+    with _on(dev):
         check(
             lib().lk_sample(
                 out.data_ptr(), logits.data_ptr(), B, V, logits.stride(0), _ptr(temperatures),
@@ -333,7 +343,7 @@ def softmax_temp(logits: torch.Tensor, temperatures: torch.Tensor) -> torch.Tens
     code = _dtype_code(logits, (torch.float32, torch.float16, torch.bfloat16))
     temperatures = temperatures.to(torch.float32).contiguous()
     probs = torch.empty((B, V), dtype=torch.float32, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         check(
             lib().lk_softmax_temp(
                 probs.data_ptr(), V, logits.data_ptr(), B, V, V, temperatures.data_ptr(), code,

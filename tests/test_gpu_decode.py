@@ -51,7 +51,7 @@ def test_decode_gqa_ratios_and_head_groups(cuda, H, H_kv):
     _check(b)
 
 
-@pytest.mark.parametrize("num_splits", [1, 2, 3, 7, 64])
+@pytest.mark.parametrize("num_splits", [-1, 1, 2, 3, 7, 64])
 def test_decode_split_kv_consistent(cuda, num_splits):
     b = workloads.make_decode_batch(2, 5, seed=11, device=cuda, ctx=[4096, 1, 2000, 17, 1023])
     _check(b, num_splits=num_splits)
@@ -122,9 +122,9 @@ def test_decode_out_of_range_block_flags_status(cuda):
     b = workloads.make_decode_batch(2, 2, seed=17, device=cuda, ctx=[40, 40])
     nb = b.key_cache.shape[0]
     b.block_tables[1, 1] = nb + 5
-    ws = torch.zeros(1 << 20, dtype=torch.uint8, device=cuda)
+    ws = torch.zeros(ops.decode_workspace_bytes(2, 32, 8, 128, -1), dtype=torch.uint8, device=cuda)
     ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables, b.context_lens, b.scale,
-                     workspace=ws)
+                     workspace=ws, num_splits=-1)
     assert ops.decode_status(ws) & 2
 
 
@@ -132,3 +132,27 @@ def test_decode_workspace_reused_across_batch_shapes(cuda):
     for B, splits in [(3, 5), (40, 7), (5, 64), (40, 7)]:
         b = workloads.make_decode_batch(2, B, seed=B, device=cuda)
         _check(b, num_splits=splits)
+
+
+def test_persistent_many_tiny_sequences(cuda):
+    """Hundreds of 1-40 token sequences: many units per CTA, ranges cutting units."""
+    ctx = [1 + (i * 7) % 40 for i in range(1000)]
+    b = workloads.make_decode_batch(2, len(ctx), seed=21, device=cuda, ctx=ctx)
+    _check(b, num_splits=-1)
+    _check(b)
+
+
+def test_persistent_single_long_sequence_spans_all_ctas(cuda):
+    """One 100K-token sequence is cut across every SM; the last CTA merges all."""
+    b = workloads.make_decode_batch(5, 1, seed=22, device=cuda, ctx=[100_003])
+    _check(b, num_splits=-1)
+    _check(b)
+
+
+def test_persistent_matches_split_kernel(cuda):
+    b = workloads.make_decode_batch(2, 64, seed=23, device=cuda)
+    a = ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables, b.context_lens,
+                         b.scale, num_splits=-1)
+    s = ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables, b.context_lens,
+                         b.scale, num_splits=3)
+    assert_attn_close(a, s.float(), max_abs=8e-3, mean_rel=2e-3)
