@@ -22,6 +22,10 @@
 #include "lk_common.cuh"
 #include "lk_host.h"
 
+#include <stdlib.h>
+
+#include <type_traits>
+
 namespace {
 
 constexpr int kD = 128;
@@ -297,6 +301,340 @@ int launch_prefill(const CUtensorMap& km, const CUtensorMap& vm, const PrefillPa
   return lk::check_launch();
 }
 
+
+// ---------------------------------------------------------------------------
+// tcgen05 (fifth-generation tensor core) version.
+//
+// CTA = 128 query rows (128 / G positions x the G heads of one KV head).
+// Warps 0-3: softmax and epilogue, thread r owns row r (= TMEM lane r).
+// Warp 4: TMA producer (64-token K and V tiles, two-stage ring).
+// Warp 5: MMA issuer. S = Q K^T (M=128, N=64 keys, K=D) into TMEM columns
+// [0,64); the softmax writes P (bf16/f16, two per 32-bit column) into TMEM
+// columns [64,96); O += P V (A = P from TMEM, B = V from shared memory,
+// MN-major, N = D) accumulates in columns [128,256). Shared memory is
+// 97 KB, so two CTAs share an SM and one CTA's softmax overlaps the other's
+// MMAs. The running max is applied lazily: O is rescaled only when a row's
+// max grows by more than 2^8.
+constexpr int kTcThreads = 192;
+constexpr int kTcKT = 64;                 // keys per tile
+constexpr int kTcQHalf = 128 * 128;       // Q: 128 rows x 128 B (64 values of D)
+constexpr int kTcKHalf = kTcKT * 128;     // K or V: 64 rows x 128 B
+constexpr int kTcStage = 4 * kTcKHalf;    // K (two halves) + V (two halves) = 32 KB
+constexpr int kTcSmem = 2 * kTcQHalf + 2 * kTcStage + 1024;
+constexpr float kLazyRescale = 8.f;       // log2 units
+
+template <typename T>
+__global__ void __launch_bounds__(kTcThreads, 2)
+paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
+                        const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t k_full[2];
+  __shared__ __align__(8) uint64_t k_empty[2];
+  __shared__ __align__(8) uint64_t v_full[2];
+  __shared__ __align__(8) uint64_t v_empty[2];
+  __shared__ __align__(8) uint64_t s_full[2];
+  __shared__ __align__(8) uint64_t p_full[2];
+  __shared__ __align__(8) uint64_t o_done;
+  __shared__ __align__(8) uint64_t o_final;
+  __shared__ uint32_t tmem_slot;
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = smem + 2 * kTcQHalf;
+
+  const int qt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.G, BQ = p.BQ;
+  const int q_start = p.cu_seqlens_q[b];
+  const int q_len = p.cu_seqlens_q[b + 1] - q_start;
+  const int pos0 = qt * BQ;
+  if (pos0 >= q_len) return;
+  int prior = 0;
+  if (p.block_tables != nullptr && p.context_lens != nullptr) {
+    prior = p.context_lens[b] - q_len;
+    if (prior < 0) {
+      if (threadIdx.x == 0 && p.status) atomicOr(p.status, LK_STATUS_CTX_OOB);
+      prior = 0;
+    }
+  }
+  const int kv_end = prior + min(q_len, pos0 + BQ);
+  const int ntiles = (kv_end + kTcKT - 1) / kTcKT;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      lk::mbar_init(&k_full[i], 1);
+      lk::mbar_init(&k_empty[i], 1);
+      lk::mbar_init(&v_full[i], 1);
+      lk::mbar_init(&v_empty[i], 1);
+    }
+    lk::mbar_init(&s_full[0], 1);
+    lk::mbar_init(&s_full[1], 1);
+    lk::mbar_init(&p_full[0], 4);
+    lk::mbar_init(&p_full[1], 4);
+    lk::mbar_init(&o_done, 1);
+    lk::mbar_init(&o_final, 1);
+    lk::fence_barrier_init();
+  }
+  if (warp == 5) lk::tc::alloc(&tmem_slot, 256);
+  if (warp < 4) {
+    // Q tile -> shared memory, K-major with 128-byte swizzle.
+    const int r = threadIdx.x;
+    const int pos = pos0 + r / G, g = r % G;
+    const T* qrow = static_cast<const T*>(p.q) + static_cast<int64_t>(q_start + pos) * p.q_stride +
+                    static_cast<int64_t>(kvh * G + g) * kD;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (pos < q_len) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
+      *reinterpret_cast<uint4*>(sQ + (c >> 3) * kTcQHalf + lk::swz128(r, c & 7)) = v;
+    }
+    lk::fence_proxy_async();
+  }
+  lk::tc::fence_before();
+  __syncthreads();
+  lk::tc::fence_after();
+  const uint32_t tmem = tmem_slot;
+  // S double buffer: tile j uses columns [64 * (j & 1), +64); its P is written
+  // over the first 32 columns of the same buffer. O in columns [128, 256).
+  const uint32_t tO = tmem + 128;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      lk::prefetch_tensormap(&kmap);
+      lk::prefetch_tensormap(&vmap);
+      const int32_t* bt =
+          p.block_tables ? p.block_tables + static_cast<int64_t>(b) * p.bt_stride : nullptr;
+      const int oob = static_cast<int>(p.num_slots < 0x7fffffffLL ? p.num_slots : 0x7fffffffLL);
+      // K and V rings are separate: a K stage frees when its S MMA completes,
+      // long before the V stage of the same tile.
+      auto slot_of = [&](int tok) -> int {
+        if (tok >= kv_end) return oob;
+        if (!bt) return q_start + tok;
+        const int blk = bt[tok / p.bs];
+        if (blk < 0 || blk >= p.num_blocks) {
+          if (p.status) atomicOr(p.status, LK_STATUS_BLOCK_OOB);
+          return oob;
+        }
+        return blk * p.bs + tok % p.bs;
+      };
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = ((j >> 1) & 1) ^ 1;
+        int slots[kTcKT / 16];
+#pragma unroll
+        for (int tb = 0; tb < kTcKT / 16; ++tb) slots[tb] = slot_of(j * kTcKT + tb * 16);
+        if (!lk::mbar_wait(&k_empty[st], ph)) {
+          if (p.status) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
+          break;
+        }
+        lk::mbar_arrive_expect_tx(&k_full[st], 2 * kTcKHalf);
+        uint8_t* dk = sKV + st * kTcStage;
+#pragma unroll
+        for (int tb = 0; tb < kTcKT / 16; ++tb)
+#pragma unroll
+          for (int dh = 0; dh < 2; ++dh)
+            lk::tma_load_3d(dk + dh * kTcKHalf + tb * 2048, &kmap, &k_full[st], dh * 64, slots[tb],
+                            kvh);
+        if (!lk::mbar_wait(&v_empty[st], ph)) {
+          if (p.status) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
+          break;
+        }
+        lk::mbar_arrive_expect_tx(&v_full[st], 2 * kTcKHalf);
+#pragma unroll
+        for (int tb = 0; tb < kTcKT / 16; ++tb)
+#pragma unroll
+          for (int dh = 0; dh < 2; ++dh)
+            lk::tma_load_3d(dk + 2 * kTcKHalf + dh * kTcKHalf + tb * 2048, &vmap, &v_full[st],
+                            dh * 64, slots[tb], kvh);
+      }
+    }
+  } else if (warp == 5) {
+    // ----------------------------------------------------------- MMA issue
+    // Issue order: S(0), S(1), PV(0), S(2), PV(1), ... so that S(j+1) runs on
+    // the tensor core while the softmax of tile j runs on the SM.
+    if (lane == 0) {
+      constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+      constexpr uint32_t idS = lk::tc::idesc_f16(fmt, 0, 0, 128, kTcKT);
+      constexpr uint32_t idO = lk::tc::idesc_f16(fmt, 0, 1, 128, 128);
+      const uint32_t q_addr = lk::smem_u32(sQ);
+      bool ok = true;
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!lk::mbar_wait(&k_full[st], (j >> 1) & 1)) return false;
+        lk::tc::fence_after();
+        const uint32_t k_addr = lk::smem_u32(sKV + st * kTcStage);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          lk::tc::mma_f16(
+              tmem + 64 * st,
+              lk::tc::smem_desc_sw128(q_addr + (ks >> 2) * kTcQHalf + (ks & 3) * 32, 16, 1024),
+              lk::tc::smem_desc_sw128(k_addr + (ks >> 2) * kTcKHalf + (ks & 3) * 32, 16, 1024),
+              idS, ks > 0 ? 1u : 0u);
+        }
+        lk::tc::commit(&s_full[st]);
+        lk::tc::commit(&k_empty[st]);
+        return true;
+      };
+      ok = issue_s(0);
+      for (int j = 0; j < ntiles && ok; ++j) {
+        const int st = j & 1;
+        if (j + 1 < ntiles && !issue_s(j + 1)) {
+          ok = false;
+          break;
+        }
+        if (!lk::mbar_wait(&p_full[st], (j >> 1) & 1) ||
+            !lk::mbar_wait(&v_full[st], (j >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        lk::tc::fence_after();
+        const uint32_t v_addr = lk::smem_u32(sKV + st * kTcStage) + 2 * kTcKHalf;
+#pragma unroll
+        for (int kk = 0; kk < kTcKT / 16; ++kk) {
+          const uint64_t bd = lk::tc::smem_desc_sw128(v_addr + kk * 2048, kTcKHalf, 1024);
+          lk::tc::mma_f16_ts(tO, tmem + 64 * st + kk * 8, bd, idO, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        lk::tc::commit(&v_empty[st]);
+        lk::tc::commit(&o_done);
+      }
+      if (!ok && p.status) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
+      lk::tc::commit(&o_final);
+    }
+  } else {
+    // ------------------------------------------------- softmax / epilogue
+    const int r = threadIdx.x;
+    const int pos = pos0 + r / G, g = r % G;
+    const int limit = prior + pos;  // last visible key of this row
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const float sl2 = p.scale_log2;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j & 1;
+      const uint32_t tS = tmem + 64 * st;
+      if (!lk::mbar_wait(&s_full[st], (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      lk::tc::fence_after();
+      uint32_t sv[2][32];
+      lk::tc::ld32(tS + lane_base, sv[0]);
+      lk::tc::ld32(tS + lane_base + 32, sv[1]);
+      lk::tc::wait_ld();
+      const int kb = j * kTcKT;
+      const bool need_mask = kb + kTcKT - 1 > limit;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float x = __uint_as_float(sv[h][i]) * sl2;
+          if (need_mask && kb + h * 32 + i > limit) x = -INFINITY;
+          sv[h][i] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+      }
+      float new_m = m_used;
+      if (mx > m_used + kLazyRescale) new_m = mx;
+      const float alpha = (new_m == m_used) ? 1.f : exp2f(m_used - new_m);
+      const float ms = new_m == -INFINITY ? 0.f : new_m;
+      float sum = 0.f;
+      uint32_t pw[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const float e0 = exp2f(__uint_as_float(sv[c >> 4][(2 * c) & 31]) - ms);
+        const float e1 = exp2f(__uint_as_float(sv[c >> 4][(2 * c + 1) & 31]) - ms);
+        sum += e0 + e1;
+        pw[c] = lk::pack2<T>(e0, e1);
+      }
+      lk::tc::st32(tS + lane_base, pw);  // P over the S buffer it came from
+      l = l * alpha + sum;
+      // O may only be touched once PV(j-1) has completed; o_done completes
+      // once per tile, so every tile waits for its predecessor's phase.
+      if (j > 0 && !lk::mbar_wait(&o_done, (j - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      lk::tc::fence_after();
+      // tcgen05.ld / st are warp-collective: the warp rescales together if
+      // any of its rows needs it (alpha is 1 for the others).
+      if (j > 0 && __any_sync(0xffffffffu, new_m != m_used)) {
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t ov[32];
+          lk::tc::ld32(tO + lane_base + c4 * 32, ov);
+          lk::tc::wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+          lk::tc::st32(tO + lane_base + c4 * 32, ov);
+        }
+      }
+      lk::tc::wait_st();
+      m_used = new_m;
+      lk::tc::fence_before();
+      __syncwarp();
+      if (lane == 0) lk::mbar_arrive(&p_full[st]);
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok && lk::mbar_wait(&o_final, 0)) {
+      lk::tc::fence_after();
+      const float inv = 1.f / l;
+      T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(q_start + pos) * p.H * kD +
+                static_cast<int64_t>(kvh * G + g) * kD;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t ov[32];
+        lk::tc::ld32(tO + lane_base + c4 * 32, ov);  // whole warp, every row
+        lk::tc::wait_ld();
+        if (pos < q_len) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              w[e] = lk::pack2<T>(__uint_as_float(ov[c * 8 + 2 * e]) * inv,
+                                  __uint_as_float(ov[c * 8 + 2 * e + 1]) * inv);
+            *reinterpret_cast<uint4*>(orow + c4 * 32 + c * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+    } else if (p.status && lane == 0) {
+      atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
+    }
+  }
+  lk::tc::fence_before();
+  __syncthreads();
+  lk::tc::fence_after();
+  if (warp == 5) lk::tc::dealloc(tmem, 256);
+}
+
+template <typename T>
+int launch_prefill_tc(const CUtensorMap& km, const CUtensorMap& vm, const PrefillParams& p,
+                      int num_seqs, int max_q_len, int H_kv, cudaStream_t s) {
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(paged_prefill_tc_kernel<T>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) != cudaSuccess)
+      return LK_ERR_CUDA;
+    configured[dev] = 1;
+  }
+  dim3 grid((max_q_len + p.BQ - 1) / p.BQ, H_kv, num_seqs);
+  paged_prefill_tc_kernel<T><<<grid, kTcThreads, kTcSmem, s>>>(km, vm, p);
+  return lk::check_launch();
+}
+
+// mma.sync kernel instead of tcgen05 (LITEKERN_PREFILL_MMA_SYNC=1, read once).
+bool use_mma_sync() {
+  static int v = [] {
+    const char* e = getenv("LITEKERN_PREFILL_MMA_SYNC");
+    return (e && atoi(e) != 0) ? 1 : 0;
+  }();
+  return v != 0;
+}
+
 }  // namespace
 
 extern "C" int lk_paged_prefill(void* out, const void* q, int64_t q_token_stride,
@@ -349,6 +687,11 @@ extern "C" int lk_paged_prefill(void* out, const void* q, int64_t q_token_stride
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = status;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!use_mma_sync()) {
+    if (dtype == LK_DTYPE_BF16)
+      return launch_prefill_tc<__nv_bfloat16>(km, vm, p, num_seqs, max_q_len, H_kv, s);
+    return launch_prefill_tc<__half>(km, vm, p, num_seqs, max_q_len, H_kv, s);
+  }
   if (dtype == LK_DTYPE_BF16)
     return launch_prefill<__nv_bfloat16>(km, vm, p, num_seqs, max_q_len, H_kv, s);
   return launch_prefill<__half>(km, vm, p, num_seqs, max_q_len, H_kv, s);
