@@ -193,6 +193,47 @@ LK_DEVINL uint32_t swz128(uint32_t row, uint32_t chunk) {
   return row * 128u + ((chunk ^ (row & 7u)) << 4);
 }
 
+// 2^x on the special-function unit (single MUFU instruction, flush to zero).
+LK_DEVINL float ex2_mufu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 2^x on the FMA / ALU pipes: x = n + f with n = round(x), f in [-1/2, 1/2];
+// 2^f by a cubic least-squares fit on Chebyshev nodes (coefficients fitted
+// for this library; max relative error 2.5e-4, below the rounding of the
+// 16-bit attention probabilities it feeds); 2^n added to the exponent.
+// Returns 0 for x < -126 (masked scores are -inf).
+LK_DEVINL float exp2_fma(float x) {
+  const float xc = fmaxf(x, -126.f);
+  const float y = xc + 12582912.f;  // 1.5 * 2^23: integer part lands in the low bits
+  const int n = __float_as_int(y) - 0x4B400000;
+  const float f = xc - (y - 12582912.f);
+  const float pf = fmaf(fmaf(fmaf(0.05746771767735481f, f, 0.24254462122917175f), f,
+                             0.6928921341896057f),
+                        f, 0.9999291300773621f);
+  const float r = __int_as_float(__float_as_int(pf) + (n << 23));
+  return x < -126.f ? 0.f : r;
+}
+
+// Packed fp32x2 arithmetic (sm_100): two lanes per instruction.
+LK_DEVINL void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                     float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+LK_DEVINL void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 LK_DEVINL float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

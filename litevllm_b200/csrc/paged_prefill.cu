@@ -524,30 +524,35 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
       lk::tc::wait_ld();
       const int kb = j * kTcKT;
       const bool need_mask = kb + kTcKT - 1 > limit;
-      float mx = -INFINITY;
+      float mraw = -INFINITY;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          float x = __uint_as_float(sv[h][i]) * sl2;
-          if (need_mask && kb + h * 32 + i > limit) x = -INFINITY;
-          sv[h][i] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
+          if (need_mask && kb + h * 32 + i > limit) sv[h][i] = __float_as_uint(-INFINITY);
+          mraw = fmaxf(mraw, __uint_as_float(sv[h][i]));
         }
       }
+      const float mx = mraw * sl2;  // sl2 > 0: max commutes with the scaling
       float new_m = m_used;
       if (mx > m_used + kLazyRescale) new_m = mx;
       const float alpha = (new_m == m_used) ? 1.f : exp2f(m_used - new_m);
       const float ms = new_m == -INFINITY ? 0.f : new_m;
-      float sum = 0.f;
+      // Two scores per instruction for the scale-and-shift and the row sum
+      // (packed fp32x2), one MUFU ex2 per score.
+      float sum0 = 0.f, sum1 = 0.f;
       uint32_t pw[32];
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
-        const float e0 = exp2f(__uint_as_float(sv[c >> 4][(2 * c) & 31]) - ms);
-        const float e1 = exp2f(__uint_as_float(sv[c >> 4][(2 * c + 1) & 31]) - ms);
-        sum += e0 + e1;
+        float x0, x1;
+        lk::ffma2(x0, x1, __uint_as_float(sv[c >> 4][(2 * c) & 31]),
+                  __uint_as_float(sv[c >> 4][(2 * c + 1) & 31]), sl2, sl2, -ms, -ms);
+        const float e0 = lk::ex2_mufu(x0);
+        const float e1 = lk::ex2_mufu(x1);
+        lk::fadd2(sum0, sum1, sum0, sum1, e0, e1);
         pw[c] = lk::pack2<T>(e0, e1);
       }
+      const float sum = sum0 + sum1;
       lk::tc::st32(tS + lane_base, pw);  // P over the S buffer it came from
       l = l * alpha + sum;
       // O may only be touched once PV(j-1) has completed; o_done completes
