@@ -234,6 +234,13 @@ LK_DEVINL void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
+// Three-input fp32 max (sm_100).
+LK_DEVINL float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 LK_DEVINL float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -524,15 +524,21 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
       lk::tc::wait_ld();
       const int kb = j * kTcKT;
       const bool need_mask = kb + kTcKT - 1 > limit;
-      float mraw = -INFINITY;
+      if (need_mask) {
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (need_mask && kb + h * 32 + i > limit) sv[h][i] = __float_as_uint(-INFINITY);
-          mraw = fmaxf(mraw, __uint_as_float(sv[h][i]));
-        }
+          for (int i = 0; i < 32; ++i)
+            if (kb + h * 32 + i > limit) sv[h][i] = __float_as_uint(-INFINITY);
       }
+      // two independent chains of three-input max
+      float ma = -INFINITY, mb = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        ma = lk::fmax3(ma, __uint_as_float(sv[0][i]), __uint_as_float(sv[0][i + 1]));
+        mb = lk::fmax3(mb, __uint_as_float(sv[1][i]), __uint_as_float(sv[1][i + 1]));
+      }
+      const float mraw = fmaxf(ma, mb);
       const float mx = mraw * sl2;  // sl2 > 0: max commutes with the scaling
       float new_m = m_used;
       if (mx > m_used + kLazyRescale) new_m = mx;
