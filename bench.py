@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--num-splits", type=int, default=0, help="decode split-KV override (0=auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg5"],
+                    help="cfg2 (default) is the contract's workload; cfg3 / cfg5 print a "
+                         "secondary line for the mixed prefill step / long-context decode")
     return ap.parse_args()
 
 
@@ -365,6 +368,138 @@ def run_reference(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
+def measured_tflops():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except Exception:
+            pass
+    return 1590.0, "fallback"
+
+
+def _time_events(stream, fn, K, warmup):
+    for _ in range(warmup):
+        fn(None)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    evs = []
+    t0.record(stream)
+    for _ in range(K):
+        evs.append(fn(stream))
+    t1.record(stream)
+    torch.cuda.synchronize()
+    return t0.elapsed_time(t1) / K, evs
+
+
+def run_secondary(args, ws, rank, local):
+    """Config 3 (mixed chunked-prefill + decode step) or config 5 (long-context
+    decode + T=1.0 sampler), device-timed per kernel. One JSON line on rank 0."""
+    from litevllm_b200 import ops, workloads
+    from litevllm_b200.sharding import shard
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    peak_hbm, _ = measured_peak()
+    peak_tf, tf_kind = measured_tflops()
+    Ev = lambda: torch.cuda.Event(enable_timing=True)
+    if args.workload == "cfg5":
+        mine = shard(64, ws, rank)
+        B = len(mine)
+        b = workloads.make_decode_batch(5, B, seed=0, first_seq=mine.start, device=dev)
+        V5 = 151936
+        logits = workloads.make_logits(5, B, V5, seed=0, first_seq=mine.start, device=dev)
+        temps = workloads.temperatures_for(5, B, device=dev)
+        ids = torch.empty(B, dtype=torch.int64, device=dev)
+        out = torch.empty_like(b.query)
+        nsplit = ops.decode_num_splits(B, H_KV, b.block_tables.shape[1], BS)
+
+        def step(st, i=[0]):
+            i[0] += 1
+            e = (Ev(), Ev()) if st is not None else None
+            ops.store_kvcache(b.key, b.value, b.key_cache, b.value_cache, b.slot_mapping)
+            if e: e[0].record(st)
+            ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables, b.context_lens,
+                             b.scale, num_splits=nsplit, out=out)
+            if e: e[1].record(st)
+            ops.sample(logits, temps, seed=7, offset=i[0], out=ids)
+            return e
+
+        ms, evs = _time_events(stream, step, args.steps, max(3, args.warmup))
+        dec_ms = sum(a.elapsed_time(c) for a, c in evs) / len(evs)
+        t = torch.tensor([ms, dec_ms], device=dev)
+        if ws > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, dec_ms = float(t[0]), float(t[1])
+        dec_b = decode_bytes(b.ctx, B)
+        step_b = dec_b + store_bytes(B) + B * V5 * 2
+        line = {"workload": "cfg5", "metric": METRIC, "n_gpus": ws, "steps": args.steps,
+                "config": {"workload": "config 5: bf16 long-context decode, 64 sequences in total "
+                           f"({B} per GPU), context U[32768,131072], 32 Q / 8 KV heads, D=128, "
+                           "block 16, split-KV, + T=1.0 Gumbel-max sampler (in-kernel Philox) "
+                           "over 151936", "parallelism": f"request-sharded x{ws}"},
+                "value": round(step_b * ws / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "ms_per_step": round(ms, 4), "sampled_tok_s": round(B * ws / (ms * 1e-3), 1),
+                "decode_split_kv": nsplit,
+                "roofline": {"kernel": "paged_decode_kernel", "bound": "hbm",
+                             "achieved": round(dec_b / (dec_ms * 1e-3) / 1e9, 1), "peak": peak_hbm,
+                             "unit": "GB/s",
+                             "frac": round(dec_b / (dec_ms * 1e-3) / 1e9 / peak_hbm, 4)}}
+    else:
+        # config 3: 4 chunks of 512 on prior U[0,3584] + 252 decode sequences,
+        # 2300 new tokens stored through slot_mapping, pool of 65536 blocks.
+        prior = [workloads.prefill_prior(0, i) for i in range(4)]
+        pf = workloads.make_prefill_batch([512] * 4, prior, seed=0, device=dev)
+        npf = pf.key_cache.shape[0]
+        dec = workloads.make_decode_batch(3, 252, seed=0, device=dev, pool_blocks=65536 - npf)
+        pout = torch.empty_like(pf.query)
+        dout = torch.empty_like(dec.query)
+        nsplit = ops.decode_num_splits(252, H_KV, dec.block_tables.shape[1], BS)
+
+        def step(st):
+            e = (Ev(), Ev(), Ev()) if st is not None else None
+            ops.store_kvcache(pf.key, pf.value, pf.key_cache, pf.value_cache, pf.slot_mapping)
+            ops.store_kvcache(dec.key, dec.value, dec.key_cache, dec.value_cache, dec.slot_mapping)
+            if e: e[0].record(st)
+            ops.paged_prefill(pf.query, pf.key_cache, pf.value_cache, pf.cu_seqlens_q, 512,
+                              pf.scale, block_tables=pf.block_tables, context_lens=pf.context_lens,
+                              out=pout)
+            if e: e[1].record(st)
+            ops.paged_decode(dec.query, dec.key_cache, dec.value_cache, dec.block_tables,
+                             dec.context_lens, dec.scale, num_splits=nsplit, out=dout)
+            if e: e[2].record(st)
+            return e
+
+        ms, evs = _time_events(stream, step, args.steps, max(3, args.warmup))
+        pre_ms = sum(a.elapsed_time(c) for a, c, _ in evs) / len(evs)
+        dec_ms = sum(c.elapsed_time(d) for _, c, d in evs) / len(evs)
+        t = torch.tensor([ms, pre_ms, dec_ms], device=dev)
+        if ws > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, pre_ms, dec_ms = (float(x) for x in t)
+        flops = sum(4 * H * D * 512 * (p_ + (512 + 1) / 2) for p_ in prior)
+        dec_b = decode_bytes(dec.ctx, 252)
+        tf = flops / (pre_ms * 1e-3) / 1e12
+        line = {"workload": "cfg3", "metric": METRIC, "n_gpus": ws, "steps": args.steps,
+                "config": {"workload": "config 3: bf16 mixed step, Qwen3-8B attention (32 Q / 8 KV "
+                           "heads, D=128): 4 prefill chunks of 512 on prior context "
+                           f"{prior} + 252 decode sequences (context U[64,2048]); 2300 new "
+                           "tokens stored; 65536-block pool", "parallelism": f"replica x{ws}"},
+                "ms_per_step": round(ms, 4), "unit": "TFLOP/s",
+                "value": round(tf, 1),
+                "prefill": {"ms": round(pre_ms, 4), "tflops": round(tf, 1),
+                            "roofline": {"kernel": "paged_prefill_tc_kernel", "bound": "tensor",
+                                         "achieved": round(tf, 1), "peak": peak_tf,
+                                         "peak_source": f"{tf_kind} bf16 burst", "unit": "TFLOP/s",
+                                         "frac": round(tf / peak_tf, 4)}},
+                "decode": {"ms": round(dec_ms, 4),
+                           "gbs": round(dec_b / (dec_ms * 1e-3) / 1e9, 1),
+                           "frac_of_hbm_peak": round(dec_b / (dec_ms * 1e-3) / 1e9 / peak_hbm, 4)}}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     ws, rank, local = dist_env()
@@ -374,6 +509,12 @@ def main():
     if ws > 1:
         torch.cuda.set_device(local)
         torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local))
+    if args.workload != "cfg2":
+        run_secondary(args, ws, rank, local)
+        if ws > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        return
     r = run_ours(args, ws, rank, local)
     N = ws
     ms = r["ms"]
