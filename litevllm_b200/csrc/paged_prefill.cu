@@ -315,28 +315,31 @@ int launch_prefill(const CUtensorMap& km, const CUtensorMap& vm, const PrefillPa
 // 97 KB, so two CTAs share an SM and one CTA's softmax overlaps the other's
 // MMAs. The running max is applied lazily: O is rescaled only when a row's
 // max grows by more than 2^8.
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 320;  // 8 softmax warps, 1 TMA warp, 1 MMA warp
+constexpr int kTcProducer = 8, kTcMma = 9;
 constexpr int kTcKT = 64;                 // keys per tile
 constexpr int kTcQHalf = 128 * 128;       // Q: 128 rows x 128 B (64 values of D)
 constexpr int kTcKHalf = kTcKT * 128;     // K or V: 64 rows x 128 B
 constexpr int kTcStage = 4 * kTcKHalf;    // K (two halves) + V (two halves) = 32 KB
-constexpr int kTcSmem = 2 * kTcQHalf + 2 * kTcStage + 1024;
+template <int NKV> constexpr int tc_smem() { return 2 * kTcQHalf + NKV * kTcStage + 1024; }
 constexpr float kLazyRescale = 8.f;       // log2 units
 
-template <typename T>
-__global__ void __launch_bounds__(kTcThreads, 2)
+template <typename T, int NKV>
+__global__ void __launch_bounds__(kTcThreads, NKV == 2 ? 2 : 1)
 paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t k_full[2];
-  __shared__ __align__(8) uint64_t k_empty[2];
-  __shared__ __align__(8) uint64_t v_full[2];
-  __shared__ __align__(8) uint64_t v_empty[2];
+  __shared__ __align__(8) uint64_t k_full[NKV];
+  __shared__ __align__(8) uint64_t k_empty[NKV];
+  __shared__ __align__(8) uint64_t v_full[NKV];
+  __shared__ __align__(8) uint64_t v_empty[NKV];
   __shared__ __align__(8) uint64_t s_full[2];
   __shared__ __align__(8) uint64_t p_full[2];
   __shared__ __align__(8) uint64_t o_done;
   __shared__ __align__(8) uint64_t o_final;
   __shared__ uint32_t tmem_slot;
+  __shared__ float s_red[2][2][128];  // [tile parity][half][row] partial row max
+  __shared__ float s_sum[2][128];     // [half][row] partial row sum
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sQ = smem;
@@ -361,7 +364,7 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
   const int ntiles = (kv_end + kTcKT - 1) / kTcKT;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NKV; ++i) {
       lk::mbar_init(&k_full[i], 1);
       lk::mbar_init(&k_empty[i], 1);
       lk::mbar_init(&v_full[i], 1);
@@ -369,24 +372,25 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
     }
     lk::mbar_init(&s_full[0], 1);
     lk::mbar_init(&s_full[1], 1);
-    lk::mbar_init(&p_full[0], 4);
-    lk::mbar_init(&p_full[1], 4);
+    lk::mbar_init(&p_full[0], 8);
+    lk::mbar_init(&p_full[1], 8);
     lk::mbar_init(&o_done, 1);
     lk::mbar_init(&o_final, 1);
     lk::fence_barrier_init();
   }
-  if (warp == 5) lk::tc::alloc(&tmem_slot, 256);
-  if (warp < 4) {
-    // Q tile -> shared memory, K-major with 128-byte swizzle.
-    const int r = threadIdx.x;
+  if (warp == kTcMma) lk::tc::alloc(&tmem_slot, 256);
+  if (warp < 8) {
+    // Q tile -> shared memory, K-major with 128-byte swizzle; warpgroup wg
+    // loads half h = wg of the head dimension of row r.
+    const int r = threadIdx.x & 127, h = threadIdx.x >> 7;
     const int pos = pos0 + r / G, g = r % G;
     const T* qrow = static_cast<const T*>(p.q) + static_cast<int64_t>(q_start + pos) * p.q_stride +
-                    static_cast<int64_t>(kvh * G + g) * kD;
+                    static_cast<int64_t>(kvh * G + g) * kD + h * 64;
 #pragma unroll
-    for (int c = 0; c < 16; ++c) {
+    for (int c = 0; c < 8; ++c) {
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
       if (pos < q_len) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
-      *reinterpret_cast<uint4*>(sQ + (c >> 3) * kTcQHalf + lk::swz128(r, c & 7)) = v;
+      *reinterpret_cast<uint4*>(sQ + h * kTcQHalf + lk::swz128(r, c)) = v;
     }
     lk::fence_proxy_async();
   }
@@ -398,58 +402,73 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
   // over the first 32 columns of the same buffer. O in columns [128, 256).
   const uint32_t tO = tmem + 128;
 
-  if (warp == 4) {
+  if (warp == kTcProducer) {
     // ------------------------------------------------------------ producer
+    // The whole warp resolves block-table entries, 32 boxes (8 tiles) per
+    // batch, one batch ahead, so the table reads never sit between two TMA
+    // issues; lane 0 waits on the rings and issues the copies.
     if (lane == 0) {
       lk::prefetch_tensormap(&kmap);
       lk::prefetch_tensormap(&vmap);
-      const int32_t* bt =
-          p.block_tables ? p.block_tables + static_cast<int64_t>(b) * p.bt_stride : nullptr;
-      const int oob = static_cast<int>(p.num_slots < 0x7fffffffLL ? p.num_slots : 0x7fffffffLL);
-      // K and V rings are separate: a K stage frees when its S MMA completes,
-      // long before the V stage of the same tile.
-      auto slot_of = [&](int tok) -> int {
-        if (tok >= kv_end) return oob;
-        if (!bt) return q_start + tok;
-        const int blk = bt[tok / p.bs];
-        if (blk < 0 || blk >= p.num_blocks) {
-          if (p.status) atomicOr(p.status, LK_STATUS_BLOCK_OOB);
-          return oob;
+    }
+    const int32_t* bt =
+        p.block_tables ? p.block_tables + static_cast<int64_t>(b) * p.bt_stride : nullptr;
+    const int oob = static_cast<int>(p.num_slots < 0x7fffffffLL ? p.num_slots : 0x7fffffffLL);
+    auto slot_of = [&](int tok) -> int {
+      if (tok >= kv_end) return oob;
+      if (!bt) return q_start + tok;
+      const int blk = __ldg(bt + tok / p.bs);
+      if (blk < 0 || blk >= p.num_blocks) {
+        if (p.status) atomicOr(p.status, LK_STATUS_BLOCK_OOB);
+        return oob;
+      }
+      return blk * p.bs + tok % p.bs;
+    };
+    constexpr int kBoxes = kTcKT / 16;      // boxes per tile
+    constexpr int kTilesPer = 32 / kBoxes;  // tiles per 32-box batch
+    int nxt = slot_of(lane * 16);
+    bool ok = true;
+    for (int j0 = 0; j0 < ntiles && ok; j0 += kTilesPer) {
+      const int cur = nxt;
+      nxt = slot_of((j0 + kTilesPer) * kTcKT + lane * 16);
+      const int jn = min(ntiles, j0 + kTilesPer);
+      for (int j = j0; j < jn; ++j) {
+        int slots[kBoxes];
+#pragma unroll
+        for (int tb = 0; tb < kBoxes; ++tb)
+          slots[tb] = __shfl_sync(0xffffffffu, cur, (j - j0) * kBoxes + tb);
+        if (lane == 0) {
+          const int st = j % NKV;
+          const uint32_t ph = ((j / NKV) & 1) ^ 1;
+          uint8_t* dk = sKV + st * kTcStage;
+          if (!lk::mbar_wait(&k_empty[st], ph)) {
+            ok = false;
+          } else {
+            lk::mbar_arrive_expect_tx(&k_full[st], 2 * kTcKHalf);
+#pragma unroll
+            for (int tb = 0; tb < kBoxes; ++tb)
+#pragma unroll
+              for (int dh = 0; dh < 2; ++dh)
+                lk::tma_load_3d(dk + dh * kTcKHalf + tb * 2048, &kmap, &k_full[st], dh * 64,
+                                slots[tb], kvh);
+          }
+          if (ok && !lk::mbar_wait(&v_empty[st], ph)) ok = false;
+          if (ok) {
+            lk::mbar_arrive_expect_tx(&v_full[st], 2 * kTcKHalf);
+#pragma unroll
+            for (int tb = 0; tb < kBoxes; ++tb)
+#pragma unroll
+              for (int dh = 0; dh < 2; ++dh)
+                lk::tma_load_3d(dk + 2 * kTcKHalf + dh * kTcKHalf + tb * 2048, &vmap,
+                                &v_full[st], dh * 64, slots[tb], kvh);
+          }
+          if (!ok && p.status) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
         }
-        return blk * p.bs + tok % p.bs;
-      };
-      for (int j = 0; j < ntiles; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = ((j >> 1) & 1) ^ 1;
-        int slots[kTcKT / 16];
-#pragma unroll
-        for (int tb = 0; tb < kTcKT / 16; ++tb) slots[tb] = slot_of(j * kTcKT + tb * 16);
-        if (!lk::mbar_wait(&k_empty[st], ph)) {
-          if (p.status) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
-          break;
-        }
-        lk::mbar_arrive_expect_tx(&k_full[st], 2 * kTcKHalf);
-        uint8_t* dk = sKV + st * kTcStage;
-#pragma unroll
-        for (int tb = 0; tb < kTcKT / 16; ++tb)
-#pragma unroll
-          for (int dh = 0; dh < 2; ++dh)
-            lk::tma_load_3d(dk + dh * kTcKHalf + tb * 2048, &kmap, &k_full[st], dh * 64, slots[tb],
-                            kvh);
-        if (!lk::mbar_wait(&v_empty[st], ph)) {
-          if (p.status) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
-          break;
-        }
-        lk::mbar_arrive_expect_tx(&v_full[st], 2 * kTcKHalf);
-#pragma unroll
-        for (int tb = 0; tb < kTcKT / 16; ++tb)
-#pragma unroll
-          for (int dh = 0; dh < 2; ++dh)
-            lk::tma_load_3d(dk + 2 * kTcKHalf + dh * kTcKHalf + tb * 2048, &vmap, &v_full[st],
-                            dh * 64, slots[tb], kvh);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kTcMma) {
     // ----------------------------------------------------------- MMA issue
     // Issue order: S(0), S(1), PV(0), S(2), PV(1), ... so that S(j+1) runs on
     // the tensor core while the softmax of tile j runs on the SM.
@@ -460,31 +479,31 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
       const uint32_t q_addr = lk::smem_u32(sQ);
       bool ok = true;
       auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!lk::mbar_wait(&k_full[st], (j >> 1) & 1)) return false;
+        const int st = j % NKV;
+        if (!lk::mbar_wait(&k_full[st], (j / NKV) & 1)) return false;
         lk::tc::fence_after();
         const uint32_t k_addr = lk::smem_u32(sKV + st * kTcStage);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           lk::tc::mma_f16(
-              tmem + 64 * st,
+              tmem + 64 * (j & 1),
               lk::tc::smem_desc_sw128(q_addr + (ks >> 2) * kTcQHalf + (ks & 3) * 32, 16, 1024),
               lk::tc::smem_desc_sw128(k_addr + (ks >> 2) * kTcKHalf + (ks & 3) * 32, 16, 1024),
               idS, ks > 0 ? 1u : 0u);
         }
-        lk::tc::commit(&s_full[st]);
+        lk::tc::commit(&s_full[j & 1]);
         lk::tc::commit(&k_empty[st]);
         return true;
       };
       ok = issue_s(0);
       for (int j = 0; j < ntiles && ok; ++j) {
-        const int st = j & 1;
+        const int sb = j & 1, st = j % NKV;
         if (j + 1 < ntiles && !issue_s(j + 1)) {
           ok = false;
           break;
         }
-        if (!lk::mbar_wait(&p_full[st], (j >> 1) & 1) ||
-            !lk::mbar_wait(&v_full[st], (j >> 1) & 1)) {
+        if (!lk::mbar_wait(&p_full[sb], (j >> 1) & 1) ||
+            !lk::mbar_wait(&v_full[st], (j / NKV) & 1)) {
           ok = false;
           break;
         }
@@ -493,7 +512,7 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
 #pragma unroll
         for (int kk = 0; kk < kTcKT / 16; ++kk) {
           const uint64_t bd = lk::tc::smem_desc_sw128(v_addr + kk * 2048, kTcKHalf, 1024);
-          lk::tc::mma_f16_ts(tO, tmem + 64 * st + kk * 8, bd, idO, (j > 0 || kk > 0) ? 1u : 0u);
+          lk::tc::mma_f16_ts(tO, tmem + 64 * sb + kk * 8, bd, idO, (j > 0 || kk > 0) ? 1u : 0u);
         }
         lk::tc::commit(&v_empty[st]);
         lk::tc::commit(&o_done);
@@ -503,82 +522,83 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
     }
   } else {
     // ------------------------------------------------- softmax / epilogue
-    const int r = threadIdx.x;
+    // Warps w and w + 4 share TMEM lanes 32 (w % 4) .. +31: thread (wg, r)
+    // handles columns [32 wg, 32 wg + 32) of row r's scores and columns
+    // [64 wg, 64 wg + 64) of its output; the two halves agree on the row max
+    // through shared memory and a 64-thread named barrier per warp pair.
+    const int wg = warp >> 2, r = threadIdx.x & 127;
     const int pos = pos0 + r / G, g = r % G;
     const int limit = prior + pos;  // last visible key of this row
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int pair_bar = 1 + (warp & 3);
     const float sl2 = p.scale_log2;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int st = j & 1;
       const uint32_t tS = tmem + 64 * st;
-      if (!lk::mbar_wait(&s_full[st], (j >> 1) & 1)) {
-        ok = false;
-        break;
-      }
+      // On a (never expected) wait timeout the warp carries on with garbage
+      // instead of leaving: its partner warp must still meet it at every
+      // named barrier below.
+      if (ok && !lk::mbar_wait(&s_full[st], (j >> 1) & 1)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
       lk::tc::fence_after();
-      uint32_t sv[2][32];
-      lk::tc::ld32(tS + lane_base, sv[0]);
-      lk::tc::ld32(tS + lane_base + 32, sv[1]);
+      uint32_t sv[32];
+      lk::tc::ld32(tS + lane_base + 32 * wg, sv);
       lk::tc::wait_ld();
-      const int kb = j * kTcKT;
-      const bool need_mask = kb + kTcKT - 1 > limit;
-      if (need_mask) {
+      const int kb = j * kTcKT + 32 * wg;
+      if (kb + 31 > limit) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (kb + h * 32 + i > limit) sv[h][i] = __float_as_uint(-INFINITY);
+        for (int i = 0; i < 32; ++i)
+          if (kb + i > limit) sv[i] = __float_as_uint(-INFINITY);
       }
-      // two independent chains of three-input max
       float ma = -INFINITY, mb = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        ma = lk::fmax3(ma, __uint_as_float(sv[0][i]), __uint_as_float(sv[0][i + 1]));
-        mb = lk::fmax3(mb, __uint_as_float(sv[1][i]), __uint_as_float(sv[1][i + 1]));
+      for (int i = 0; i < 32; i += 4) {
+        ma = lk::fmax3(ma, __uint_as_float(sv[i]), __uint_as_float(sv[i + 1]));
+        mb = lk::fmax3(mb, __uint_as_float(sv[i + 2]), __uint_as_float(sv[i + 3]));
       }
-      const float mraw = fmaxf(ma, mb);
+      s_red[j & 1][wg][r] = fmaxf(ma, mb);
+      lk::named_sync(pair_bar, 64);
+      // both halves have read their scores (wait::ld above) before either
+      // writes P over the buffer below
+      const float mraw = fmaxf(s_red[j & 1][0][r], s_red[j & 1][1][r]);
       const float mx = mraw * sl2;  // sl2 > 0: max commutes with the scaling
       float new_m = m_used;
       if (mx > m_used + kLazyRescale) new_m = mx;
       const float alpha = (new_m == m_used) ? 1.f : exp2f(m_used - new_m);
       const float ms = new_m == -INFINITY ? 0.f : new_m;
-      // Two scores per instruction for the scale-and-shift and the row sum
-      // (packed fp32x2), one MUFU ex2 per score.
       float sum0 = 0.f, sum1 = 0.f;
-      uint32_t pw[32];
+      uint32_t pw[16];
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
+      for (int c = 0; c < 16; ++c) {
         float x0, x1;
-        lk::ffma2(x0, x1, __uint_as_float(sv[c >> 4][(2 * c) & 31]),
-                  __uint_as_float(sv[c >> 4][(2 * c + 1) & 31]), sl2, sl2, -ms, -ms);
+        lk::ffma2(x0, x1, __uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1]), sl2, sl2,
+                  -ms, -ms);
         const float e0 = lk::ex2_mufu(x0);
         const float e1 = lk::ex2_mufu(x1);
         lk::fadd2(sum0, sum1, sum0, sum1, e0, e1);
         pw[c] = lk::pack2<T>(e0, e1);
       }
-      const float sum = sum0 + sum1;
-      lk::tc::st32(tS + lane_base, pw);  // P over the S buffer it came from
-      l = l * alpha + sum;
+      lk::tc::st16(tS + lane_base + 16 * wg, pw);  // P over the S buffer it came from
+      l = l * alpha + (sum0 + sum1);
       // O may only be touched once PV(j-1) has completed; o_done completes
       // once per tile, so every tile waits for its predecessor's phase.
-      if (j > 0 && !lk::mbar_wait(&o_done, (j - 1) & 1)) {
-        ok = false;
-        break;
-      }
+      if (ok && j > 0 && !lk::mbar_wait(&o_done, (j - 1) & 1)) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
       lk::tc::fence_after();
       // tcgen05.ld / st are warp-collective: the warp rescales together if
       // any of its rows needs it (alpha is 1 for the others).
       if (j > 0 && __any_sync(0xffffffffu, new_m != m_used)) {
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
+        for (int c2 = 0; c2 < 2; ++c2) {
           uint32_t ov[32];
-          lk::tc::ld32(tO + lane_base + c4 * 32, ov);
+          const uint32_t ta = tO + lane_base + 64 * wg + 32 * c2;
+          lk::tc::ld32(ta, ov);
           lk::tc::wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-          lk::tc::st32(tO + lane_base + c4 * 32, ov);
+          lk::tc::st32(ta, ov);
         }
       }
       lk::tc::wait_st();
@@ -588,15 +608,19 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
       if (lane == 0) lk::mbar_arrive(&p_full[st]);
     }
     ok = __all_sync(0xffffffffu, ok);
+    // row sum = the two halves' partial sums (same running max in both)
+    s_sum[wg][r] = l;
+    lk::named_sync(pair_bar, 64);
+    l = s_sum[0][r] + s_sum[1][r];
     if (ok && lk::mbar_wait(&o_final, 0)) {
       lk::tc::fence_after();
       const float inv = 1.f / l;
       T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(q_start + pos) * p.H * kD +
-                static_cast<int64_t>(kvh * G + g) * kD;
+                static_cast<int64_t>(kvh * G + g) * kD + 64 * wg;
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int c2 = 0; c2 < 2; ++c2) {
         uint32_t ov[32];
-        lk::tc::ld32(tO + lane_base + c4 * 32, ov);  // whole warp, every row
+        lk::tc::ld32(tO + lane_base + 64 * wg + 32 * c2, ov);  // whole warp, every row
         lk::tc::wait_ld();
         if (pos < q_len) {
 #pragma unroll
@@ -606,7 +630,7 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
             for (int e = 0; e < 4; ++e)
               w[e] = lk::pack2<T>(__uint_as_float(ov[c * 8 + 2 * e]) * inv,
                                   __uint_as_float(ov[c * 8 + 2 * e + 1]) * inv);
-            *reinterpret_cast<uint4*>(orow + c4 * 32 + c * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint4*>(orow + c2 * 32 + c * 8) = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
       }
@@ -617,24 +641,43 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
   lk::tc::fence_before();
   __syncthreads();
   lk::tc::fence_after();
-  if (warp == 5) lk::tc::dealloc(tmem, 256);
+  if (warp == kTcMma) lk::tc::dealloc(tmem, 256);
+}
+
+template <typename T, int NKV>
+int launch_prefill_tc_n(const CUtensorMap& km, const CUtensorMap& vm, const PrefillParams& p,
+                        int num_seqs, int max_q_len, int H_kv, cudaStream_t s) {
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(paged_prefill_tc_kernel<T, NKV>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             tc_smem<NKV>()) != cudaSuccess)
+      return LK_ERR_CUDA;
+    configured[dev] = 1;
+  }
+  dim3 grid((max_q_len + p.BQ - 1) / p.BQ, H_kv, num_seqs);
+  paged_prefill_tc_kernel<T, NKV><<<grid, kTcThreads, tc_smem<NKV>(), s>>>(km, vm, p);
+  return lk::check_launch();
+}
+
+// K/V ring depth: 2 stages (two CTAs per SM) or 5 (one CTA per SM);
+// LITEKERN_PREFILL_STAGES (read once) selects, for tuning.
+int prefill_stages() {
+  static int v = [] {
+    const char* e = getenv("LITEKERN_PREFILL_STAGES");
+    return (e && atoi(e) == 5) ? 5 : 2;
+  }();
+  return v;
 }
 
 template <typename T>
 int launch_prefill_tc(const CUtensorMap& km, const CUtensorMap& vm, const PrefillParams& p,
                       int num_seqs, int max_q_len, int H_kv, cudaStream_t s) {
-  static int configured[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(paged_prefill_tc_kernel<T>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) != cudaSuccess)
-      return LK_ERR_CUDA;
-    configured[dev] = 1;
-  }
-  dim3 grid((max_q_len + p.BQ - 1) / p.BQ, H_kv, num_seqs);
-  paged_prefill_tc_kernel<T><<<grid, kTcThreads, kTcSmem, s>>>(km, vm, p);
-  return lk::check_launch();
+  if (prefill_stages() == 5)
+    return launch_prefill_tc_n<T, 5>(km, vm, p, num_seqs, max_q_len, H_kv, s);
+  return launch_prefill_tc_n<T, 2>(km, vm, p, num_seqs, max_q_len, H_kv, s);
 }
 
 // mma.sync kernel instead of tcgen05 (LITEKERN_PREFILL_MMA_SYNC=1, read once).
