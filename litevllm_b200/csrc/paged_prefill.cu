@@ -305,45 +305,57 @@ int launch_prefill(const CUtensorMap& km, const CUtensorMap& vm, const PrefillPa
 // ---------------------------------------------------------------------------
 // tcgen05 (fifth-generation tensor core) version.
 //
-// CTA = 128 query rows (128 / G positions x the G heads of one KV head).
-// Warps 0-3: softmax and epilogue, thread r owns row r (= TMEM lane r).
-// Warp 4: TMA producer (64-token K and V tiles, two-stage ring).
-// Warp 5: MMA issuer. S = Q K^T (M=128, N=64 keys, K=D) into TMEM columns
-// [0,64); the softmax writes P (bf16/f16, two per 32-bit column) into TMEM
-// columns [64,96); O += P V (A = P from TMEM, B = V from shared memory,
-// MN-major, N = D) accumulates in columns [128,256). Shared memory is
-// 97 KB, so two CTAs share an SM and one CTA's softmax overlaps the other's
-// MMAs. The running max is applied lazily: O is rescaled only when a row's
-// max grows by more than 2^8.
-constexpr int kTcThreads = 320;  // 8 softmax warps, 1 TMA warp, 1 MMA warp
-constexpr int kTcProducer = 8, kTcMma = 9;
+// A CTA holds NSUB query sub-tiles of 128 rows (rows = positions x the G heads
+// of one KV head), all reading the same K/V tiles. Per sub-tile u:
+//   warps 8u .. 8u+7: softmax and epilogue; warps w and w+4 share TMEM lanes
+//     32 (w % 4) .. +31, thread (half, r) handles half of row r's 64 scores
+//     and half of its 128 outputs, the halves agree on the row max through
+//     shared memory and a 64-thread named barrier;
+//   TMEM columns [256u, 256u+128): S double buffer (64 keys each, P written in
+//     place over the S it came from); [256u+128, 256u+256): O accumulator.
+// Warp 8 NSUB: TMA producer (64-token K and V tiles through the block table,
+// separate K and V rings of NKV stages); warp 8 NSUB + 1: MMA issuer:
+//   S_u = Q_u K^T   (kind::f16, M=128, N=64, K=128, A and B from shared memory)
+//   O_u += P_u V    (M=128, N=128, K=64, A = P from TMEM, B = V MN-major)
+// issued as S(j+1) for every sub-tile, then PV(j) for every sub-tile, so the
+// tensor core works on tile j+1 while the softmax works on tile j. The
+// running max is applied lazily: O is rescaled only when a row's max grows
+// by more than 2^8.
 constexpr int kTcKT = 64;                 // keys per tile
 constexpr int kTcQHalf = 128 * 128;       // Q: 128 rows x 128 B (64 values of D)
 constexpr int kTcKHalf = kTcKT * 128;     // K or V: 64 rows x 128 B
 constexpr int kTcStage = 4 * kTcKHalf;    // K (two halves) + V (two halves) = 32 KB
-template <int NKV> constexpr int tc_smem() { return 2 * kTcQHalf + NKV * kTcStage + 1024; }
 constexpr float kLazyRescale = 8.f;       // log2 units
 
-template <typename T, int NKV>
-__global__ void __launch_bounds__(kTcThreads, NKV == 2 ? 2 : 1)
+template <int NSUB, int NKV> struct TcShape {
+  static constexpr int kThreads = NSUB * 256 + 64;
+  static constexpr int kProducer = NSUB * 8, kMma = NSUB * 8 + 1;
+  static constexpr int kSmem = NSUB * 2 * kTcQHalf + NKV * kTcStage + 1024;
+  static constexpr int kTmemCols = NSUB * 256;
+  static constexpr int kRows = NSUB * 128;
+};
+
+template <typename T, int NSUB, int NKV>
+__global__ void __launch_bounds__(TcShape<NSUB, NKV>::kThreads, NSUB == 1 ? 2 : 1)
 paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
+  using Sh = TcShape<NSUB, NKV>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t k_full[NKV];
   __shared__ __align__(8) uint64_t k_empty[NKV];
   __shared__ __align__(8) uint64_t v_full[NKV];
   __shared__ __align__(8) uint64_t v_empty[NKV];
-  __shared__ __align__(8) uint64_t s_full[2];
-  __shared__ __align__(8) uint64_t p_full[2];
-  __shared__ __align__(8) uint64_t o_done;
+  __shared__ __align__(8) uint64_t s_full[NSUB][2];
+  __shared__ __align__(8) uint64_t p_full[NSUB][2];
+  __shared__ __align__(8) uint64_t o_done[NSUB][2];  // PV(j) completes o_done[u][j & 1]
   __shared__ __align__(8) uint64_t o_final;
   __shared__ uint32_t tmem_slot;
-  __shared__ float s_red[2][2][128];  // [tile parity][half][row] partial row max
-  __shared__ float s_sum[2][128];     // [half][row] partial row sum
+  __shared__ float s_red[NSUB][2][2][128];  // [sub][tile parity][half][row] partial row max
+  __shared__ float s_sum[NSUB][2][128];     // [sub][half][row] partial row sum
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sKV = smem + 2 * kTcQHalf;
+  uint8_t* sQ = smem;                          // sub u at u * 2 * kTcQHalf
+  uint8_t* sKV = smem + NSUB * 2 * kTcQHalf;
 
   const int qt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -370,27 +382,33 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
       lk::mbar_init(&v_full[i], 1);
       lk::mbar_init(&v_empty[i], 1);
     }
-    lk::mbar_init(&s_full[0], 1);
-    lk::mbar_init(&s_full[1], 1);
-    lk::mbar_init(&p_full[0], 8);
-    lk::mbar_init(&p_full[1], 8);
-    lk::mbar_init(&o_done, 1);
+    for (int u = 0; u < NSUB; ++u) {
+      lk::mbar_init(&s_full[u][0], 1);
+      lk::mbar_init(&s_full[u][1], 1);
+      lk::mbar_init(&p_full[u][0], 8);
+      lk::mbar_init(&p_full[u][1], 8);
+      lk::mbar_init(&o_done[u][0], 1);
+      lk::mbar_init(&o_done[u][1], 1);
+    }
     lk::mbar_init(&o_final, 1);
     lk::fence_barrier_init();
   }
-  if (warp == kTcMma) lk::tc::alloc(&tmem_slot, 256);
-  if (warp < 8) {
-    // Q tile -> shared memory, K-major with 128-byte swizzle; warpgroup wg
-    // loads half h = wg of the head dimension of row r.
-    const int r = threadIdx.x & 127, h = threadIdx.x >> 7;
-    const int pos = pos0 + r / G, g = r % G;
+  if (warp == Sh::kMma) lk::tc::alloc(&tmem_slot, Sh::kTmemCols);
+  if (warp < NSUB * 8) {
+    // Q -> shared memory, K-major with 128-byte swizzle: sub-tile u, half h of
+    // the head dimension of row r.
+    const int u = warp >> 3, t = threadIdx.x & 255;
+    const int r = t & 127, h = t >> 7;
+    const int R = u * 128 + r;
+    const int pos = pos0 + R / G, g = R % G;
     const T* qrow = static_cast<const T*>(p.q) + static_cast<int64_t>(q_start + pos) * p.q_stride +
                     static_cast<int64_t>(kvh * G + g) * kD + h * 64;
+    uint8_t* dq = sQ + u * 2 * kTcQHalf + h * kTcQHalf;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
       if (pos < q_len) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
-      *reinterpret_cast<uint4*>(sQ + h * kTcQHalf + lk::swz128(r, c)) = v;
+      *reinterpret_cast<uint4*>(dq + lk::swz128(r, c)) = v;
     }
     lk::fence_proxy_async();
   }
@@ -398,11 +416,8 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
   __syncthreads();
   lk::tc::fence_after();
   const uint32_t tmem = tmem_slot;
-  // S double buffer: tile j uses columns [64 * (j & 1), +64); its P is written
-  // over the first 32 columns of the same buffer. O in columns [128, 256).
-  const uint32_t tO = tmem + 128;
 
-  if (warp == kTcProducer) {
+  if (warp == Sh::kProducer) {
     // ------------------------------------------------------------ producer
     // The whole warp resolves block-table entries, 32 boxes (8 tiles) per
     // batch, one batch ahead, so the table reads never sit between two TMA
@@ -468,10 +483,8 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
         if (!ok) break;
       }
     }
-  } else if (warp == kTcMma) {
+  } else if (warp == Sh::kMma) {
     // ----------------------------------------------------------- MMA issue
-    // Issue order: S(0), S(1), PV(0), S(2), PV(1), ... so that S(j+1) runs on
-    // the tensor core while the softmax of tile j runs on the SM.
     if (lane == 0) {
       constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       constexpr uint32_t idS = lk::tc::idesc_f16(fmt, 0, 0, 128, kTcKT);
@@ -484,14 +497,17 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
         lk::tc::fence_after();
         const uint32_t k_addr = lk::smem_u32(sKV + st * kTcStage);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          lk::tc::mma_f16(
-              tmem + 64 * (j & 1),
-              lk::tc::smem_desc_sw128(q_addr + (ks >> 2) * kTcQHalf + (ks & 3) * 32, 16, 1024),
-              lk::tc::smem_desc_sw128(k_addr + (ks >> 2) * kTcKHalf + (ks & 3) * 32, 16, 1024),
-              idS, ks > 0 ? 1u : 0u);
+        for (int u = 0; u < NSUB; ++u) {
+          const uint32_t qa = q_addr + u * 2 * kTcQHalf;
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            lk::tc::mma_f16(
+                tmem + 256 * u + 64 * (j & 1),
+                lk::tc::smem_desc_sw128(qa + (ks >> 2) * kTcQHalf + (ks & 3) * 32, 16, 1024),
+                lk::tc::smem_desc_sw128(k_addr + (ks >> 2) * kTcKHalf + (ks & 3) * 32, 16, 1024),
+                idS, ks > 0 ? 1u : 0u);
+          lk::tc::commit(&s_full[u][j & 1]);
         }
-        lk::tc::commit(&s_full[j & 1]);
         lk::tc::commit(&k_empty[st]);
         return true;
       };
@@ -502,45 +518,51 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
           ok = false;
           break;
         }
-        if (!lk::mbar_wait(&p_full[sb], (j >> 1) & 1) ||
-            !lk::mbar_wait(&v_full[st], (j / NKV) & 1)) {
+        if (!lk::mbar_wait(&v_full[st], (j / NKV) & 1)) {
           ok = false;
           break;
         }
-        lk::tc::fence_after();
         const uint32_t v_addr = lk::smem_u32(sKV + st * kTcStage) + 2 * kTcKHalf;
 #pragma unroll
-        for (int kk = 0; kk < kTcKT / 16; ++kk) {
-          const uint64_t bd = lk::tc::smem_desc_sw128(v_addr + kk * 2048, kTcKHalf, 1024);
-          lk::tc::mma_f16_ts(tO, tmem + 64 * sb + kk * 8, bd, idO, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int u = 0; u < NSUB; ++u) {
+          if (!lk::mbar_wait(&p_full[u][sb], (j >> 1) & 1)) {
+            ok = false;
+            break;
+          }
+          lk::tc::fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kTcKT / 16; ++kk) {
+            const uint64_t bd = lk::tc::smem_desc_sw128(v_addr + kk * 2048, kTcKHalf, 1024);
+            lk::tc::mma_f16_ts(tmem + 256 * u + 128, tmem + 256 * u + 64 * sb + kk * 8, bd, idO,
+                               (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          lk::tc::commit(&o_done[u][sb]);
         }
+        if (!ok) break;
         lk::tc::commit(&v_empty[st]);
-        lk::tc::commit(&o_done);
       }
       if (!ok && p.status) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
       lk::tc::commit(&o_final);
     }
   } else {
     // ------------------------------------------------- softmax / epilogue
-    // Warps w and w + 4 share TMEM lanes 32 (w % 4) .. +31: thread (wg, r)
-    // handles columns [32 wg, 32 wg + 32) of row r's scores and columns
-    // [64 wg, 64 wg + 64) of its output; the two halves agree on the row max
-    // through shared memory and a 64-thread named barrier per warp pair.
-    const int wg = warp >> 2, r = threadIdx.x & 127;
-    const int pos = pos0 + r / G, g = r % G;
+    const int u = warp >> 3, wg = (warp >> 2) & 1, r = threadIdx.x & 127;
+    const int R = u * 128 + r;
+    const int pos = pos0 + R / G, g = R % G;
     const int limit = prior + pos;  // last visible key of this row
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const int pair_bar = 1 + (warp & 3);
+    const uint32_t tSub = tmem + 256 * u, tO = tSub + 128;
+    const int pair_bar = 1 + (warp & 3) + 4 * u;
     const float sl2 = p.scale_log2;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      const int st = j & 1;
-      const uint32_t tS = tmem + 64 * st;
+      const int sb = j & 1;
+      const uint32_t tS = tSub + 64 * sb;
       // On a (never expected) wait timeout the warp carries on with garbage
       // instead of leaving: its partner warp must still meet it at every
       // named barrier below.
-      if (ok && !lk::mbar_wait(&s_full[st], (j >> 1) & 1)) ok = false;
+      if (ok && !lk::mbar_wait(&s_full[u][sb], (j >> 1) & 1)) ok = false;
       ok = __all_sync(0xffffffffu, ok);
       lk::tc::fence_after();
       uint32_t sv[32];
@@ -558,16 +580,17 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
         ma = lk::fmax3(ma, __uint_as_float(sv[i]), __uint_as_float(sv[i + 1]));
         mb = lk::fmax3(mb, __uint_as_float(sv[i + 2]), __uint_as_float(sv[i + 3]));
       }
-      s_red[j & 1][wg][r] = fmaxf(ma, mb);
+      s_red[u][sb][wg][r] = fmaxf(ma, mb);
       lk::named_sync(pair_bar, 64);
       // both halves have read their scores (wait::ld above) before either
       // writes P over the buffer below
-      const float mraw = fmaxf(s_red[j & 1][0][r], s_red[j & 1][1][r]);
+      const float mraw = fmaxf(s_red[u][sb][0][r], s_red[u][sb][1][r]);
       const float mx = mraw * sl2;  // sl2 > 0: max commutes with the scaling
       float new_m = m_used;
       if (mx > m_used + kLazyRescale) new_m = mx;
       const float alpha = (new_m == m_used) ? 1.f : exp2f(m_used - new_m);
       const float ms = new_m == -INFINITY ? 0.f : new_m;
+      // two scores per packed fp32x2 instruction, one MUFU ex2 per score
       float sum0 = 0.f, sum1 = 0.f;
       uint32_t pw[16];
 #pragma unroll
@@ -582,14 +605,16 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
       }
       lk::tc::st16(tS + lane_base + 16 * wg, pw);  // P over the S buffer it came from
       l = l * alpha + (sum0 + sum1);
-      // O may only be touched once PV(j-1) has completed; o_done completes
-      // once per tile, so every tile waits for its predecessor's phase.
-      if (ok && j > 0 && !lk::mbar_wait(&o_done, (j - 1) & 1)) ok = false;
-      ok = __all_sync(0xffffffffu, ok);
-      lk::tc::fence_after();
       // tcgen05.ld / st are warp-collective: the warp rescales together if
-      // any of its rows needs it (alpha is 1 for the others).
+      // any of its rows needs it (alpha is 1 for the others). O may only be
+      // touched once PV(j-1) has completed: PV(i) completes o_done[i & 1]
+      // for the (i >> 1)-th time, and PV(j+1) cannot complete before this
+      // warp releases P(j), so a parity wait is exact even though most tiles
+      // skip it.
       if (j > 0 && __any_sync(0xffffffffu, new_m != m_used)) {
+        if (ok && !lk::mbar_wait(&o_done[u][(j - 1) & 1], ((j - 1) >> 1) & 1)) ok = false;
+        ok = __all_sync(0xffffffffu, ok);
+        lk::tc::fence_after();
 #pragma unroll
         for (int c2 = 0; c2 < 2; ++c2) {
           uint32_t ov[32];
@@ -605,13 +630,12 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
       m_used = new_m;
       lk::tc::fence_before();
       __syncwarp();
-      if (lane == 0) lk::mbar_arrive(&p_full[st]);
+      if (lane == 0) lk::mbar_arrive(&p_full[u][sb]);
     }
-    ok = __all_sync(0xffffffffu, ok);
     // row sum = the two halves' partial sums (same running max in both)
-    s_sum[wg][r] = l;
+    s_sum[u][wg][r] = l;
     lk::named_sync(pair_bar, 64);
-    l = s_sum[0][r] + s_sum[1][r];
+    l = s_sum[u][0][r] + s_sum[u][1][r];
     if (ok && lk::mbar_wait(&o_final, 0)) {
       lk::tc::fence_after();
       const float inv = 1.f / l;
@@ -641,33 +665,36 @@ paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap,
   lk::tc::fence_before();
   __syncthreads();
   lk::tc::fence_after();
-  if (warp == kTcMma) lk::tc::dealloc(tmem, 256);
+  if (warp == Sh::kMma) lk::tc::dealloc(tmem, Sh::kTmemCols);
 }
 
-template <typename T, int NKV>
-int launch_prefill_tc_n(const CUtensorMap& km, const CUtensorMap& vm, const PrefillParams& p,
+template <typename T, int NSUB, int NKV>
+int launch_prefill_tc_n(const CUtensorMap& km, const CUtensorMap& vm, PrefillParams p,
                         int num_seqs, int max_q_len, int H_kv, cudaStream_t s) {
+  using Sh = TcShape<NSUB, NKV>;
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(paged_prefill_tc_kernel<T, NKV>,
+    if (cudaFuncSetAttribute(paged_prefill_tc_kernel<T, NSUB, NKV>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             tc_smem<NKV>()) != cudaSuccess)
+                             Sh::kSmem) != cudaSuccess)
       return LK_ERR_CUDA;
     configured[dev] = 1;
   }
+  p.BQ = Sh::kRows / p.G;
   dim3 grid((max_q_len + p.BQ - 1) / p.BQ, H_kv, num_seqs);
-  paged_prefill_tc_kernel<T, NKV><<<grid, kTcThreads, tc_smem<NKV>(), s>>>(km, vm, p);
+  paged_prefill_tc_kernel<T, NSUB, NKV><<<grid, Sh::kThreads, Sh::kSmem, s>>>(km, vm, p);
   return lk::check_launch();
 }
 
-// K/V ring depth: 2 stages (two CTAs per SM) or 5 (one CTA per SM);
-// LITEKERN_PREFILL_STAGES (read once) selects, for tuning.
-int prefill_stages() {
+// Query sub-tiles per CTA: 1 (128-row CTAs, two per SM; measured fastest on
+// B200) by default; LITEKERN_PREFILL_SUBTILES=2 selects one CTA per SM with
+// two 128-row sub-tiles sharing each K/V tile (read once).
+int prefill_subtiles() {
   static int v = [] {
-    const char* e = getenv("LITEKERN_PREFILL_STAGES");
-    return (e && atoi(e) == 5) ? 5 : 2;
+    const char* e = getenv("LITEKERN_PREFILL_SUBTILES");
+    return (e && atoi(e) == 2) ? 2 : 1;
   }();
   return v;
 }
@@ -675,9 +702,9 @@ int prefill_stages() {
 template <typename T>
 int launch_prefill_tc(const CUtensorMap& km, const CUtensorMap& vm, const PrefillParams& p,
                       int num_seqs, int max_q_len, int H_kv, cudaStream_t s) {
-  if (prefill_stages() == 5)
-    return launch_prefill_tc_n<T, 5>(km, vm, p, num_seqs, max_q_len, H_kv, s);
-  return launch_prefill_tc_n<T, 2>(km, vm, p, num_seqs, max_q_len, H_kv, s);
+  if (prefill_subtiles() == 1)
+    return launch_prefill_tc_n<T, 1, 2>(km, vm, p, num_seqs, max_q_len, H_kv, s);
+  return launch_prefill_tc_n<T, 2, 4>(km, vm, p, num_seqs, max_q_len, H_kv, s);
 }
 
 // mma.sync kernel instead of tcgen05 (LITEKERN_PREFILL_MMA_SYNC=1, read once).
