@@ -239,30 +239,55 @@ def run_ours(args, ws, rank, local):
         h_ids = torch.empty(B, dtype=torch.int64).pin_memory()
         kc, vc = pools[0]
 
-        def e2e_step(i):
-            q = h_q.to(dev, non_blocking=True)
-            k = h_k.to(dev, non_blocking=True)
-            v = h_v.to(dev, non_blocking=True)
-            slot = h_slot.to(dev, non_blocking=True)
-            bt = h_bt.to(dev, non_blocking=True)
-            ctx = h_ctx.to(dev, non_blocking=True)
-            lg = h_logits[i & 1].to(dev, non_blocking=True)
-            o = attn.forward(q, k, v, kc, vc, bt, slot, ctx, is_prefill=False)
+        # Step i+1's host inputs are uploaded on a copy stream into the other
+        # of two device buffer sets while step i computes; every step still
+        # waits for its own token ids on the host.
+        cstream = torch.cuda.Stream(dev)
+        host_in = [dict(q=h_q, k=h_k, v=h_v, slot=h_slot, bt=h_bt, ctx=h_ctx, lg=h_logits[s_])
+                   for s_ in (0, 1)]
+        bufs = [{n: torch.empty_like(t, device=dev) for n, t in hi.items()} for hi in host_in]
+        ready = [torch.cuda.Event(), torch.cuda.Event()]
+        free = [torch.cuda.Event(), torch.cuda.Event()]
+        for ev in free:
+            ev.record(stream)
+
+        def upload(i):
+            s_ = i & 1
+            with torch.cuda.stream(cstream):
+                cstream.wait_event(free[s_])
+                for n, t in host_in[s_].items():
+                    bufs[s_][n].copy_(t, non_blocking=True)
+                ready[s_].record(cstream)
+
+        def compute(i):
+            s_ = i & 1
+            d = bufs[s_]
+            stream.wait_event(ready[s_])
+            o = attn.forward(d["q"], d["k"], d["v"], kc, vc, d["bt"], d["slot"], d["ctx"],
+                             is_prefill=False)
             for li in range(1, args.layers):
-                o = attn.forward(q, k, v, pools[li][0], pools[li][1], bt, slot, ctx, is_prefill=False)
-            tok = Sampler.sample_batch(lg, None, seed=1, offset=i)
+                o = attn.forward(d["q"], d["k"], d["v"], pools[li][0], pools[li][1], d["bt"],
+                                 d["slot"], d["ctx"], is_prefill=False)
+            tok = Sampler.sample_batch(d["lg"], None, seed=1, offset=i)
+            free[s_].record(stream)
             h_ids.copy_(tok, non_blocking=True)
-            torch.cuda.current_stream(dev).synchronize()
+            stream.synchronize()
             return o
 
-        for i in range(max(3, args.warmup)):
-            e2e_step(i)
+        def run(n, first):
+            upload(first)
+            for i in range(first, first + n):
+                if i + 1 < first + n:
+                    upload(i + 1)
+                compute(i)
+
+        run(max(3, args.warmup), 0)
         if ws > 1:
             torch.distributed.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for i in range(K):
-            e2e_step(i)
+        cstream.wait_event(e0)
+        run(K, 1000)
         e1.record(stream)
         torch.cuda.synchronize(dev)
         e2e_ms = e0.elapsed_time(e1) / K
