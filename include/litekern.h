@@ -169,6 +169,32 @@ int lk_sample(int64_t* out_ids, const void* logits, int32_t B, int32_t V, int64_
  * reference falls back to F.softmax).
  */
 /*
+ * Block copies for copy-on-write forks and swaps. Replaces the per-block,
+ * per-layer copy_ loops of KVCache.swap_in / swap_out
+ * (litevllm/cache/kv_cache.py:74-102) and serves SchedulerOutput.blocks_to_copy
+ * (litevllm/engine/scheduler.py:25-27): for every pair p and layer l,
+ *   dst[l][mapping[p][1]] = src[l][mapping[p][0]]   (K and V).
+ * src_cache_ptrs / dst_cache_ptrs: device arrays of 2 * num_layers addresses
+ * (K of layer 0, V of layer 0, K of layer 1, ...); an address may point to
+ * pinned host memory (unified addressing) for swaps. block_mapping: device
+ * int64 [num_pairs, 2] (src, dst). block_bytes = block_size * H_kv * D * elem.
+ * Pairs outside [0, num_blocks) are skipped and flagged LK_STATUS_BLOCK_OOB in
+ * *status (may be NULL). Destination blocks must be distinct.
+ */
+int lk_copy_blocks(const uint64_t* src_cache_ptrs, const uint64_t* dst_cache_ptrs,
+                   int32_t num_layers, const int64_t* block_mapping, int32_t num_pairs,
+                   int64_t block_bytes, int64_t src_num_blocks, int64_t dst_num_blocks,
+                   int32_t* status, void* stream);
+
+/*
+ * Device address of pinned (page-locked) host memory, for the swap pointer
+ * tables of lk_copy_blocks. No counterpart in the reference (its swaps are
+ * torch copy_ calls). Returns LK_ERR_INVALID_ARG for memory that is not
+ * pinned, so a kernel is never given an unmapped host address.
+ */
+int lk_host_device_pointer(const void* host_ptr, uint64_t* device_ptr);
+
+/*
  * Allocation-free variant of lk_sample. It has no counterpart in the
  * reference. It is for callers that cannot call cudaMalloc at the point where
  * they sample: code running while another component owns the allocator

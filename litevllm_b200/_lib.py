@@ -56,6 +56,12 @@ SIGNATURES: dict[str, tuple] = {
         [c_void_p, c_void_p, c_int32, c_int32, c_int64, c_void_p, c_void_p, c_int64, c_uint64,
          c_uint64, c_void_p, c_int32, c_void_p],
     ),
+    "lk_copy_blocks": (
+        c_int32,
+        [c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_int64, c_int64, c_int64, c_void_p,
+         c_void_p],
+    ),
+    "lk_host_device_pointer": (c_int32, [c_void_p, c_void_p]),
     "lk_softmax_temp": (
         c_int32,
         [c_void_p, c_int64, c_void_p, c_int32, c_int32, c_int64, c_void_p, c_int32, c_void_p],

@@ -8,6 +8,7 @@ computes on the host: a CPU tensor or a missing library raises.
 from __future__ import annotations
 
 import contextlib
+import ctypes
 import math
 from typing import Optional
 
@@ -351,6 +352,88 @@ def softmax_temp(logits: torch.Tensor, temperatures: torch.Tensor) -> torch.Tens
             )
         )
     return probs
+
+
+# ------------------------------------------------------------- block copies ---
+def _device_address(t: torch.Tensor) -> int:
+    if t.is_cuda:
+        return t.data_ptr()
+    if not t.is_pinned():
+        raise RuntimeError("host caches must be pinned (page-locked) for device-side swaps")
+    out = ctypes.c_uint64(0)
+    check(lib().lk_host_device_pointer(t.data_ptr(), ctypes.byref(out)))
+    return out.value
+
+
+def copy_blocks_between(src_caches, dst_caches, mapping, device=None,
+                        status: Optional[torch.Tensor] = None) -> None:
+    """dst[layer][d] = src[layer][s] for every (s, d) in mapping and every layer,
+    K and V, in one launch. src_caches / dst_caches: lists of (key_cache,
+    value_cache) per layer ([num_blocks, bs, H_kv, D], contiguous); CUDA tensors
+    or pinned host tensors. mapping: dict {src: dst}, list of pairs or int64
+    [n, 2] tensor. Mirrors KVCache.swap_in / swap_out and blocks_to_copy
+    (litevllm/cache/kv_cache.py:74-102, engine/scheduler.py:25-27)."""
+    if len(src_caches) != len(dst_caches) or not src_caches:
+        raise ValueError("need the same, non-zero number of layers on both sides")
+    k0 = src_caches[0][0]
+    for kc, vc in list(src_caches) + list(dst_caches):
+        if kc.shape[1:] != k0.shape[1:] or vc.shape != kc.shape or kc.dtype != k0.dtype:
+            raise ValueError("all caches must share block shape and dtype")
+        if not (kc.is_contiguous() and vc.is_contiguous()):
+            raise ValueError("caches must be contiguous")
+    if device is None:
+        devs = [t.device for pair in list(src_caches) + list(dst_caches) for t in pair if t.is_cuda]
+        if not devs:
+            raise RuntimeError("at least one side must be on a CUDA device")
+        device = devs[0]
+    device = torch.device(device)
+    if isinstance(mapping, dict):
+        pairs = list(mapping.items())
+    elif isinstance(mapping, torch.Tensor):
+        pairs = None
+    else:
+        pairs = list(mapping)
+    if pairs is not None:
+        if not pairs:
+            return
+        mapping = torch.tensor(pairs, dtype=torch.int64)
+    mapping = mapping.to(device=device, dtype=torch.int64).contiguous().view(-1, 2)
+    n = mapping.shape[0]
+    if n == 0:
+        return
+    src_ptrs = torch.tensor([_device_address(t) for pair in src_caches for t in pair],
+                            dtype=torch.uint64).to(device)
+    dst_ptrs = torch.tensor([_device_address(t) for pair in dst_caches for t in pair],
+                            dtype=torch.uint64).to(device)
+    block_bytes = k0[0].numel() * k0.element_size()
+    with _on(device):
+        check(
+            lib().lk_copy_blocks(
+                src_ptrs.data_ptr(), dst_ptrs.data_ptr(), len(src_caches), mapping.data_ptr(), n,
+                block_bytes, src_caches[0][0].shape[0], dst_caches[0][0].shape[0],
+                _ptr(status), _stream(device),
+            )
+        )
+    # src_ptrs / dst_ptrs / mapping are freed in stream order on the launching
+    # stream, after the kernel that reads them.
+
+
+def copy_blocks(caches, mapping) -> None:
+    """Copy-on-write block copies inside one set of device caches."""
+    copy_blocks_between(caches, caches, mapping)
+
+
+def swap_in(gpu_caches, cpu_caches, mapping) -> None:
+    """KVCache.swap_in: gpu[layer][dst] = cpu[layer][src] (pinned host caches)."""
+    copy_blocks_between(cpu_caches, gpu_caches, mapping)
+
+
+def swap_out(gpu_caches, cpu_caches, mapping) -> None:
+    """KVCache.swap_out: cpu[layer][dst] = gpu[layer][src]; synchronises the
+    stream so the host copy is complete on return."""
+    copy_blocks_between(gpu_caches, cpu_caches, mapping)
+    dev = next(t.device for pair in gpu_caches for t in pair)
+    torch.cuda.current_stream(dev).synchronize()
 
 
 def default_scale(head_dim: int) -> float:
