@@ -187,6 +187,27 @@ int lk_copy_blocks(const uint64_t* src_cache_ptrs, const uint64_t* dst_cache_ptr
                    int32_t* status, void* stream);
 
 /*
+ * Fused q/k RMSNorm + rotary embedding + KV-cache store, the steps between the
+ * projections and attention in Qwen3Attention.forward
+ * (litevllm/models/qwen3.py:76-92; LlamaAttention without the norm):
+ * LlamaRMSNorm (models/llama.py:18-27) when a weight is given, then the
+ * half-split rotation of apply_rotary_emb (layers/rotary_emb.py:104-117) with
+ * the caller's fp32 cos / sin tables ([max_pos, D/2], the RotaryEmbedding
+ * cos_cached / sin_cached buffers) at positions[t]; q is rotated in place
+ * ([T, H, D]); k is rotated and stored with v into slot slot_mapping[t] of the
+ * caches (slot_mapping NULL: q / k only, no store; -1: skip). D = 128, dtype
+ * F16 or BF16, rounding points as in the reference (16-bit after the norm
+ * and after the weight, fp32 rotation, 16-bit store).
+ */
+int lk_rope_store_kv(void* q, int64_t q_token_stride, const void* k, int64_t k_token_stride,
+                     const void* v, int64_t v_token_stride, void* k_cache, void* v_cache,
+                     int64_t num_slots, const int64_t* slot_mapping, const int64_t* positions,
+                     const float* cos_cache, const float* sin_cache, int64_t max_pos,
+                     const void* q_norm_weight, const void* k_norm_weight, float eps,
+                     int32_t num_tokens, int32_t H, int32_t H_kv, int32_t D, int32_t dtype,
+                     int32_t* status, void* stream);
+
+/*
  * Device address of pinned (page-locked) host memory, for the swap pointer
  * tables of lk_copy_blocks. No counterpart in the reference (its swaps are
  * torch copy_ calls). Returns LK_ERR_INVALID_ARG for memory that is not

@@ -354,6 +354,61 @@ def softmax_temp(logits: torch.Tensor, temperatures: torch.Tensor) -> torch.Tens
     return probs
 
 
+# ------------------------------------------------ norm + RoPE + KV store ---
+def rope_store_kvcache(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    key_cache: Optional[torch.Tensor],
+    value_cache: Optional[torch.Tensor],
+    slot_mapping: Optional[torch.Tensor],
+    positions: torch.Tensor,
+    cos_cached: torch.Tensor,
+    sin_cached: torch.Tensor,
+    q_norm_weight: Optional[torch.Tensor] = None,
+    k_norm_weight: Optional[torch.Tensor] = None,
+    eps: float = 1e-6,
+    status: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """In one launch: optional q/k RMSNorm, RoPE on q (in place) and k, and the
+    store of k / v into the paged cache. Mirrors Qwen3Attention.forward
+    (litevllm/models/qwen3.py:76-92) up to the attention call; returns query."""
+    dev = _cuda(query, key, value, key_cache, value_cache, slot_mapping, positions, cos_cached,
+                sin_cached, q_norm_weight, k_norm_weight, status)
+    T, H, D = query.shape
+    H_kv = key.shape[1]
+    for t in (query, key, value):
+        if t.stride(2) != 1 or t.stride(1) != D:
+            raise ValueError("q/k/v must have unit d-stride and head stride D")
+    code = _dtype_code(query)
+    if key.dtype != query.dtype or value.dtype != query.dtype:
+        raise TypeError("q, k, v must share a dtype")
+    if cos_cached.dtype != torch.float32 or sin_cached.dtype != torch.float32:
+        raise TypeError("cos / sin tables must be fp32 (RotaryEmbedding buffers)")
+    cos_cached, sin_cached = cos_cached.contiguous(), sin_cached.contiguous()
+    positions = positions.to(torch.int64).contiguous()
+    for w in (q_norm_weight, k_norm_weight):
+        if w is not None and (w.dtype != query.dtype or w.numel() != D):
+            raise TypeError("norm weights must be [D] in the activation dtype")
+    num_slots = 0
+    if slot_mapping is not None:
+        if key_cache is None or value_cache is None or not key_cache.is_contiguous():
+            raise ValueError("a slot mapping needs contiguous caches")
+        slot_mapping = slot_mapping.to(torch.int64).contiguous()
+        num_slots = key_cache.shape[0] * key_cache.shape[1]
+    with _on(dev):
+        check(
+            lib().lk_rope_store_kv(
+                query.data_ptr(), query.stride(0), key.data_ptr(), key.stride(0), value.data_ptr(),
+                value.stride(0), _ptr(key_cache), _ptr(value_cache), num_slots, _ptr(slot_mapping),
+                positions.data_ptr(), cos_cached.data_ptr(), sin_cached.data_ptr(),
+                cos_cached.shape[0], _ptr(q_norm_weight), _ptr(k_norm_weight), float(eps), T, H,
+                H_kv, D, code, _ptr(status), _stream(dev),
+            )
+        )
+    return query
+
+
 # ------------------------------------------------------------- block copies ---
 def _device_address(t: torch.Tensor) -> int:
     if t.is_cuda:

@@ -12,6 +12,10 @@ seeded inputs, what its own functions return:
   decode_g4.npz      same, 32 Q / 8 KV heads (Llama-3-8B GQA ratio 4).
   prefill.npz        Attention.forward(..., is_prefill=True)    (store + _prefill,
                      :141-151) for G=2 and G=4.
+  rope.npz           LlamaRMSNorm (litevllm/models/llama.py:18-27) on q and k, then
+                     RotaryEmbedding + apply_rotary_emb (layers/rotary_emb.py) at Qwen3
+                     settings (theta 1e6), as Qwen3Attention.forward does (qwen3.py:76-84);
+                     the cos / sin rows of the used positions are stored with it.
   sampler.npz        Sampler.sample greedy ids (litevllm/layers/sampler.py:151-175)
                      with planted ties, and the temperature softmax the reference
                      computes before its multinomial draw (:178 / :133-135).
@@ -115,6 +119,31 @@ def main(ref_root: str) -> None:
         HERE / "sampler.npz",
         logits=logits.numpy(), greedy=greedy.numpy(), probs07=probs07.numpy(),
         ref_vec=ref_vec.numpy(), ref_vec_out=ref_vec_out.numpy(),
+    )
+    # q/k RMSNorm + RoPE, as in Qwen3Attention.forward
+    from litevllm.layers.rotary_emb import RotaryEmbedding, apply_rotary_emb
+    from litevllm.models.llama import LlamaRMSNorm
+
+    T, H, H_kv, D = 9, 16, 8, 128
+    rope = RotaryEmbedding(D, 40960, 1000000.0, None)
+    positions = torch.randint(0, 40960, (T,), generator=g)
+    qn, kn = LlamaRMSNorm(D), LlamaRMSNorm(D)
+    with torch.no_grad():
+        qn.weight.copy_(1 + 0.1 * torch.randn(D, generator=g))
+        kn.weight.copy_(1 + 0.1 * torch.randn(D, generator=g))
+    qn, kn = qn.bfloat16(), kn.bfloat16()
+    q = torch.randn((T, H, D), generator=g).bfloat16()
+    k = torch.randn((T, H_kv, D), generator=g).bfloat16()
+    with torch.no_grad():
+        cos, sin = rope(positions)
+        q_ref = apply_rotary_emb(qn(q), cos.unsqueeze(1), sin.unsqueeze(1))
+        k_ref = apply_rotary_emb(kn(k), cos.unsqueeze(1), sin.unsqueeze(1))
+    np.savez_compressed(
+        HERE / "rope.npz", q=bf16_bits(q), k=bf16_bits(k), positions=positions.numpy(),
+        cos=cos.numpy(), sin=sin.numpy(), q_w=bf16_bits(qn.weight.detach()),
+        k_w=bf16_bits(kn.weight.detach()), eps=np.float32(qn.eps),
+        q_out=q_ref.float().numpy(), k_out=k_ref.float().numpy(),
+        q_out_dtype=str(q_ref.dtype),
     )
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
 

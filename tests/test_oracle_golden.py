@@ -123,3 +123,15 @@ def test_uniform_mapping_open_interval():
     assert 0.0 < u[0] < 1e-6 and 1 - 1e-6 < u[1] < 1.0
     g = osamp.gumbel_from_u(u)
     assert np.all(np.isfinite(g))
+
+
+def test_rope_oracle_matches_reference():
+    from oracle import rope as orope
+
+    d = golden_io.load("rope.npz")
+    q, k = golden_io.bf16(d["q"]), golden_io.bf16(d["k"])
+    cos, sin = torch.from_numpy(d["cos"]), torch.from_numpy(d["sin"])
+    qw, kw = golden_io.bf16(d["q_w"]), golden_io.bf16(d["k_w"])
+    eps = float(d["eps"])
+    assert torch.equal(orope.norm_rope(q, cos, sin, qw, eps), torch.from_numpy(d["q_out"]))
+    assert torch.equal(orope.norm_rope(k, cos, sin, kw, eps), torch.from_numpy(d["k_out"]))
