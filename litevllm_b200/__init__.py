@@ -22,11 +22,15 @@ _ATTENTION_SITES = ("litevllm.layers.attention", "litevllm.layers", "litevllm.mo
 _SAMPLER_SITES = ("litevllm.layers.sampler", "litevllm.layers", "litevllm.engine.llm_engine")
 
 
-def install() -> list[str]:
+def install(engine_hooks: bool = False) -> list[str]:
     """Point litevllm's Attention, PagedAttention and Sampler at this package.
 
     Returns the patched "module.name" sites. Modules of litevllm that are not
     importable are skipped; the reference's call sites need no other change.
+    With engine_hooks=True, ModelRunner.prepare_inputs and
+    LLMEngine._process_outputs are also replaced by the vectorised / batched
+    versions in litevllm_b200.engine_hooks (one sampler launch and one host
+    sync per step instead of one per sequence).
     """
     from .attention import Attention, PagedAttention
     from .sampler import Sampler
@@ -49,4 +53,15 @@ def install() -> list[str]:
         if hasattr(mod, "Sampler"):
             setattr(mod, "Sampler", Sampler)
             patched.append(f"{mod_name}.Sampler")
+    if engine_hooks:
+        try:
+            runner_mod = importlib.import_module("litevllm.engine.model_runner")
+            engine_mod = importlib.import_module("litevllm.engine.llm_engine")
+        except Exception:
+            return patched
+        from . import engine_hooks as hooks
+
+        hooks.install(runner_mod.ModelRunner, engine_mod.LLMEngine)
+        patched += ["litevllm.engine.model_runner.ModelRunner.prepare_inputs",
+                    "litevllm.engine.llm_engine.LLMEngine._process_outputs"]
     return patched

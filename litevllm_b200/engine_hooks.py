@@ -1,0 +1,132 @@
+"""Replacements for the two engine methods either side of the hot path.
+
+* ``prepare_inputs`` — same result as ``ModelRunner.prepare_inputs``
+  (litevllm/engine/model_runner.py:180-260): input ids, positions, slot
+  mapping (missing blocks map to slot 0), zero-padded int32 block tables and
+  int32 context lengths for decode batches, ``None`` tables for prefill. The
+  per-token Python loops become numpy arithmetic, and all int64 data reaches
+  the device in one pinned host-to-device copy (one more for the int32 data)
+  instead of one synchronous copy per tensor.
+* ``process_outputs`` — same bookkeeping as ``LLMEngine._process_outputs``
+  (litevllm/engine/llm_engine.py:172-199): each sequence gets the token
+  sampled from its row (the last prompt row for a prefill), prompts are marked
+  computed, stop rules run in sequence order. Rows whose parameters are plain
+  temperature / greedy are sampled in one ``Sampler.sample_batch`` launch with
+  per-row temperatures and read back with one ``.tolist()``; rows that need
+  repetition penalty, top-k or top-p go through ``Sampler.sample`` as before.
+
+``install(runner_cls, engine_cls)`` binds both onto the reference classes.
+"""
+
+from __future__ import annotations
+
+import sys
+
+import numpy as np
+import torch
+
+from .sampler import Sampler
+
+
+def _fast_params(params) -> bool:
+    return (getattr(params, "repetition_penalty", 1.0) == 1.0
+            and getattr(params, "top_k", -1) <= 0 and getattr(params, "top_p", 1.0) >= 1.0)
+
+
+def prepare_inputs(self, seq_groups, block_manager):
+    """Vectorised ModelRunner.prepare_inputs; returns the runner module's InputMetadata."""
+    InputMetadata = sys.modules[type(self).__module__].InputMetadata
+    bs = self.config.cache_config.block_size
+    ids_parts, pos_parts, slot_parts = [], [], []
+    tables, ctx_lens, seq_ids = [], [], []
+    is_prefill = False
+    for sg in seq_groups:
+        for seq in sg.get_unfinished_seqs():
+            seq_ids.append(seq.seq_id)
+            blocks = np.asarray(block_manager.get_block_table(seq.seq_id).physical_block_ids,
+                                dtype=np.int64)
+            if seq.is_prefill:
+                is_prefill = True
+                start, end = seq.num_computed_tokens, seq.data.prompt_len
+                toks = np.asarray(seq.data.prompt_token_ids[start:end], dtype=np.int64)
+                pos = np.arange(start, end, dtype=np.int64)
+            else:
+                toks = np.asarray(seq.data.all_token_ids[-1:], dtype=np.int64)
+                pos = np.asarray([seq.data.total_len - 1], dtype=np.int64)
+                ctx_lens.append(seq.data.total_len)
+                tables.append(blocks)
+            bidx = pos // bs
+            have = bidx < blocks.shape[0]
+            slot = np.zeros_like(pos)
+            if have.any():
+                slot[have] = blocks[bidx[have]] * bs + pos[have] % bs
+            ids_parts.append(toks)
+            pos_parts.append(pos)
+            slot_parts.append(slot)
+    n = sum(p.shape[0] for p in pos_parts)
+    cat = lambda parts: np.concatenate(parts) if parts else np.zeros(0, dtype=np.int64)
+    packed = np.concatenate([cat(ids_parts), cat(pos_parts), cat(slot_parts)])
+    device = torch.device(self.device)
+    host = torch.from_numpy(packed)
+    if device.type == "cuda":
+        host = host.pin_memory()
+    dev64 = host.to(device, non_blocking=True)
+    input_ids, positions, slot_mapping = dev64[:n], dev64[n:2 * n], dev64[2 * n:]
+    if is_prefill:
+        block_tables = context_lens = None
+    else:
+        max_blocks = max((t.shape[0] for t in tables), default=0)
+        tab = np.zeros((len(tables), max_blocks), dtype=np.int32)
+        for i, t in enumerate(tables):
+            tab[i, :t.shape[0]] = t
+        tab = np.concatenate([tab.reshape(-1), np.asarray(ctx_lens, dtype=np.int32)])
+        h32 = torch.from_numpy(tab)
+        if device.type == "cuda":
+            h32 = h32.pin_memory()
+        d32 = h32.to(device, non_blocking=True)
+        nb = len(tables) * max_blocks
+        block_tables = d32[:nb].view(len(tables), max_blocks)
+        context_lens = d32[nb:]
+    return InputMetadata(input_ids=input_ids, positions=positions, slot_mapping=slot_mapping,
+                         block_tables=block_tables, context_lens=context_lens,
+                         is_prefill=is_prefill, seq_ids=seq_ids)
+
+
+def process_outputs(self, logits, seq_groups) -> None:
+    """Batched LLMEngine._process_outputs (one sampler launch for plain rows)."""
+    entries = []
+    idx = 0
+    for sg in seq_groups:
+        for seq in sg.get_unfinished_seqs():
+            if seq.is_prefill:
+                n = seq.data.prompt_len - seq.num_computed_tokens
+                seq.num_computed_tokens = seq.data.prompt_len
+                row = idx + n - 1
+                idx += n
+            else:
+                row = idx
+                idx += 1
+            entries.append((sg, seq, row))
+    if logits.dim() == 1:
+        logits = logits.unsqueeze(0)
+    tokens = [None] * len(entries)
+    fast = [i for i, (sg, _, _) in enumerate(entries) if _fast_params(sg.sampling_params)]
+    if fast:
+        rows = torch.tensor([entries[i][2] for i in fast], dtype=torch.int64, device=logits.device)
+        temps = torch.tensor([float(entries[i][0].sampling_params.temperature) for i in fast],
+                             dtype=torch.float32, device=logits.device)
+        picked = Sampler.sample_batch(logits.index_select(0, rows), temps).tolist()
+        for i, t in zip(fast, picked):
+            tokens[i] = int(t)
+    for i, (sg, seq, row) in enumerate(entries):
+        if tokens[i] is None:
+            tokens[i] = int(self.sampler.sample(logits[row:row + 1], sg.sampling_params).item())
+    for (sg, seq, _), tok in zip(entries, tokens):
+        seq.data.append_token(tok)
+        self._should_stop(seq, sg.sampling_params, tok)
+
+
+def install(runner_cls, engine_cls) -> None:
+    """Bind the batched methods onto the reference ModelRunner / LLMEngine."""
+    runner_cls.prepare_inputs = prepare_inputs
+    engine_cls._process_outputs = process_outputs

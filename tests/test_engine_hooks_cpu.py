@@ -1,0 +1,112 @@
+"""Engine hooks vs the reference engine methods, on CPU: the vectorised
+prepare_inputs must build exactly the reference's tensors, and the batched
+process_outputs must leave sequences exactly as the reference's per-sequence
+loop does (greedy rows; the GPU sampler is replaced by argmax here)."""
+
+import sys
+import types
+from pathlib import Path
+
+import pytest
+import torch
+
+REF = Path("/root/reference")
+pytestmark = pytest.mark.skipif(not (REF / "litevllm").exists(),
+                                reason="reference checkout not present")
+
+
+@pytest.fixture(scope="module")
+def ref():
+    sys.path.insert(0, str(REF))
+    from litevllm.cache.block_manager import BlockManager
+    from litevllm.config import CacheConfig, SamplingParams, SchedulerConfig
+    from litevllm.engine import llm_engine, model_runner
+    from litevllm.engine.scheduler import Scheduler
+    from litevllm.engine.sequence import SequenceGroup
+
+    yield types.SimpleNamespace(BlockManager=BlockManager, CacheConfig=CacheConfig,
+                                SamplingParams=SamplingParams, SchedulerConfig=SchedulerConfig,
+                                Scheduler=Scheduler, SequenceGroup=SequenceGroup,
+                                ModelRunner=model_runner.ModelRunner,
+                                LLMEngine=llm_engine.LLMEngine)
+    sys.path.remove(str(REF))
+
+
+def _schedule(ref, prompts, steps_of_decode=0, block_size=16):
+    cache = ref.CacheConfig(block_size=block_size, num_gpu_blocks=256)
+    sched = ref.Scheduler(ref.SchedulerConfig(max_num_seqs=16, max_num_batched_tokens=4096,
+                                              chunked_prefill=False, chunk_size=4096),
+                          cache, ref.BlockManager(block_size=block_size, num_gpu_blocks=256))
+    for i, p in enumerate(prompts):
+        sched.add_request(ref.SequenceGroup.create(f"r{i}", p, ref.SamplingParams(temperature=0.0)))
+    return sched
+
+
+def _runner(ref, block_size=16):
+    return types.SimpleNamespace(config=types.SimpleNamespace(
+        cache_config=types.SimpleNamespace(block_size=block_size)), device="cpu")
+
+
+def _same(a, b):
+    assert a.is_prefill == b.is_prefill and a.seq_ids == b.seq_ids
+    for name in ("input_ids", "positions", "slot_mapping", "block_tables", "context_lens"):
+        x, y = getattr(a, name), getattr(b, name)
+        if x is None or y is None:
+            assert x is None and y is None, name
+        else:
+            assert x.dtype == y.dtype and torch.equal(x, y), name
+
+
+def test_prepare_inputs_matches_reference_prefill_and_decode(ref, monkeypatch):
+    from litevllm_b200 import engine_hooks
+
+    sched = _schedule(ref, [list(range(3, 40)), list(range(7, 12)), list(range(1, 70))])
+    out = sched.schedule()
+    groups = out.scheduled_seq_groups
+    runner = _runner(ref)
+    runner.prepare_inputs = types.MethodType(engine_hooks.prepare_inputs, runner)
+    # prepare_inputs finds InputMetadata in the module of the runner's class;
+    # the stand-in runner's class lives in `types`
+    import litevllm.engine.model_runner as mr
+    monkeypatch.setattr(sys.modules[type(runner).__module__], "InputMetadata", mr.InputMetadata,
+                        raising=False)
+    want = ref.ModelRunner.prepare_inputs(runner, groups, sched.block_manager)
+    got = engine_hooks.prepare_inputs(runner, groups, sched.block_manager)
+    _same(got, want)
+    assert got.is_prefill
+    # move every sequence to decode and grow it across a block boundary
+    for sg in groups:
+        for seq in sg.get_unfinished_seqs():
+            seq.num_computed_tokens = seq.data.prompt_len
+            for t in range(12):
+                seq.data.append_token(100 + t)
+                table = sched.block_manager.get_block_table(seq.seq_id)
+                if seq.get_num_blocks(16) > len(table):
+                    sched.block_manager.append_slot(seq.seq_id)
+    want = ref.ModelRunner.prepare_inputs(runner, groups, sched.block_manager)
+    got = engine_hooks.prepare_inputs(runner, groups, sched.block_manager)
+    _same(got, want)
+    assert not got.is_prefill and got.block_tables.shape[0] == 3
+
+
+def test_process_outputs_matches_reference(ref, monkeypatch):
+    from litevllm_b200 import engine_hooks
+    from litevllm_b200.sampler import Sampler
+
+    monkeypatch.setattr(Sampler, "sample_batch",
+                        staticmethod(lambda logits, temps=None, **kw: logits.argmax(-1)))
+    prompts = [list(range(3, 20)), list(range(5, 9)), list(range(2, 40))]
+    logits = torch.randn(17 + 4 + 38, 50)
+
+    def run(fn):
+        sched = _schedule(ref, prompts)
+        groups = sched.schedule().scheduled_seq_groups
+        eng = types.SimpleNamespace(
+            sampler=types.SimpleNamespace(sample=lambda lg, p: lg.argmax(-1)),
+            _should_stop=lambda seq, p, tok: ref.LLMEngine._should_stop(eng, seq, p, tok),
+            tokenizer=types.SimpleNamespace(eos_token_id=7, decode=lambda ids, **k: ""))
+        fn(eng, logits, groups)
+        return [(s.data.output_token_ids, s.num_computed_tokens, s.status)
+                for g in groups for s in g.seqs]
+
+    assert run(engine_hooks.process_outputs) == run(ref.LLMEngine._process_outputs)
