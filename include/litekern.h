@@ -216,6 +216,23 @@ int lk_rope_store_kv(void* q, int64_t q_token_stride, const void* k, int64_t k_t
 int lk_host_device_pointer(const void* host_ptr, uint64_t* device_ptr);
 
 /*
+ * Sampling with top-k / top-p filters, fused. Replaces the filtered branch of
+ * Sampler.sample (litevllm/layers/sampler.py:178-187 with _apply_top_k_top_p,
+ * :204-225: softmax(x / T), zero p below the k-th largest, drop tokens whose
+ * preceding sorted mass exceeds top_p, renormalise, draw) with a Gumbel-max
+ * draw over the kept tokens (same distribution; bit-exact given the noise).
+ * Per row: temperatures[b] (0 = greedy, filters ignored), top_k[b] (<= 0 or
+ * NULL: off), top_p[b] (>= 1 or NULL: off). Noise as for lk_sample (given
+ * tensor, or Philox keyed by seed / offset / row / index). 16-bit logits
+ * ([B, V], row stride ld); tokens with equal logits are kept or dropped
+ * together. No workspace.
+ */
+int lk_sample_filtered(int64_t* out_ids, const void* logits, int32_t B, int32_t V, int64_t ld,
+                       const float* temperatures, const int32_t* top_k, const float* top_p,
+                       const float* noise, int64_t noise_ld, uint64_t seed, uint64_t offset,
+                       int32_t dtype, void* stream);
+
+/*
  * Allocation-free variant of lk_sample. It has no counterpart in the
  * reference. It is for callers that cannot call cudaMalloc at the point where
  * they sample: code running while another component owns the allocator

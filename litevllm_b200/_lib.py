@@ -62,6 +62,11 @@ SIGNATURES: dict[str, tuple] = {
          c_void_p],
     ),
     "lk_host_device_pointer": (c_int32, [c_void_p, c_void_p]),
+    "lk_sample_filtered": (
+        c_int32,
+        [c_void_p, c_void_p, c_int32, c_int32, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_int64, c_uint64, c_uint64, c_int32, c_void_p],
+    ),
     "lk_rope_store_kv": (
         c_int32,
         [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64,

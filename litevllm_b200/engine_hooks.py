@@ -10,10 +10,10 @@
 * ``process_outputs`` — same bookkeeping as ``LLMEngine._process_outputs``
   (litevllm/engine/llm_engine.py:172-199): each sequence gets the token
   sampled from its row (the last prompt row for a prefill), prompts are marked
-  computed, stop rules run in sequence order. Rows whose parameters are plain
-  temperature / greedy are sampled in one ``Sampler.sample_batch`` launch with
-  per-row temperatures and read back with one ``.tolist()``; rows that need
-  repetition penalty, top-k or top-p go through ``Sampler.sample`` as before.
+  computed, stop rules run in sequence order. Rows without a repetition
+  penalty are sampled in one ``Sampler.sample_batch`` launch with per-row
+  temperature, top-k and top-p (top-k / top-p rows need 16-bit logits) and read
+  back with one ``.tolist()``; the other rows go through ``Sampler.sample``.
 
 ``install(runner_cls, engine_cls)`` binds both onto the reference classes.
 """
@@ -28,9 +28,11 @@ import torch
 from .sampler import Sampler
 
 
-def _fast_params(params) -> bool:
-    return (getattr(params, "repetition_penalty", 1.0) == 1.0
-            and getattr(params, "top_k", -1) <= 0 and getattr(params, "top_p", 1.0) >= 1.0)
+def _fast_params(params, logits_dtype) -> bool:
+    if getattr(params, "repetition_penalty", 1.0) != 1.0:
+        return False
+    filtered = getattr(params, "top_k", -1) > 0 or getattr(params, "top_p", 1.0) < 1.0
+    return not filtered or logits_dtype in (torch.bfloat16, torch.float16)
 
 
 def prepare_inputs(self, seq_groups, block_manager):
@@ -110,12 +112,21 @@ def process_outputs(self, logits, seq_groups) -> None:
     if logits.dim() == 1:
         logits = logits.unsqueeze(0)
     tokens = [None] * len(entries)
-    fast = [i for i, (sg, _, _) in enumerate(entries) if _fast_params(sg.sampling_params)]
+    fast = [i for i, (sg, _, _) in enumerate(entries)
+            if _fast_params(sg.sampling_params, logits.dtype)]
     if fast:
-        rows = torch.tensor([entries[i][2] for i in fast], dtype=torch.int64, device=logits.device)
-        temps = torch.tensor([float(entries[i][0].sampling_params.temperature) for i in fast],
-                             dtype=torch.float32, device=logits.device)
-        picked = Sampler.sample_batch(logits.index_select(0, rows), temps).tolist()
+        dev = logits.device
+        params = [entries[i][0].sampling_params for i in fast]
+        rows = torch.tensor([entries[i][2] for i in fast], dtype=torch.int64, device=dev)
+        temps = torch.tensor([float(sp.temperature) for sp in params], dtype=torch.float32,
+                             device=dev)
+        top_k = top_p = None
+        if any(sp.top_k > 0 or sp.top_p < 1.0 for sp in params):
+            top_k = torch.tensor([int(sp.top_k) for sp in params], dtype=torch.int32, device=dev)
+            top_p = torch.tensor([float(sp.top_p) for sp in params], dtype=torch.float32,
+                                 device=dev)
+        picked = Sampler.sample_batch(logits.index_select(0, rows), temps, top_k=top_k,
+                                      top_p=top_p).tolist()
         for i, t in zip(fast, picked):
             tokens[i] = int(t)
     for i, (sg, seq, row) in enumerate(entries):

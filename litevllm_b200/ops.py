@@ -334,6 +334,50 @@ def sample(
     return out
 
 
+def sample_filtered(
+    logits: torch.Tensor,
+    temperatures: torch.Tensor,
+    top_k: Optional[torch.Tensor] = None,
+    top_p: Optional[torch.Tensor] = None,
+    noise: Optional[torch.Tensor] = None,
+    seed: int = 0,
+    offset: int = 0,
+    out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """Top-k / top-p filtered Gumbel-max sampling (16-bit logits), int64 [B].
+    Mirrors Sampler.sample's filtered branch (litevllm/layers/sampler.py:178-225)."""
+    if logits.dim() == 1:
+        logits = logits.unsqueeze(0)
+    dev = _cuda(logits, temperatures, top_k, top_p, noise, out)
+    B, V = logits.shape
+    if logits.stride(1) != 1:
+        logits = logits.contiguous()
+    code = _dtype_code(logits)
+    temperatures = temperatures.to(torch.float32).contiguous()
+    if top_k is not None:
+        top_k = top_k.to(torch.int32).contiguous()
+    if top_p is not None:
+        top_p = top_p.to(torch.float32).contiguous()
+    noise_ld = 0
+    if noise is not None:
+        if noise.dtype != torch.float32 or noise.shape[0] != B or noise.shape[1] < V or noise.stride(1) != 1:
+            raise TypeError("noise must be fp32 [B, >=V]")
+        noise_ld = noise.stride(0)
+    if out is None:
+        out = torch.empty(B, dtype=torch.int64, device=dev)
+    if B == 0:
+        return out
+    with _on(dev):
+        check(
+            lib().lk_sample_filtered(
+                out.data_ptr(), logits.data_ptr(), B, V, logits.stride(0), temperatures.data_ptr(),
+                _ptr(top_k), _ptr(top_p), _ptr(noise), noise_ld, seed & (2**64 - 1),
+                offset & (2**64 - 1), code, _stream(dev),
+            )
+        )
+    return out
+
+
 def softmax_temp(logits: torch.Tensor, temperatures: torch.Tensor) -> torch.Tensor:
     """fp32 softmax(logits / T) per row (the top-k / top-p path)."""
     if logits.dim() == 1:

@@ -6,8 +6,9 @@ reference signature (litevllm/layers/sampler.py:147-187):
 * repetition penalty -> same arithmetic as the reference (:190-201), torch ops
   on the GPU;
 * temperature 0 -> liblitekern greedy argmax (replaces _argmax_kernel);
-* top-k / top-p -> liblitekern softmax(x / T), the reference's top-k / top-p
-  masking (:204-225), torch.multinomial;
+* top-k / top-p -> fused liblitekern filter + Gumbel-max draw for 16-bit
+  logits (same kept set and distribution as :204-225); fp32 logits use
+  liblitekern softmax(x / T), the reference's masking and torch.multinomial;
 * otherwise -> liblitekern Gumbel-max with in-kernel Philox noise: one pass,
   no probability tensor. The seed is drawn from torch's CPU generator, so
   torch.manual_seed makes it reproducible; sampling_params.seed, when set,
@@ -81,6 +82,15 @@ class Sampler:
             return ops.sample(logits)
         temps = torch.full((B,), T, dtype=torch.float32, device=logits.device)
         if sampling_params.top_k > 0 or sampling_params.top_p < 1.0:
+            if logits.dtype in (torch.bfloat16, torch.float16):
+                # fused: filter + Gumbel-max in one launch, no probability tensor
+                ks = torch.full((B,), int(sampling_params.top_k), dtype=torch.int32,
+                                device=logits.device)
+                ps = torch.full((B,), float(sampling_params.top_p), dtype=torch.float32,
+                                device=logits.device)
+                return ops.sample_filtered(logits, temps, ks, ps,
+                                           seed=Sampler._seed(sampling_params),
+                                           offset=Sampler._next_offset())
             probs = ops.softmax_temp(logits, temps)
             probs = _apply_top_k_top_p(probs, sampling_params.top_k, sampling_params.top_p)
             return torch.multinomial(probs, num_samples=1).squeeze(-1)
@@ -100,11 +110,23 @@ class Sampler:
         offset: Optional[int] = None,
         noise_dump: Optional[torch.Tensor] = None,
         out: Optional[torch.Tensor] = None,
+        top_k: Optional[torch.Tensor] = None,
+        top_p: Optional[torch.Tensor] = None,
     ) -> torch.Tensor:
         """One sampler launch for a whole step: rows with temperature 0 are
-        greedy, the others Gumbel-max at their own temperature."""
+        greedy, the others Gumbel-max at their own temperature; with per-row
+        top_k (int32, <= 0 off) / top_p (fp32, >= 1 off) the fused filtered
+        kernel runs instead (16-bit logits)."""
         if temperatures is not None and temperatures.dtype != torch.float32:
             temperatures = temperatures.float()
+        if top_k is not None or top_p is not None:
+            if temperatures is None:
+                temperatures = torch.zeros(logits.shape[0], dtype=torch.float32,
+                                           device=logits.device)
+            return ops.sample_filtered(
+                logits, temperatures, top_k, top_p, noise=noise,
+                seed=Sampler._seed() if seed is None else seed,
+                offset=Sampler._next_offset() if offset is None else offset, out=out)
         return ops.sample(
             logits,
             temperatures,

@@ -89,3 +89,33 @@ def philox_uniforms(b: int, V: int, seed: int, offset: int) -> np.ndarray:
 def gumbel_from_u(u: np.ndarray) -> np.ndarray:
     u = np.asarray(u, dtype=np.float32)
     return (-np.log(-np.log(u))).astype(np.float32)
+
+
+def filtered_kept(logits, temperature: float, top_k: int, top_p: float):
+    """Tokens the reference keeps: softmax(x / T) in fp32, then the masking of
+    _apply_top_k_top_p (litevllm/layers/sampler.py:204-225) before its
+    renormalisation; returns (kept bool [V], probs fp32 [V]). Torch on CPU."""
+    import torch
+
+    x = torch.as_tensor(np.asarray(logits, dtype=np.float32))
+    probs = torch.softmax(x / np.float32(temperature), dim=-1)
+    p = probs.clone()
+    if top_k > 0:
+        k = min(top_k, p.size(-1))
+        kth = torch.topk(p, k, dim=-1).values[..., -1, None]
+        p = torch.where(p < kth, torch.zeros_like(p), p)
+    if top_p < 1.0:
+        sp, si = torch.sort(p, descending=True, dim=-1)
+        cum = torch.cumsum(sp, dim=-1)
+        sp = torch.where(cum - sp > top_p, torch.zeros_like(sp), sp)
+        p = torch.zeros_like(p).scatter_(-1, si, sp)
+    return (p > 0).numpy(), probs.numpy()
+
+
+def filtered_gumbel(logits, temperature: float, top_k: int, top_p: float, noise) -> int:
+    """argmax over kept tokens of fp32(x) / T + g (IEEE fp32), lowest index on ties."""
+    kept, _ = filtered_kept(logits, temperature, top_k, top_p)
+    x = np.asarray(logits, dtype=np.float32)
+    key = (x / np.float32(temperature)).astype(np.float32) + np.asarray(noise, np.float32)
+    key = np.where(kept, key.astype(np.float32), -np.inf)
+    return int(np.argmax(key))

@@ -95,6 +95,7 @@ def test_process_outputs_matches_reference(ref, monkeypatch):
 
     monkeypatch.setattr(Sampler, "sample_batch",
                         staticmethod(lambda logits, temps=None, **kw: logits.argmax(-1)))
+    # (greedy rows; the filter arguments stay None)
     prompts = [list(range(3, 20)), list(range(5, 9)), list(range(2, 40))]
     logits = torch.randn(17 + 4 + 38, 50)
 
