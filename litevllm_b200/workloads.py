@@ -263,3 +263,41 @@ def make_prefill_batch(
         q_lens=list(q_lens),
         scale=1.0 / math.sqrt(D),
     )
+
+
+def make_prefix_batch(B: int = 128, shared_blocks: int = 128, private_blocks: int = 16,
+                      seed: int = 0, dtype=torch.bfloat16, device="cpu", H: int = 32,
+                      H_kv: int = 8, D: int = 128, bs: int = 16, fork=None) -> DecodeBatch:
+    """Config 4: every sequence's table starts with the same `shared_blocks`
+    physical blocks (a common prefix), except that the last shared block is
+    copy-on-write forked into a private copy per sequence, followed by
+    `private_blocks` private blocks. `fork(caches, mapping)` performs the copy
+    (the library's block copy); without it the copy is done with torch."""
+    pool = (shared_blocks - 1) + B * (1 + private_blocks)
+    ctx = (shared_blocks + private_blocks) * bs
+    g = _gen(seed * 1000003 + 44, "cpu")
+    perm = torch.randperm(pool, generator=g)
+    shared = perm[: shared_blocks - 1]
+    rest = perm[shared_blocks - 1:].view(B, 1 + private_blocks)
+    bt = torch.empty((B, shared_blocks + private_blocks), dtype=torch.int32)
+    bt[:, : shared_blocks - 1] = shared.to(torch.int32)
+    bt[:, shared_blocks - 1:] = rest.to(torch.int32)
+    base = (seed * 7919 + 4) * 16
+    kc = _randn((pool, bs, H_kv, D), dtype, device, base + 1)
+    vc = _randn((pool, bs, H_kv, D), dtype, device, base + 2)
+    # the original last shared block lives at rest[0, 0]; fork it into rest[b, 0]
+    if fork is not None:
+        fork([(kc, vc)], [(int(rest[0, 0]), int(rest[b, 0])) for b in range(1, B)])
+    else:
+        for b in range(1, B):
+            kc[int(rest[b, 0])] = kc[int(rest[0, 0])]
+            vc[int(rest[b, 0])] = vc[int(rest[0, 0])]
+    slots = [int(bt[i, (ctx - 1) // bs]) * bs + (ctx - 1) % bs for i in range(B)]
+    return DecodeBatch(
+        query=_randn((B, H, D), dtype, device, base + 3),
+        key=_randn((B, H_kv, D), dtype, device, base + 4),
+        value=_randn((B, H_kv, D), dtype, device, base + 5),
+        key_cache=kc, value_cache=vc, block_tables=bt.to(device),
+        context_lens=torch.full((B,), ctx, dtype=torch.int32).to(device),
+        slot_mapping=torch.tensor(slots, dtype=torch.int64).to(device),
+        ctx=[ctx] * B, scale=1.0 / math.sqrt(D))

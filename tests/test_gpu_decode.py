@@ -156,3 +156,12 @@ def test_persistent_matches_split_kernel(cuda):
     s = ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables, b.context_lens,
                          b.scale, num_splits=3)
     assert_attn_close(a, s.float(), max_abs=8e-3, mean_rel=2e-3)
+
+
+def test_decode_shared_prefix_with_cow_fork(cuda):
+    """Config 4: 128 sequences share a 2048-token prefix (127 shared blocks plus a
+    copy-on-write fork of the last one, made with the library's block copy)."""
+    b = workloads.make_prefix_batch(B=128, seed=1, device=cuda, fork=ops.copy_blocks)
+    ref_b = workloads.make_prefix_batch(B=128, seed=1, device=cuda)  # torch fork
+    assert torch.equal(b.key_cache, ref_b.key_cache) and torch.equal(b.value_cache, ref_b.value_cache)
+    _check(b, rows=[0, 1, 64, 127])
