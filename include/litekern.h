@@ -233,6 +233,14 @@ int lk_sample_filtered(int64_t* out_ids, const void* logits, int32_t B, int32_t 
                        int32_t dtype, void* stream);
 
 /*
+ * Self-test of the bounded-wait failure path (no counterpart in the
+ * reference): a kernel waits on an mbarrier that nothing arrives on, gives up
+ * after timeout_ns (at most 100 ms), sets LK_STATUS_WAIT_TIMEOUT in *status
+ * and returns. Faults nothing; the context stays usable.
+ */
+int lk_selftest_wait_timeout(int32_t* status, uint64_t timeout_ns, void* stream);
+
+/*
  * Allocation-free variant of lk_sample. It has no counterpart in the
  * reference. It is for callers that cannot call cudaMalloc at the point where
  * they sample: code running while another component owns the allocator

@@ -101,12 +101,12 @@ LK_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Wait for the phase with the given parity to complete. Returns false when the
 // wait exceeded kWaitTimeoutNs (the caller then flags an error and unwinds).
-LK_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity) {
+LK_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t it = 0;
   while (!mbar_try_wait(bar, parity)) {
-    if ((++it & 255u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
+    if ((++it & 255u) == 0 && globaltimer_ns() - t0 > timeout_ns) return false;
   }
   return true;
 }

@@ -99,3 +99,33 @@ def test_install_patches_reference_namespace():
         assert Q.Attention is Attention
     finally:
         sys.path.remove(str(REF))
+
+
+def _rank_dies(rank, world, port, q):
+    import datetime
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.distributed.init_process_group("gloo", rank=rank, world_size=world,
+                                         timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(0)  # a worker that leaves between steps, nothing in flight
+    try:
+        torch.distributed.barrier()
+        q.put((rank, "no error"))
+    except Exception as e:  # the survivor learns of it on the host
+        q.put((rank, type(e).__name__))
+
+
+def test_dead_rank_is_detected_by_timed_barrier():
+    """A rank that exits between steps: the other rank's next barrier fails
+    within the process-group timeout instead of hanging."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29700 + os.getpid() % 1000
+    procs = [ctx.Process(target=_rank_dies, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    rank, outcome = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+    assert rank == 0 and outcome != "no error"
