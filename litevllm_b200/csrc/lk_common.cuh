@@ -200,6 +200,23 @@ LK_DEVINL float ex2_mufu(float x) {
   return y;
 }
 
+// Packed fp32x2 arithmetic (sm_100): two lanes per instruction.
+LK_DEVINL void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                     float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+LK_DEVINL void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // 2^x on the FMA / ALU pipes: x = n + f with n = round(x), f in [-1/2, 1/2];
 // 2^f by a cubic least-squares fit on Chebyshev nodes (coefficients fitted
 // for this library; max relative error 2.5e-4, below the rounding of the
@@ -217,22 +234,24 @@ LK_DEVINL float exp2_fma(float x) {
   return x < -126.f ? 0.f : r;
 }
 
-// Packed fp32x2 arithmetic (sm_100): two lanes per instruction.
-LK_DEVINL void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
-                     float c1) {
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+// Two exponentials with the same polynomial on the packed fp32x2 pipe (no
+// select: inputs are clamped at -126, where the result is a denormal-sized
+// positive value, below anything a 16-bit probability can hold next to the
+// row maximum's 1.0).
+LK_DEVINL void exp2_fma2(float& r0, float& r1, float x0, float x1) {
+  const float a0 = fmaxf(x0, -126.f), a1 = fmaxf(x1, -126.f);
+  float y0, y1, t0, t1, f0, f1, q0, q1;
+  fadd2(y0, y1, a0, a1, 12582912.f, 12582912.f);
+  fadd2(t0, t1, y0, y1, -12582912.f, -12582912.f);
+  ffma2(f0, f1, t0, t1, -1.f, -1.f, a0, a1);  // a - round(a), exact
+  ffma2(q0, q1, f0, f1, 0.05746771767735481f, 0.05746771767735481f, 0.24254462122917175f,
+        0.24254462122917175f);
+  ffma2(q0, q1, q0, q1, f0, f1, 0.6928921341896057f, 0.6928921341896057f);
+  ffma2(q0, q1, q0, q1, f0, f1, 0.9999291300773621f, 0.9999291300773621f);
+  r0 = __int_as_float(__float_as_int(q0) + (__float_as_int(y0) << 23));
+  r1 = __int_as_float(__float_as_int(q1) + (__float_as_int(y1) << 23));
 }
-LK_DEVINL void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
+
 
 // Three-input fp32 max (sm_100).
 LK_DEVINL float fmax3(float a, float b, float c) {

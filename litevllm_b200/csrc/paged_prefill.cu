@@ -24,6 +24,9 @@
 
 #include <stdlib.h>
 
+#include <mutex>
+#include <string>
+#include <vector>
 #include <type_traits>
 
 namespace {
@@ -53,6 +56,8 @@ struct PrefillParams {
   int H, G, bs, BQ;
   float scale_log2;
   int32_t* status;
+  int num_seqs, H_kv, nqt;  // persistent ping-pong kernel: work-item grid
+  int* sched;               // its work-item counter (zeroed per launch)
 };
 
 template <typename T>
@@ -707,6 +712,506 @@ int launch_prefill_tc(const CUtensorMap& km, const CUtensorMap& vm, const Prefil
   return launch_prefill_tc_n<T, 2, 4>(km, vm, p, num_seqs, max_q_len, H_kv, s);
 }
 
+// ---------------------------------------------------------------------------
+// Ping-pong kernel (the default): persistent, one CTA per SM; each work item
+// is two 128-row query sub-tiles A and B (256 rows: BQ = 256 / G positions x
+// G heads) sharing 128-token K/V tiles. TMEM (512 columns): S_A [0,128),
+// S_B [128,256), O_A [256,384), O_B [384,512); each sub-tile's P (16-bit
+// pairs) is written over the first 64 columns of its own S, in two 64-key
+// halves released separately so PV on keys 0-63 overlaps the exponentials of
+// keys 64-127. The MMA thread issues PV_A(j), S_A(j+1), PV_B(j), S_B(j+1), ...
+// so the tensor core works on one sub-tile while the other's softmax runs.
+// Warps 0-3: softmax of A, 4-7: softmax of B (one row per thread); warp 8:
+// TMA producer and work scheduler; warp 9: MMA issue. Work items come from a
+// global counter (the hardware's dynamic CTA dispatch, kept inside one
+// persistent CTA), so barriers and TMEM are set up once per SM and the next
+// item's K/V and Q loads overlap the current item's last tiles and output.
+constexpr int kPpKT = 128;                 // keys per tile
+constexpr int kPpKHalf = kPpKT * 128;      // K or V d-half: 128 rows x 128 B = 16 KB
+constexpr int kPpKStage = 2 * kPpKHalf;    // one K (or V) tile: 32 KB
+constexpr int kPpThreads = 320;
+constexpr int kPpSmem = 2 * 2 * kTcQHalf + 4 * kPpKStage + 1024;  // Q_A, Q_B, 2 K + 2 V stages
+
+template <typename T>
+__global__ void __launch_bounds__(kPpThreads, 1)
+paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
+                        const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t k_full[2];
+  __shared__ __align__(8) uint64_t k_empty[2];
+  __shared__ __align__(8) uint64_t v_full[2];
+  __shared__ __align__(8) uint64_t v_empty[2];
+  __shared__ __align__(8) uint64_t q_full[2];     // [sub-tile]
+  __shared__ __align__(8) uint64_t s_full[2];     // [sub-tile]
+  __shared__ __align__(8) uint64_t p_full[2][2];  // [sub-tile][key half]
+  __shared__ __align__(8) uint64_t o_final;
+  __shared__ __align__(8) uint64_t item_full[2];   // work-item ring, depth 2
+  __shared__ __align__(8) uint64_t item_empty[2];
+  __shared__ int item_ring[2];
+  __shared__ uint32_t tmem_slot;
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem;                           // sub-tile u at u * 2 * kTcQHalf
+  uint8_t* sK = smem + 4 * kTcQHalf;            // stage st at st * kPpKStage
+  uint8_t* sV = sK + 2 * kPpKStage;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.G, BQ = p.BQ;
+  const int per_q = p.H_kv * p.num_seqs;
+  const int num_items = p.nqt * per_q;
+
+  // Work item w: all items of query tile nqt - 1 first, then nqt - 2, ...
+  // (later tiles see more keys under the causal mask). The producer warp
+  // takes items from a global counter as it runs out of work and passes
+  // them to the MMA thread and the softmax warps through item_ring.
+  struct Item {
+    int q_start, q_len, pos0, prior, kv_end, ntiles, kvh, b;
+  };
+  auto item = [&](int w) {
+    Item it;
+    const int qt = p.nqt - 1 - w / per_q, rem = w % per_q;
+    it.kvh = rem % p.H_kv;
+    it.b = rem / p.H_kv;
+    it.q_start = p.cu_seqlens_q[it.b];
+    it.q_len = p.cu_seqlens_q[it.b + 1] - it.q_start;
+    it.pos0 = qt * BQ;
+    it.prior = 0;
+    if (p.block_tables != nullptr && p.context_lens != nullptr) {
+      it.prior = p.context_lens[it.b] - it.q_len;
+      if (it.prior < 0) {
+        if (threadIdx.x == 0 && p.status) atomicOr(p.status, LK_STATUS_CTX_OOB);
+        it.prior = 0;
+      }
+    }
+    it.kv_end = it.prior + min(it.q_len, it.pos0 + BQ);
+    it.ntiles = it.pos0 < it.q_len ? (it.kv_end + kPpKT - 1) / kPpKT : 0;
+    return it;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      lk::mbar_init(&k_full[i], 1);
+      lk::mbar_init(&k_empty[i], 1);
+      lk::mbar_init(&v_full[i], 1);
+      lk::mbar_init(&v_empty[i], 1);
+      lk::mbar_init(&q_full[i], 4);
+      lk::mbar_init(&s_full[i], 1);
+      lk::mbar_init(&p_full[i][0], 4);
+      lk::mbar_init(&p_full[i][1], 4);
+    }
+    lk::mbar_init(&o_final, 1);
+    for (int i = 0; i < 2; ++i) {
+      lk::mbar_init(&item_full[i], 1);
+      lk::mbar_init(&item_empty[i], 9);  // the MMA thread + 8 softmax warps
+    }
+    lk::fence_barrier_init();
+  }
+  if (warp == 9) lk::tc::alloc(&tmem_slot, 512);
+  lk::tc::fence_before();
+  __syncthreads();
+  lk::tc::fence_after();
+  const uint32_t tmem = tmem_slot;
+  // Consumers: the n-th item this CTA processes (num_items = no more work).
+  // Lane 0 waits, reads and releases the slot; the result goes to all lanes.
+  auto next_item = [&](int n, bool& ok) -> int {
+    int w = num_items;
+    if (lane == 0) {
+      if (ok && lk::mbar_wait(&item_full[n & 1], (n >> 1) & 1)) {
+        w = item_ring[n & 1];
+        lk::mbar_arrive(&item_empty[n & 1]);
+      } else {
+        ok = false;
+      }
+    }
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    return __shfl_sync(0xffffffffu, w, 0);
+  };
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      lk::prefetch_tensormap(&kmap);
+      lk::prefetch_tensormap(&vmap);
+    }
+    const int oob = static_cast<int>(p.num_slots < 0x7fffffffLL ? p.num_slots : 0x7fffffffLL);
+    constexpr int kBoxes = kPpKT / 16;      // 8 boxes per tile
+    constexpr int kTilesPer = 32 / kBoxes;  // 4 tiles per block-table batch
+    bool ok = true;
+    int g = 0;  // K/V tiles loaded so far by this CTA
+    for (int n = 0; ok; ++n) {
+      int w = num_items;
+      if (lane == 0) {
+        do {
+          w = atomicAdd(p.sched, 1);
+        } while (w < num_items && item(w).ntiles == 0);
+        if (w > num_items) w = num_items;
+        if (lk::mbar_wait(&item_empty[n & 1], ((n >> 1) & 1) ^ 1)) {
+          item_ring[n & 1] = w;
+          lk::mbar_arrive(&item_full[n & 1]);
+        } else {
+          ok = false;
+          if (p.status) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      w = __shfl_sync(0xffffffffu, w, 0);
+      if (!ok || w >= num_items) break;
+      const Item it = item(w);
+      const int32_t* bt =
+          p.block_tables ? p.block_tables + static_cast<int64_t>(it.b) * p.bt_stride : nullptr;
+      auto slot_of = [&](int tok) -> int {
+        if (tok >= it.kv_end) return oob;
+        if (!bt) return it.q_start + tok;
+        const int blk = __ldg(bt + tok / p.bs);
+        if (blk < 0 || blk >= p.num_blocks) {
+          if (p.status) atomicOr(p.status, LK_STATUS_BLOCK_OOB);
+          return oob;
+        }
+        return blk * p.bs + tok % p.bs;
+      };
+      int nxt = it.ntiles > 0 ? slot_of(lane * 16) : oob;
+      for (int j0 = 0; j0 < it.ntiles && ok; j0 += kTilesPer) {
+        const int cur = nxt;
+        nxt = slot_of((j0 + kTilesPer) * kPpKT + lane * 16);
+        const int jn = min(it.ntiles, j0 + kTilesPer);
+        for (int j = j0; j < jn; ++j, ++g) {
+          int slots[kBoxes];
+#pragma unroll
+          for (int tb = 0; tb < kBoxes; ++tb)
+            slots[tb] = __shfl_sync(0xffffffffu, cur, (j - j0) * kBoxes + tb);
+          if (lane == 0) {
+            const int st = g & 1;
+            const uint32_t ph = ((g >> 1) & 1) ^ 1;
+            if (!lk::mbar_wait(&k_empty[st], ph)) {
+              ok = false;
+            } else {
+              lk::mbar_arrive_expect_tx(&k_full[st], kPpKStage);
+#pragma unroll
+              for (int tb = 0; tb < kBoxes; ++tb)
+#pragma unroll
+                for (int dh = 0; dh < 2; ++dh)
+                  lk::tma_load_3d(sK + st * kPpKStage + dh * kPpKHalf + tb * 2048, &kmap,
+                                  &k_full[st], dh * 64, slots[tb], it.kvh);
+            }
+            if (ok && !lk::mbar_wait(&v_empty[st], ph)) ok = false;
+            if (ok) {
+              lk::mbar_arrive_expect_tx(&v_full[st], kPpKStage);
+#pragma unroll
+              for (int tb = 0; tb < kBoxes; ++tb)
+#pragma unroll
+                for (int dh = 0; dh < 2; ++dh)
+                  lk::tma_load_3d(sV + st * kPpKStage + dh * kPpKHalf + tb * 2048, &vmap,
+                                  &v_full[st], dh * 64, slots[tb], it.kvh);
+            }
+            if (!ok && p.status) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
+          }
+          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+          if (!ok) break;
+        }
+      }
+    }
+  } else if (warp == 9) {
+    // ----------------------------------------------------------- MMA issue
+    if (lane == 0) {
+      constexpr int fmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+      constexpr uint32_t idS = lk::tc::idesc_f16(fmt, 0, 0, 128, kPpKT);
+      constexpr uint32_t idO = lk::tc::idesc_f16(fmt, 0, 1, 128, 128);
+      const uint32_t q_addr = lk::smem_u32(sQ), k_addr0 = lk::smem_u32(sK),
+                     v_addr0 = lk::smem_u32(sV);
+      auto issue_s = [&](int u, int g) {
+        const uint32_t qa = q_addr + u * 2 * kTcQHalf;
+        const uint32_t ka = k_addr0 + (g & 1) * kPpKStage;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          lk::tc::mma_f16(
+              tmem + 128 * u,
+              lk::tc::smem_desc_sw128(qa + (ks >> 2) * kTcQHalf + (ks & 3) * 32, 16, 1024),
+              lk::tc::smem_desc_sw128(ka + (ks >> 2) * kPpKHalf + (ks & 3) * 32, 16, 1024), idS,
+              ks > 0 ? 1u : 0u);
+        lk::tc::commit(&s_full[u]);
+      };
+      auto issue_pv = [&](int u, int g, bool first, int h) {  // keys 64h .. 64h + 63
+        const uint32_t va = v_addr0 + (g & 1) * kPpKStage;
+#pragma unroll
+        for (int kk = 4 * h; kk < 4 * h + 4; ++kk) {
+          const uint64_t bd = lk::tc::smem_desc_sw128(va + kk * 2048, kPpKHalf, 1024);
+          lk::tc::mma_f16_ts(tmem + 256 + 128 * u, tmem + 128 * u + kk * 8, bd, idO,
+                             (!first || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = true;
+      int g = 0, n_items = 0;
+      for (;;) {
+        int w = num_items;
+        if (lk::mbar_wait(&item_full[n_items & 1], (n_items >> 1) & 1)) {
+          w = item_ring[n_items & 1];
+          lk::mbar_arrive(&item_empty[n_items & 1]);
+        } else {
+          ok = false;
+        }
+        if (!ok || w >= num_items) break;
+        const Item it = item(w);
+        // first tile's S for both sub-tiles, each once its Q is in shared memory
+        ok = lk::mbar_wait(&k_full[g & 1], (g >> 1) & 1);
+#pragma unroll
+        for (int u = 0; u < 2 && ok; ++u) {
+          ok = lk::mbar_wait(&q_full[u], n_items & 1);
+          lk::tc::fence_after();
+          if (ok) issue_s(u, g);
+        }
+        if (!ok) break;
+        lk::tc::commit(&k_empty[g & 1]);
+        for (int j = 0; j < it.ntiles && ok; ++j, ++g) {
+          const int st = g & 1;
+          const bool more = j + 1 < it.ntiles;
+          if (!lk::mbar_wait(&v_full[st], (g >> 1) & 1)) { ok = false; break; }
+          if (more && !lk::mbar_wait(&k_full[st ^ 1], ((g + 1) >> 1) & 1)) { ok = false; break; }
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            if (!lk::mbar_wait(&p_full[u][0], g & 1)) { ok = false; break; }
+            lk::tc::fence_after();
+            issue_pv(u, g, j == 0, 0);
+            if (!lk::mbar_wait(&p_full[u][1], g & 1)) { ok = false; break; }
+            lk::tc::fence_after();
+            issue_pv(u, g, j == 0, 1);
+            if (u == 1) lk::tc::commit(&v_empty[st]);
+            if (more) issue_s(u, g + 1);  // S_u(j+1) after PV_u(j): P_u(j) is read first
+          }
+          if (!ok) break;
+          if (more) lk::tc::commit(&k_empty[st ^ 1]);
+        }
+        lk::tc::commit(&o_final);
+        ++n_items;
+      }
+      if (!ok && p.status) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
+    }
+  } else {
+    // ------------------------------------------------- softmax / epilogue
+    const int u = warp >> 2, t = threadIdx.x, r = t & 127;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + 128 * u, tO = tmem + 256 + 128 * u;
+    uint8_t* dq = sQ + u * 2 * kTcQHalf;
+    const float sl2 = p.scale_log2;
+    // Row t of an item's 256-row tile: position pos0 + t / G, head g = t % G.
+    auto load_q = [&](const Item& it, uint4 (&qv)[16]) {
+      const int pos = it.pos0 + t / G, g = t % G;
+      const T* qrow = static_cast<const T*>(p.q) +
+                      static_cast<int64_t>(it.q_start + pos) * p.q_stride +
+                      static_cast<int64_t>(it.kvh * G + g) * kD;
+#pragma unroll
+      for (int c = 0; c < 16; ++c)
+        qv[c] = pos < it.q_len ? *reinterpret_cast<const uint4*>(qrow + c * 8)
+                               : make_uint4(0u, 0u, 0u, 0u);
+    };
+    auto store_q = [&](const uint4 (&qv)[16]) {
+#pragma unroll
+      for (int c = 0; c < 16; ++c)
+        *reinterpret_cast<uint4*>(dq + (c >> 3) * kTcQHalf + lk::swz128(r, c & 7)) = qv[c];
+      lk::fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) lk::mbar_arrive(&q_full[u]);
+    };
+    bool ok = true;
+    int g = 0, n_items = 0;
+    int w = next_item(0, ok);
+    if (w < num_items) {
+      uint4 qv[16];
+      load_q(item(w), qv);
+      store_q(qv);
+    }
+    while (w < num_items && ok) {
+      const Item it = item(w);
+      const int pos = it.pos0 + t / G, gh = t % G;
+      const int limit = it.prior + pos;  // last visible key of this row
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < it.ntiles; ++j, ++g) {
+        if (ok && !lk::mbar_wait(&s_full[u], g & 1)) ok = false;
+        ok = __all_sync(0xffffffffu, ok);
+        lk::tc::fence_after();
+        // Pass 1: row maximum over the 128 scores, 64 columns per TMEM load.
+        const int kb = j * kPpKT;
+        const bool diag = kb + kPpKT - 1 > limit;  // tile crosses the causal edge
+        auto load_half = [&](int h, uint32_t (&sv)[2][32]) {
+          lk::tc::ld32(tS + lane_base + 64 * h, sv[0]);
+          lk::tc::ld32(tS + lane_base + 64 * h + 32, sv[1]);
+          lk::tc::wait_ld();
+          if (diag) {
+#pragma unroll
+            for (int c2 = 0; c2 < 2; ++c2)
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (kb + 64 * h + 32 * c2 + i > limit) sv[c2][i] = __float_as_uint(-INFINITY);
+          }
+        };
+        float mc[4];  // four independent max chains
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t sv[2][32];
+          load_half(h, sv);
+#pragma unroll
+          for (int c2 = 0; c2 < 2; ++c2) {
+            float m = lk::fmax3(__uint_as_float(sv[c2][0]), __uint_as_float(sv[c2][1]),
+                                __uint_as_float(sv[c2][2]));
+#pragma unroll
+            for (int i = 3; i < 31; i += 2)
+              m = lk::fmax3(m, __uint_as_float(sv[c2][i]), __uint_as_float(sv[c2][i + 1]));
+            mc[2 * h + c2] = fmaxf(m, __uint_as_float(sv[c2][31]));
+          }
+        }
+        const float mx = fmaxf(fmaxf(mc[0], mc[1]), fmaxf(mc[2], mc[3])) * sl2;
+        float new_m = m_used;
+        if (mx > m_used + kLazyRescale) new_m = mx;
+        const float alpha = (new_m == m_used) ? 1.f : lk::ex2_mufu(m_used - new_m);
+        const float ms = new_m == -INFINITY ? 0.f : new_m;
+        // Rescale O_u before any of P(j) is released (PV(j) accumulates onto
+        // it). O_u is stable here: S_u(j) was issued after PV_u(j-1), and
+        // s_full of tile j was committed after S_u(j). The warp rescales
+        // together if any of its rows needs it (tcgen05.ld / st are
+        // warp-collective); the first half's wait_st orders these stores
+        // before the release.
+        if (j > 0 && __any_sync(0xffffffffu, new_m != m_used)) {
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            uint32_t ov[32];
+            lk::tc::ld32(tO + lane_base + 32 * c4, ov);
+            lk::tc::wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+            lk::tc::st32(tO + lane_base + 32 * c4, ov);
+          }
+        }
+        // Pass 2: exponentials per 64-key half, P written over the half's
+        // first 32 columns and released half by half.
+        float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t sv[2][32];
+          load_half(h, sv);
+          uint32_t pw[32];
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            float x0, x1;
+            lk::ffma2(x0, x1, __uint_as_float(sv[c >> 4][(2 * c) & 31]),
+                      __uint_as_float(sv[c >> 4][(2 * c + 1) & 31]), sl2, sl2, -ms, -ms);
+            const float e0 = lk::ex2_mufu(x0);
+            const float e1 = lk::ex2_mufu(x1);
+            lk::fadd2(sum0, sum1, sum0, sum1, e0, e1);
+            pw[c] = lk::pack2<T>(e0, e1);
+          }
+          lk::tc::st32(tS + lane_base + 32 * h, pw);  // keys 64h.. -> P columns 32h..
+          lk::tc::wait_st();
+          lk::tc::fence_before();
+          __syncwarp();
+          if (lane == 0) lk::mbar_arrive(&p_full[u][h]);
+        }
+        l = l * alpha + (sum0 + sum1);
+        m_used = new_m;
+      }
+      // Next item's query rows travel while the last PV MMAs run; they go
+      // to shared memory after this item's output has left TMEM (the S MMA
+      // that reads them overwrites this sub-tile's S / P columns).
+      const int wn = next_item(n_items + 1, ok);
+      uint4 qv[16];
+      if (wn < num_items) load_q(item(wn), qv);
+      if (ok && lk::mbar_wait(&o_final, n_items & 1)) {
+        lk::tc::fence_after();
+        const float inv = 1.f / l;
+        T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(it.q_start + pos) * p.H * kD +
+                  static_cast<int64_t>(it.kvh * G + gh) * kD;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t ov[32];
+          lk::tc::ld32(tO + lane_base + 32 * c4, ov);  // whole warp, every row
+          lk::tc::wait_ld();
+          if (pos < it.q_len) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              uint32_t o4[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                o4[e] = lk::pack2<T>(__uint_as_float(ov[c * 8 + 2 * e]) * inv,
+                                     __uint_as_float(ov[c * 8 + 2 * e + 1]) * inv);
+              *reinterpret_cast<uint4*>(orow + c4 * 32 + c * 8) =
+                  make_uint4(o4[0], o4[1], o4[2], o4[3]);
+            }
+          }
+        }
+      } else {
+        ok = false;
+        if (p.status && lane == 0) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      ++n_items;
+      w = wn;
+      if (w < num_items && ok) {
+        lk::tc::fence_before();  // O reads done before the next item's MMAs
+        store_q(qv);
+      }
+    }
+  }
+  lk::tc::fence_before();
+  __syncthreads();
+  lk::tc::fence_after();
+  if (warp == 9) lk::tc::dealloc(tmem, 512);
+}
+
+// Work-item counter of the persistent kernel, one per (device, stream) so
+// that launches on different streams never share one; zeroed before each
+// launch on the launch stream.
+int* sched_counter(cudaStream_t s) {
+  struct Entry {
+    int dev;
+    cudaStream_t stream;
+    int* ptr;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> table;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const Entry& e : table)
+    if (e.dev == dev && e.stream == s) return e.ptr;
+  int* ptr = nullptr;
+  if (cudaMalloc(&ptr, 256) != cudaSuccess) return nullptr;
+  table.push_back({dev, s, ptr});
+  return ptr;
+}
+
+template <typename T>
+int launch_prefill_pp(const CUtensorMap& km, const CUtensorMap& vm, PrefillParams p,
+                      int num_seqs, int max_q_len, int H_kv, cudaStream_t s) {
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(paged_prefill_pp_kernel<T>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kPpSmem) != cudaSuccess)
+      return LK_ERR_CUDA;
+    configured[dev] = 1;
+  }
+  p.BQ = 256 / p.G;
+  p.nqt = (max_q_len + p.BQ - 1) / p.BQ;
+  p.sched = sched_counter(s);
+  if (p.sched == nullptr) return LK_ERR_CUDA;
+  if (cudaMemsetAsync(p.sched, 0, sizeof(int), s) != cudaSuccess) return LK_ERR_CUDA;
+  p.num_seqs = num_seqs;
+  p.H_kv = H_kv;
+  const int64_t items = static_cast<int64_t>(p.nqt) * H_kv * num_seqs;
+  if (items > 0x7fffffffLL) return LK_ERR_TOO_LARGE;
+  const int grid = static_cast<int>(items < lk::num_sms() ? items : lk::num_sms());
+  paged_prefill_pp_kernel<T><<<grid, kPpThreads, kPpSmem, s>>>(km, vm, p);
+  return lk::check_launch();
+}
+
+// Prefill kernel choice: the two-sub-tile ping-pong kernel by default;
+// LITEKERN_PREFILL_KERNEL=single selects the one-sub-tile kernel (read once).
+bool use_pingpong() {
+  static int v = [] {
+    const char* e = getenv("LITEKERN_PREFILL_KERNEL");
+    return (e && std::string(e) == "single") ? 0 : 1;
+  }();
+  return v != 0;
+}
+
 // mma.sync kernel instead of tcgen05 (LITEKERN_PREFILL_MMA_SYNC=1, read once).
 bool use_mma_sync() {
   static int v = [] {
@@ -768,6 +1273,11 @@ extern "C" int lk_paged_prefill(void* out, const void* q, int64_t q_token_stride
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = status;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!use_mma_sync() && use_pingpong()) {
+    if (dtype == LK_DTYPE_BF16)
+      return launch_prefill_pp<__nv_bfloat16>(km, vm, p, num_seqs, max_q_len, H_kv, s);
+    return launch_prefill_pp<__half>(km, vm, p, num_seqs, max_q_len, H_kv, s);
+  }
   if (!use_mma_sync()) {
     if (dtype == LK_DTYPE_BF16)
       return launch_prefill_tc<__nv_bfloat16>(km, vm, p, num_seqs, max_q_len, H_kv, s);
