@@ -111,6 +111,15 @@ LK_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns = k
   return true;
 }
 
+// 16-byte asynchronous global -> shared copy (cp.async, L2 only); with
+// valid = false the destination is zero-filled and nothing is read.
+LK_DEVINL void cp_async16(void* smem_dst, const void* gsrc, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)),
+               "l"(gsrc), "r"(valid ? 16 : 0)
+               : "memory");
+}
+LK_DEVINL void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // ------------------------------------------------------------------- TMA ---
 // 3-D tiled bulk-tensor load global -> shared, completion signalled on an
 // mbarrier via complete_tx. No multicast.
@@ -265,6 +274,18 @@ LK_DEVINL void named_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Named barrier that also ORs a predicate over the participating threads.
+LK_DEVINL bool named_sync_or(int id, int count, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %3, 0;\n\t"
+      "barrier.cta.red.or.pred p, %1, %2, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"(count), "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0;
+}
+
 LK_DEVINL float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -373,6 +394,19 @@ LK_DEVINL void st16(uint32_t taddr, const uint32_t (&r)[16]) {
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
       "r"(r[15])
       : "memory");
+}
+LK_DEVINL void ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+LK_DEVINL void st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(
+                   taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+               "r"(r[7])
+               : "memory");
 }
 LK_DEVINL void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 LK_DEVINL void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }

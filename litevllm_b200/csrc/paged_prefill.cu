@@ -991,21 +991,20 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
     const uint32_t tS = tmem + 128 * u, tO = tmem + 256 + 128 * u;
     uint8_t* dq = sQ + u * 2 * kTcQHalf;
     const float sl2 = p.scale_log2;
-    // Row t of an item's 256-row tile: position pos0 + t / G, head g = t % G.
-    auto load_q = [&](const Item& it, uint4 (&qv)[16]) {
-      const int pos = it.pos0 + t / G, g = t % G;
+    // Row t of an item's 256-row tile: position pos0 + t / G, head g = t % G,
+    // copied straight into the (128-byte swizzled) Q buffer with cp.async.
+    auto load_q = [&](const Item& it) {
+      const int pos = it.pos0 + t / G, gq = t % G;
+      const bool valid = pos < it.q_len;
       const T* qrow = static_cast<const T*>(p.q) +
-                      static_cast<int64_t>(it.q_start + pos) * p.q_stride +
-                      static_cast<int64_t>(it.kvh * G + g) * kD;
+                      static_cast<int64_t>(it.q_start + (valid ? pos : 0)) * p.q_stride +
+                      static_cast<int64_t>(it.kvh * G + gq) * kD;
 #pragma unroll
       for (int c = 0; c < 16; ++c)
-        qv[c] = pos < it.q_len ? *reinterpret_cast<const uint4*>(qrow + c * 8)
-                               : make_uint4(0u, 0u, 0u, 0u);
+        lk::cp_async16(dq + (c >> 3) * kTcQHalf + lk::swz128(r, c & 7), qrow + c * 8, valid);
     };
-    auto store_q = [&](const uint4 (&qv)[16]) {
-#pragma unroll
-      for (int c = 0; c < 16; ++c)
-        *reinterpret_cast<uint4*>(dq + (c >> 3) * kTcQHalf + lk::swz128(r, c & 7)) = qv[c];
+    auto publish_q = [&]() {
+      lk::cp_async_wait_all();
       lk::fence_proxy_async();
       __syncwarp();
       if (lane == 0) lk::mbar_arrive(&q_full[u]);
@@ -1014,9 +1013,8 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
     int g = 0, n_items = 0;
     int w = next_item(0, ok);
     if (w < num_items) {
-      uint4 qv[16];
-      load_q(item(w), qv);
-      store_q(qv);
+      load_q(item(w));
+      publish_q();
     }
     while (w < num_items && ok) {
       const Item it = item(w);
@@ -1106,13 +1104,16 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
         l = l * alpha + (sum0 + sum1);
         m_used = new_m;
       }
-      // Next item's query rows travel while the last PV MMAs run; they go
-      // to shared memory after this item's output has left TMEM (the S MMA
-      // that reads them overwrites this sub-tile's S / P columns).
+      // The next item's query rows go to the Q buffer (its only reader, S of
+      // this item's last tile, has completed) while the last PV MMAs run.
+      // They are published before this item's output leaves TMEM: the next
+      // S MMAs only touch the S / P columns, so they overlap the epilogue,
+      // and PV of the next item (which overwrites O) waits for P from these
+      // threads, i.e. for the end of the epilogue.
       const int wn = next_item(n_items + 1, ok);
-      uint4 qv[16];
-      if (wn < num_items) load_q(item(wn), qv);
+      if (wn < num_items) load_q(item(wn));
       if (ok && lk::mbar_wait(&o_final, n_items & 1)) {
+        if (wn < num_items) publish_q();
         lk::tc::fence_after();
         const float inv = 1.f / l;
         T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(it.q_start + pos) * p.H * kD +
@@ -1142,11 +1143,9 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
       ok = __all_sync(0xffffffffu, ok);
       ++n_items;
       w = wn;
-      if (w < num_items && ok) {
-        lk::tc::fence_before();  // O reads done before the next item's MMAs
-        store_q(qv);
-      }
+      lk::tc::fence_before();  // O reads done before P of the next item is released
     }
+    lk::cp_async_wait_all();  // nothing left in flight after a failed wait
   }
   lk::tc::fence_before();
   __syncthreads();
