@@ -559,7 +559,7 @@ def run_secondary(args, ws, rank, local):
                 "ms_per_step": round(ms, 4), "unit": "TFLOP/s",
                 "value": round(tf, 1),
                 "prefill": {"ms": round(pre_ms, 4), "tflops": round(tf, 1),
-                            "roofline": {"kernel": "paged_prefill_tc_kernel", "bound": "tensor",
+                            "roofline": {"kernel": "paged_prefill_pp_kernel", "bound": "tensor",
                                          "achieved": round(tf, 1), "peak": peak_tf,
                                          "peak_source": f"{tf_kind} bf16 burst", "unit": "TFLOP/s",
                                          "frac": round(tf / peak_tf, 4)}},

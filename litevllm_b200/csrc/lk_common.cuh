@@ -243,23 +243,6 @@ LK_DEVINL float exp2_fma(float x) {
   return x < -126.f ? 0.f : r;
 }
 
-// Two exponentials with the same polynomial on the packed fp32x2 pipe (no
-// select: inputs are clamped at -126, where the result is a denormal-sized
-// positive value, below anything a 16-bit probability can hold next to the
-// row maximum's 1.0).
-LK_DEVINL void exp2_fma2(float& r0, float& r1, float x0, float x1) {
-  const float a0 = fmaxf(x0, -126.f), a1 = fmaxf(x1, -126.f);
-  float y0, y1, t0, t1, f0, f1, q0, q1;
-  fadd2(y0, y1, a0, a1, 12582912.f, 12582912.f);
-  fadd2(t0, t1, y0, y1, -12582912.f, -12582912.f);
-  ffma2(f0, f1, t0, t1, -1.f, -1.f, a0, a1);  // a - round(a), exact
-  ffma2(q0, q1, f0, f1, 0.05746771767735481f, 0.05746771767735481f, 0.24254462122917175f,
-        0.24254462122917175f);
-  ffma2(q0, q1, q0, q1, f0, f1, 0.6928921341896057f, 0.6928921341896057f);
-  ffma2(q0, q1, q0, q1, f0, f1, 0.9999291300773621f, 0.9999291300773621f);
-  r0 = __int_as_float(__float_as_int(q0) + (__float_as_int(y0) << 23));
-  r1 = __int_as_float(__float_as_int(q1) + (__float_as_int(y1) << 23));
-}
 
 
 // Three-input fp32 max (sm_100).
@@ -274,17 +257,6 @@ LK_DEVINL void named_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-// Named barrier that also ORs a predicate over the participating threads.
-LK_DEVINL bool named_sync_or(int id, int count, bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %3, 0;\n\t"
-      "barrier.cta.red.or.pred p, %1, %2, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(r)
-      : "r"(id), "r"(count), "r"(static_cast<uint32_t>(v))
-      : "memory");
-  return r != 0;
-}
 
 LK_DEVINL float warp_max(float v) {
 #pragma unroll
@@ -394,19 +366,6 @@ LK_DEVINL void st16(uint32_t taddr, const uint32_t (&r)[16]) {
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
       "r"(r[15])
       : "memory");
-}
-LK_DEVINL void ld8(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
-                 "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
-LK_DEVINL void st8(uint32_t taddr, const uint32_t (&r)[8]) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(
-                   taddr),
-               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
-               "r"(r[7])
-               : "memory");
 }
 LK_DEVINL void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 LK_DEVINL void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
