@@ -80,3 +80,74 @@ def test_mixed_step_prefill_plus_decode(cuda):
     ref = pa.prefill(b.query.float(), b.key_cache.float(), b.value_cache.float(), b.block_tables,
                      b.context_lens, b.cu_seqlens_q, b.scale)
     assert_attn_close(out, ref)
+
+
+def test_prefill_many_ragged_items(cuda):
+    """Far more work items than SMs, ragged chunk lengths and priors: every
+    item is taken once from the persistent kernel's counter, and the query
+    hand-over between consecutive items of one CTA is exact."""
+    g = torch.Generator().manual_seed(11)
+    n = 40
+    q_lens = torch.randint(1, 700, (n,), generator=g).tolist()
+    prior = torch.randint(0, 1500, (n,), generator=g).tolist()
+    _paged_case(cuda, q_lens, prior, seed=11)
+
+
+def test_prefill_two_streams_concurrently(cuda):
+    """Launches on two streams run at the same time; each stream has its own
+    work-item counter."""
+    cases = []
+    for seed in (21, 22):
+        b = workloads.make_prefill_batch([300, 520, 64], [900, 10, 2000], seed=seed, device=cuda)
+        ops.store_kvcache(b.key, b.value, b.key_cache, b.value_cache, b.slot_mapping)
+        cases.append(b)
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    outs = []
+    for _ in range(3):
+        outs = []
+        for b, s in zip(cases, streams):
+            with torch.cuda.stream(s):
+                outs.append(ops.paged_prefill(b.query, b.key_cache, b.value_cache, b.cu_seqlens_q,
+                                              520, b.scale, block_tables=b.block_tables,
+                                              context_lens=b.context_lens))
+    torch.cuda.synchronize()
+    for b, out in zip(cases, outs):
+        ref = pa.prefill(b.query.float(), b.key_cache.float(), b.value_cache.float(),
+                         b.block_tables, b.context_lens, b.cu_seqlens_q, b.scale)
+        assert_attn_close(out, ref)
+
+
+def test_prefill_block_out_of_range_flags_status(cuda):
+    """A block id past the pool is reported (LK_STATUS_BLOCK_OOB) and read as
+    zeros instead of faulting; the other sequence is unaffected."""
+    b = workloads.make_prefill_batch([50, 50], [100, 100], seed=31, device=cuda)
+    ops.store_kvcache(b.key, b.value, b.key_cache, b.value_cache, b.slot_mapping)
+    bt = b.block_tables.clone()
+    bt[0, 2] = b.key_cache.shape[0] + 7
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = ops.paged_prefill(b.query, b.key_cache, b.value_cache, b.cu_seqlens_q, 50, b.scale,
+                            block_tables=bt, context_lens=b.context_lens, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) & 2  # LK_STATUS_BLOCK_OOB
+    ref = pa.prefill(b.query.float(), b.key_cache.float(), b.value_cache.float(), b.block_tables,
+                     b.context_lens, b.cu_seqlens_q, b.scale)
+    assert_attn_close(out[50:], ref[50:])
+
+
+@pytest.mark.parametrize("variant", ["LITEKERN_PREFILL_KERNEL=single",
+                                     "LITEKERN_PREFILL_KERNEL=pingpong",
+                                     "LITEKERN_PREFILL_MMA_SYNC=1"])
+def test_prefill_kernel_options(variant):
+    """The kernels kept as options (chosen once per process from the
+    environment) against the oracle, in a child process."""
+    import os
+    import subprocess
+    import sys
+    key, val = variant.split("=")
+    env = dict(os.environ, **{key: val})
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-m", "tests.prefill_variant_check"], cwd=root, env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert "ok" in r.stdout
