@@ -570,6 +570,15 @@ def run_secondary(args, ws, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def _decode_launches(num_splits: int) -> int:
+    """Kernels one ops.paged_decode call launches (mirrors the library's
+    LITEKERN_DECODE_ORDER switch: the longest-first ordering kernel runs before
+    the split kernel unless it is set to 0; the persistent kernel is one)."""
+    if num_splits < 0 or os.environ.get("LITEKERN_DECODE_ORDER", "1").strip() == "0":
+        return 1
+    return 2
+
+
 def main():
     args = parse()
     ws, rank, local = dist_env()
@@ -623,7 +632,9 @@ def main():
             "traffic": profiled_traffic(),
             "algorithmic_bytes_per_launch": dec_b,
         },
-        "gpu_launches": r["K"] * (2 * args.layers + 1),
+        # per layer: store, decode ordering + decode (one launch when the
+        # ordering kernel is switched off or the persistent kernel runs); sampler
+        "gpu_launches": r["K"] * ((1 + _decode_launches(r["nsplit"])) * args.layers + 1),
         "clocks": r["clocks"],
     }
     if r["e2e"]:

@@ -46,7 +46,65 @@ struct DecodeParams {
   int32_t* status;
   float* part_ml;         // [B][num_splits][H][2]  (m in log2 domain, l)
   float* part_o;          // [B][num_splits][H][D]
+  const int2* order;      // [B * num_splits]: (b * num_splits + split, ctx), longest first
 };
+
+// Launch order of the split kernel's (sequence, split) units: longest first.
+// The hardware hands CTAs to SMs in blockIdx order; with units of up to 64
+// stages (4 MB of K/V) dispatched in sequence order, the last wave leaves
+// SMs idle for tens of microseconds. One CTA buckets the units by stage
+// count (64 buckets, longest bucket first, empty contexts last) and writes
+// the list; CTA i of the decode kernel takes entry i. Order within a bucket
+// is arbitrary; results do not depend on it (each unit's partial has a fixed
+// slot and the merge reads them in split order).
+constexpr int kOrderBuckets = 64;
+
+__global__ void __launch_bounds__(1024) decode_order_kernel(const int32_t* context_lens, int B,
+                                                            int cap, int spp, int num_splits,
+                                                            int2* order) {
+  __shared__ int hist[kOrderBuckets + 1];
+  __shared__ int cursor[kOrderBuckets + 1];
+  __shared__ int total;
+  for (int i = threadIdx.x; i <= kOrderBuckets; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  auto bucket = [&](int n) {
+    return n <= 0 ? kOrderBuckets
+                  : (kOrderBuckets - 1) -
+                        static_cast<int>(static_cast<int64_t>(n - 1) * kOrderBuckets / spp);
+  };
+  auto stages = [&](int b) {
+    int ctx = context_lens[b];
+    ctx = ctx < 0 ? 0 : (ctx > cap ? cap : ctx);
+    return (ctx + kTok - 1) / kTok;
+  };
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    const int nst = stages(b);
+    const int nsp = nst == 0 ? 1 : (nst + spp - 1) / spp;
+    for (int sp = 0; sp < nsp; ++sp)
+      atomicAdd(&hist[bucket(nst == 0 ? 0 : min(spp, nst - sp * spp))], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int i = 0; i <= kOrderBuckets; ++i) {
+      cursor[i] = acc;
+      acc += hist[i];
+    }
+    total = acc;
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    const int nst = stages(b);
+    const int nsp = nst == 0 ? 1 : (nst + spp - 1) / spp;
+    const int ctx_raw = context_lens[b];
+    for (int sp = 0; sp < nsp; ++sp) {
+      const int pos = atomicAdd(&cursor[bucket(nst == 0 ? 0 : min(spp, nst - sp * spp))], 1);
+      order[pos] = make_int2(b * num_splits + sp, ctx_raw);
+    }
+  }
+  for (int i = total + threadIdx.x; i < B * num_splits; i += blockDim.x)
+    order[i] = make_int2(-1, 0);
+}
 
 template <int HPC, int NST> struct DecodeShape {
   static constexpr int kBoxBytes = HPC * kTok * 128;  // HPC heads x 16 slots x 64 values
@@ -74,11 +132,19 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
 
-  const int sp = blockIdx.x, hg = blockIdx.y, b = blockIdx.z;
+  int2 unit;
+  if (p.order != nullptr) {
+    unit = p.order[blockIdx.x];
+    if (unit.x < 0) return;
+  } else {
+    const int bb = blockIdx.x / p.num_splits;
+    unit = make_int2(blockIdx.x, p.context_lens[bb]);
+  }
+  const int sp = unit.x % p.num_splits, hg = blockIdx.y, b = unit.x / p.num_splits;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.G;
 
-  int ctx = p.context_lens[b];
+  int ctx = unit.y;
   const int cap = p.max_blocks * p.bs;
   if (ctx > cap) {
     if (threadIdx.x == 0 && sp == 0) atomicOr(p.status, LK_STATUS_CTX_OOB);
@@ -342,18 +408,77 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
   const int nq = HPC * G;
   const int qbase = hg * nq;
   const int64_t rowb = static_cast<int64_t>(b) * p.num_splits;
-  for (int i = threadIdx.x; i < nq * kD; i += Shape::kThreads) {
-    const int qh = qbase + i / kD, d = i % kD;
-    float M = -INFINITY;
-    for (int s = 0; s < nsp; ++s) M = fmaxf(M, __ldcg(p.part_ml + ((rowb + s) * p.H + qh) * 2));
-    float L = 0.f, acc = 0.f;
-    for (int s = 0; s < nsp; ++s) {
-      const float* ml = p.part_ml + ((rowb + s) * p.H + qh) * 2;
-      const float w = exp2f(__ldcg(ml) - M);
-      L += __ldcg(ml + 1) * w;
-      acc += __ldcg(p.part_o + ((rowb + s) * p.H + qh) * kD + d) * w;
+  if (nq * nsp * 4 <= Shape::kSmem - 1024) {
+    // Weights w[q][s] = exp2(m_s - M) / L into the (idle) ring once, then
+    // every split's partial rows as float4 with all loads of a thread in
+    // flight together: the merge is a few L2 round trips, not one per output.
+    float* w = reinterpret_cast<float*>(smem);
+    for (int q = threadIdx.x; q < nq; q += Shape::kThreads) {
+      const float* ml = p.part_ml + (rowb * p.H + qbase + q) * 2;
+      float M = -INFINITY;
+      for (int s2 = 0; s2 < nsp; ++s2) M = fmaxf(M, __ldcg(ml + s2 * p.H * 2));
+      float L = 0.f;
+      for (int s2 = 0; s2 < nsp; ++s2) {
+        const float e = exp2f(__ldcg(ml + s2 * p.H * 2) - M);
+        w[q * nsp + s2] = e;
+        L += __ldcg(ml + s2 * p.H * 2 + 1) * e;
+      }
+      const float inv = 1.f / L;
+      for (int s2 = 0; s2 < nsp; ++s2) w[q * nsp + s2] *= inv;
     }
-    store_out<T>(out + qh * kD + d, acc / L);
+    __syncthreads();
+    constexpr int kU = 4;
+    const int n4 = nq * kD / 4;
+    const float4* po4 = reinterpret_cast<const float4*>(p.part_o + (rowb * p.H + qbase) * kD);
+    const int64_t sstride4 = static_cast<int64_t>(p.H) * kD / 4;
+    for (int i0 = threadIdx.x; i0 < n4; i0 += kU * Shape::kThreads) {
+      float4 acc[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+      for (int s2 = 0; s2 < nsp; ++s2) {
+        float4 v[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int i = i0 + u * Shape::kThreads;
+          v[u] = i < n4 ? __ldcg(po4 + s2 * sstride4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int i = i0 + u * Shape::kThreads;
+          const float wt = i < n4 ? w[(i * 4 / kD) * nsp + s2] : 0.f;
+          acc[u].x += v[u].x * wt;
+          acc[u].y += v[u].y * wt;
+          acc[u].z += v[u].z * wt;
+          acc[u].w += v[u].w * wt;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int i = i0 + u * Shape::kThreads;
+        if (i < n4) {
+          T* o = out + qbase * kD + i * 4;
+          store_out<T>(o, acc[u].x);
+          store_out<T>(o + 1, acc[u].y);
+          store_out<T>(o + 2, acc[u].z);
+          store_out<T>(o + 3, acc[u].w);
+        }
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < nq * kD; i += Shape::kThreads) {
+      const int qh = qbase + i / kD, d = i % kD;
+      float M = -INFINITY;
+      for (int s = 0; s < nsp; ++s) M = fmaxf(M, __ldcg(p.part_ml + ((rowb + s) * p.H + qh) * 2));
+      float L = 0.f, acc = 0.f;
+      for (int s = 0; s < nsp; ++s) {
+        const float* ml = p.part_ml + ((rowb + s) * p.H + qh) * 2;
+        const float wt = exp2f(__ldcg(ml) - M);
+        L += __ldcg(ml + 1) * wt;
+        acc += __ldcg(p.part_o + ((rowb + s) * p.H + qh) * kD + d) * wt;
+      }
+      store_out<T>(out + qh * kD + d, acc / L);
+    }
   }
   if (threadIdx.x == 0) p.counters[b * p.num_groups + hg] = 0;
 }
@@ -797,7 +922,14 @@ int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, const DecodePara
       return LK_ERR_CUDA;
     configured[dev] = 1;
   }
-  dim3 grid(p.num_splits, p.num_groups, B);
+  if (p.order != nullptr) {
+    decode_order_kernel<<<1, 1024, 0, s>>>(p.context_lens, B, p.max_blocks * p.bs,
+                                           p.stages_per_split, p.num_splits,
+                                           const_cast<int2*>(p.order));
+    const int rc = lk::check_launch();
+    if (rc != LK_OK) return rc;
+  }
+  dim3 grid(B * p.num_splits, p.num_groups);
   paged_decode_kernel<T, HPC, NST><<<grid, Shape::kThreads, Shape::kSmem, s>>>(km, vm, p);
   return lk::check_launch();
 }
@@ -854,6 +986,16 @@ int prefetch_distance() {
   return d;
 }
 
+// Longest-first launch order for the split kernel (LITEKERN_DECODE_ORDER=0
+// launches units in sequence order without the ordering kernel; read once).
+bool order_units() {
+  static int v = [] {
+    const char* e = getenv("LITEKERN_DECODE_ORDER");
+    return e && atoi(e) == 0 ? 0 : 1;
+  }();
+  return v != 0;
+}
+
 // CTAs of the persistent kernel: one per SM (its shared-memory ring takes the SM).
 // LITEKERN_DECODE_GRID (read once) overrides it, for tuning.
 int persistent_grid() {
@@ -873,11 +1015,11 @@ extern "C" int lk_paged_decode_num_splits(int32_t B, int32_t H_kv, int32_t max_b
   const int64_t max_stages = (static_cast<int64_t>(max_blocks_per_seq) * block_size + 15) / 16;
   const int64_t units = static_cast<int64_t>(B) * groups;
   // Measured on B200 (config 2: B=256, contexts <= 4096; config 5: B=8..64,
-  // contexts 32K-128K): fewer, longer CTAs stream faster than many short
-  // ones. A split holds at least 64 stages (1024 tokens) and long contexts
-  // are cut into about 16 splits.
+  // contexts 32K-128K), with units launched longest first: fewer, longer
+  // CTAs stream faster than many short ones. A split holds at least 128
+  // stages (2048 tokens) and long contexts are cut into about 24 splits.
   (void)units;
-  const int64_t spp = std::max<int64_t>(64, (max_stages + 15) / 16);
+  const int64_t spp = std::max<int64_t>(128, (max_stages + 23) / 24);
   int64_t splits = (max_stages + spp - 1) / spp;
   splits = std::max<int64_t>(1, std::min<int64_t>(splits, max_stages));
   return static_cast<int>(std::min<int64_t>(splits, 65535));
@@ -893,9 +1035,12 @@ extern "C" size_t lk_paged_decode_workspace_bytes(int32_t B, int32_t H, int32_t 
     const size_t slots = 2 * static_cast<size_t>(persistent_grid());
     bytes += align256(slots * H * 2 * 4);
     bytes += align256(slots * H * D * 4);
-  } else if (num_splits > 1) {
-    bytes += align256(static_cast<size_t>(B) * num_splits * H * 2 * 4);
-    bytes += align256(static_cast<size_t>(B) * num_splits * H * D * 4);
+  } else {
+    if (num_splits > 1) {
+      bytes += align256(static_cast<size_t>(B) * num_splits * H * 2 * 4);
+      bytes += align256(static_cast<size_t>(B) * num_splits * H * D * 4);
+    }
+    bytes += align256(static_cast<size_t>(B) * std::max(num_splits, 1) * sizeof(int2));
   }
   return bytes;
 }
@@ -963,6 +1108,11 @@ extern "C" int lk_paged_decode(void* out, int64_t out_token_stride, const void* 
   const size_t ml_rows = persistent ? 2 * static_cast<size_t>(persistent_grid())
                                     : static_cast<size_t>(B) * num_splits;
   p.part_o = reinterpret_cast<float*>(ws + cnt_bytes + align256(ml_rows * H * 2 * 4));
+  const size_t part_bytes = (persistent || num_splits > 1)
+                                ? align256(ml_rows * H * 2 * 4) + align256(ml_rows * H * kD * 4)
+                                : 0;
+  p.order = reinterpret_cast<const int2*>(ws + cnt_bytes + part_bytes);
+  if (!order_units()) p.order = nullptr;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (persistent) {
     const int units = B * p.num_groups;

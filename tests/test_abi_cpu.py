@@ -74,14 +74,15 @@ def test_argument_validation_without_launch():
 
 def test_workspace_sizes_and_split_plan():
     lib = _lib.lib()
-    assert lib.lk_paged_decode_workspace_bytes(256, 32, 8, 128, 1) == 256 + 65536 * 4
+    # one split: status + counters + the launch-order list (8 bytes per unit)
+    assert lib.lk_paged_decode_workspace_bytes(256, 32, 8, 128, 1) == 256 + 65536 * 4 + 256 * 8
     w4 = lib.lk_paged_decode_workspace_bytes(256, 32, 8, 128, 4)
     assert w4 >= 256 * 4 * 32 * (128 + 2) * 4
     # long contexts split; a single short sequence per SM-wave does not over-split
-    assert lib.lk_paged_decode_num_splits(8, 8, 8192, 16) == 16
+    assert lib.lk_paged_decode_num_splits(8, 8, 8192, 16) == 24
     assert lib.lk_paged_decode_workspace_bytes(8, 32, 8, 128, -1) > 256 + 65536 * 4
     assert lib.lk_paged_decode_num_splits(256, 8, 4, 16) == 1
-    assert lib.lk_paged_decode_num_splits(256, 8, 256, 16) == 4
+    assert lib.lk_paged_decode_num_splits(256, 8, 256, 16) == 2
     assert lib.lk_sample_workspace_bytes(8, 151936) > 0
 
 
