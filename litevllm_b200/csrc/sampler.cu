@@ -135,55 +135,20 @@ LK_DEVINL void scan_chunk(const SampleParams& p, int b, int v0, int v1, float te
   if constexpr (VEC && !std::is_same<T, float>::value) {
     const int vend = v0 + ((min(v1, p.V) - v0) / kVec) * kVec;
     constexpr int kU = 4;
-    int v = v0 + threadIdx.x * kVec;
-    for (; v + (kU - 1) * kSampThreads * kVec < vend; v += kU * kSampThreads * kVec) {
-      uint4 raw[kU];
-#pragma unroll
-      for (int u = 0; u < kU; ++u)
-        raw[u] = __ldcs(reinterpret_cast<const uint4*>(row + v + u * kSampThreads * kVec));
-#pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        float f[8];
-        Load16<T>::cvt(raw[u], f);
-        const int vv = v + u * kSampThreads * kVec;
-        float g[8];
-        if constexpr (MODE == 1) {
-          const float4 a = __ldcs(reinterpret_cast<const float4*>(nrow + vv));
-          const float4 c = __ldcs(reinterpret_cast<const float4*>(nrow + vv + 4));
-          g[0] = a.x; g[1] = a.y; g[2] = a.z; g[3] = a.w;
-          g[4] = c.x; g[5] = c.y; g[6] = c.z; g[7] = c.w;
-        } else if constexpr (MODE == 2) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const U4 r = philox4x32_10(U4{static_cast<uint32_t>((vv >> 2) + h),
-                                          static_cast<uint32_t>(b), p.off_lo, p.off_hi},
-                                       p.seed_lo, p.seed_hi);
-            g[4 * h + 0] = gumbel_from_bits(r.x);
-            g[4 * h + 1] = gumbel_from_bits(r.y);
-            g[4 * h + 2] = gumbel_from_bits(r.z);
-            g[4 * h + 3] = gumbel_from_bits(r.w);
-          }
-          if (drow) {
-            reinterpret_cast<float4*>(drow + vv)[0] = make_float4(g[0], g[1], g[2], g[3]);
-            reinterpret_cast<float4*>(drow + vv)[1] = make_float4(g[4], g[5], g[6], g[7]);
-          }
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) visit(f[e], vv + e, MODE == 0 ? 0.f : g[e]);
-      }
-    }
-    for (; v < vend; v += kSampThreads * kVec) {
-      const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(row + v));
+    // One 16-byte vector of logits at element vv (its noise loaded or drawn here).
+    auto process = [&](const uint4& raw, int vv) {
       float f[8];
       Load16<T>::cvt(raw, f);
       float g[8];
       if constexpr (MODE == 1) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) g[e] = nrow[v + e];
+        const float4 a = __ldcs(reinterpret_cast<const float4*>(nrow + vv));
+        const float4 c = __ldcs(reinterpret_cast<const float4*>(nrow + vv + 4));
+        g[0] = a.x; g[1] = a.y; g[2] = a.z; g[3] = a.w;
+        g[4] = c.x; g[5] = c.y; g[6] = c.z; g[7] = c.w;
       } else if constexpr (MODE == 2) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const U4 r = philox4x32_10(U4{static_cast<uint32_t>((v >> 2) + h),
+          const U4 r = philox4x32_10(U4{static_cast<uint32_t>((vv >> 2) + h),
                                         static_cast<uint32_t>(b), p.off_lo, p.off_hi},
                                      p.seed_lo, p.seed_hi);
           g[4 * h + 0] = gumbel_from_bits(r.x);
@@ -192,12 +157,30 @@ LK_DEVINL void scan_chunk(const SampleParams& p, int b, int v0, int v1, float te
           g[4 * h + 3] = gumbel_from_bits(r.w);
         }
         if (drow) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) drow[v + e] = g[e];
+          reinterpret_cast<float4*>(drow + vv)[0] = make_float4(g[0], g[1], g[2], g[3]);
+          reinterpret_cast<float4*>(drow + vv)[1] = make_float4(g[4], g[5], g[6], g[7]);
         }
       }
 #pragma unroll
-      for (int e = 0; e < 8; ++e) visit(f[e], v + e, MODE == 0 ? 0.f : g[e]);
+      for (int e = 0; e < 8; ++e) visit(f[e], vv + e, MODE == 0 ? 0.f : g[e]);
+    };
+    constexpr int kS = kSampThreads * kVec;
+    int v = v0 + threadIdx.x * kVec;
+    for (; v + (kU - 1) * kS < vend; v += kU * kS) {
+      uint4 raw[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) raw[u] = __ldcs(reinterpret_cast<const uint4*>(row + v + u * kS));
+#pragma unroll
+      for (int u = 0; u < kU; ++u) process(raw[u], v + u * kS);
+    }
+    if (v < vend) {  // fewer than kU vectors left: one predicated batch
+      uint4 raw[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        if (v + u * kS < vend) raw[u] = __ldcs(reinterpret_cast<const uint4*>(row + v + u * kS));
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        if (v + u * kS < vend) process(raw[u], v + u * kS);
     }
     vs = vend;
   }
@@ -436,8 +419,19 @@ __global__ void __launch_bounds__(kSampThreads, kMinBlocks) argmax_kernel(const 
 #pragma unroll
     for (int u = 0; u < kU; ++u) argmax_vec<T>(raw[u], v + u * kStride, best, besti);
   }
-  for (; v < vend; v += kStride)
-    argmax_vec<T>(__ldcs(reinterpret_cast<const uint4*>(row + v)), v, best, besti);
+  if (v < vend) {
+    // fewer than kU vectors left for this thread: one predicated batch, all
+    // loads in flight together (a one-load-per-iteration loop here costs a
+    // memory round trip per vector)
+    uint4 raw[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (v + u * kStride < vend)
+        raw[u] = __ldcs(reinterpret_cast<const uint4*>(row + v + u * kStride));
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (v + u * kStride < vend) argmax_vec<T>(raw[u], v + u * kStride, best, besti);
+  }
   for (int t = vend + threadIdx.x; t < v1; t += kSampThreads) {
     const float x = lk::Elem<T>::to_f(row[t]);
     if (beats_later(x, best)) {
