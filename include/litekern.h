@@ -51,6 +51,7 @@ extern "C" {
 #define LK_STATUS_BLOCK_OOB 2      /* block table entry outside [0, num_blocks) */
 #define LK_STATUS_WAIT_TIMEOUT 4   /* a bounded mbarrier wait gave up */
 #define LK_STATUS_CTX_OOB 8        /* context_len larger than the block table */
+#define LK_STATUS_TOKEN_OOB 16     /* a past token id outside [-V, V) */
 
 /* Library version (major*10000 + minor*100 + patch). */
 int lk_version(void);
@@ -263,6 +264,22 @@ int lk_sample_noalloc(int64_t* out_ids, const void* logits, int32_t B, int32_t V
                       const float* temperatures, const float* noise, int64_t noise_ld,
                       uint64_t seed, uint64_t offset, float* noise_dump, int32_t dtype,
                       void* stream);
+
+/*
+ * Repetition penalty in place, replacing _apply_repetition_penalty
+ * (litevllm/layers/sampler.py:190-201) as Sampler.sample applies it
+ * (:168-171, on a clone of the logits): for each row b with
+ * penalties[b] != 1, every distinct id among past_token_ids[b, 0..L) (int64,
+ * row stride past_ld; negative ids index from the end of the row) gets
+ * s > 0 ? s / penalty : s * penalty, computed in fp32 and rounded once to the
+ * logits dtype (fp32, f16, bf16; [B, V], row stride ld). Ids outside
+ * [-V, V) are skipped and flagged LK_STATUS_TOKEN_OOB in *status (may be
+ * NULL); the reference raises IndexError for them.
+ */
+int lk_repetition_penalty(void* logits, int32_t B, int32_t V, int64_t ld,
+                          const int64_t* past_token_ids, int64_t past_ld, int32_t L,
+                          const float* penalties, int32_t* status, int32_t dtype,
+                          void* stream);
 
 int lk_softmax_temp(float* probs, int64_t probs_ld, const void* logits, int32_t B,
                     int32_t V, int64_t ld, const float* temperatures, int32_t dtype,

@@ -20,6 +20,7 @@ LK_STATUS_SLOT_OOB = 1
 LK_STATUS_BLOCK_OOB = 2
 LK_STATUS_WAIT_TIMEOUT = 4
 LK_STATUS_CTX_OOB = 8
+LK_STATUS_TOKEN_OOB = 16
 
 # name -> (restype, argtypes)
 SIGNATURES: dict[str, tuple] = {
@@ -73,6 +74,11 @@ SIGNATURES: dict[str, tuple] = {
         [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64,
          c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float, c_int32,
          c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p],
+    ),
+    "lk_repetition_penalty": (
+        c_int32,
+        [c_void_p, c_int32, c_int32, c_int64, c_void_p, c_int64, c_int32, c_void_p, c_void_p,
+         c_int32, c_void_p],
     ),
     "lk_softmax_temp": (
         c_int32,

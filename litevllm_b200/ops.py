@@ -398,6 +398,47 @@ def softmax_temp(logits: torch.Tensor, temperatures: torch.Tensor) -> torch.Tens
     return probs
 
 
+def repetition_penalty_(
+    logits: torch.Tensor,
+    past_token_ids: torch.Tensor,
+    penalty,
+    status: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """In place: each distinct id of past_token_ids[b] gets s / p if s > 0 else
+    s * p on row b of logits, p = penalty (a float, or fp32 [B] per row; 1.0
+    leaves the row alone). The reference's _apply_repetition_penalty
+    (litevllm/layers/sampler.py:190-201) on a caller-owned tensor."""
+    if logits.dim() == 1:
+        logits = logits.unsqueeze(0)
+    if past_token_ids.dim() == 1:
+        past_token_ids = past_token_ids.unsqueeze(0)
+    dev = _cuda(logits, past_token_ids, status)
+    B, V = logits.shape
+    if logits.stride(1) != 1:
+        raise ValueError("logits must have unit column stride")
+    code = _dtype_code(logits, (torch.float32, torch.float16, torch.bfloat16))
+    past = past_token_ids.to(device=dev, dtype=torch.int64)
+    if past.shape[0] != B:
+        raise ValueError("past_token_ids must have one row per logits row")
+    if past.shape[1] > 0 and past.stride(1) != 1:
+        past = past.contiguous()
+    if isinstance(penalty, torch.Tensor):
+        pens = penalty.to(device=dev, dtype=torch.float32).contiguous()
+        if pens.numel() != B:
+            raise ValueError("per-row penalties must have B entries")
+    else:
+        pens = torch.full((B,), float(penalty), dtype=torch.float32, device=dev)
+    with _on(dev):
+        check(
+            lib().lk_repetition_penalty(
+                logits.data_ptr(), B, V, logits.stride(0), past.data_ptr(),
+                past.stride(0) if past.shape[1] > 0 else 0, past.shape[1], pens.data_ptr(),
+                _ptr(status), code, _stream(dev),
+            )
+        )
+    return logits
+
+
 # ------------------------------------------------ norm + RoPE + KV store ---
 def rope_store_kvcache(
     query: torch.Tensor,

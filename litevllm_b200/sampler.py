@@ -3,8 +3,8 @@
 `Sampler.sample(logits, sampling_params, past_token_ids=None)` keeps the
 reference signature (litevllm/layers/sampler.py:147-187):
 
-* repetition penalty -> same arithmetic as the reference (:190-201), torch ops
-  on the GPU;
+* repetition penalty -> liblitekern fused kernel on a clone of the logits, the
+  reference's arithmetic and dedupe (:190-201);
 * temperature 0 -> liblitekern greedy argmax (replaces _argmax_kernel);
 * top-k / top-p -> fused liblitekern filter + Gumbel-max draw for 16-bit
   logits (same kept set and distribution as :204-225); fp32 logits use
@@ -26,14 +26,6 @@ from typing import Optional
 import torch
 
 from . import ops
-
-
-def _apply_repetition_penalty(logits, past_token_ids, penalty):
-    for i in range(logits.shape[0]):
-        unique_ids = past_token_ids[i].unique()
-        score = logits[i, unique_ids]
-        logits[i, unique_ids] = torch.where(score > 0, score / penalty, score * penalty)
-    return logits
 
 
 def _apply_top_k_top_p(probs, top_k, top_p):
@@ -73,8 +65,9 @@ class Sampler:
         if logits.dim() == 1:
             logits = logits.unsqueeze(0)
         if past_token_ids is not None and sampling_params.repetition_penalty != 1.0:
-            logits = _apply_repetition_penalty(
-                logits.clone(), past_token_ids, sampling_params.repetition_penalty
+            logits = ops.repetition_penalty_(
+                logits.clone(memory_format=torch.contiguous_format), past_token_ids,
+                sampling_params.repetition_penalty,
             )
         B = logits.shape[0]
         T = float(sampling_params.temperature)

@@ -7,6 +7,10 @@ greedy():  argmax over fp32 logits, first index wins ties — the reference's
 gumbel():  argmax(fp32(x) / T + g) with IEEE fp32 division and addition,
            first index on ties: the Gumbel-max form of the temperature branch
            (:178 softmax(x / T), :187 categorical draw) for a given noise g.
+repetition_penalty(): _apply_repetition_penalty (sampler.py:190-201): each
+           distinct past id (negative ids index from the row's end) of a row
+           gets s / p if s > 0 else s * p, in fp32 (IEEE, p as fp32), rounded
+           to the logits dtype ("f32", "bf16" round-to-nearest-even).
 philox4x32_10(): Philox4x32-10 (Salmon et al., SC'11), the generator the
            sampler kernel uses for in-kernel noise; uniform_bits_to_u()
            restates its bits -> u mapping.
@@ -119,3 +123,24 @@ def filtered_gumbel(logits, temperature: float, top_k: int, top_p: float, noise)
     key = (x / np.float32(temperature)).astype(np.float32) + np.asarray(noise, np.float32)
     key = np.where(kept, key.astype(np.float32), -np.inf)
     return int(np.argmax(key))
+
+
+def round_bf16(x) -> np.ndarray:
+    """fp32 -> nearest bf16 (ties to even), returned as fp32 values."""
+    b = np.asarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    r = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16) << 16
+    return r.astype(np.uint32).view(np.float32)
+
+
+def repetition_penalty(logits, past, penalty: float, dtype: str = "f32") -> np.ndarray:
+    """Restates _apply_repetition_penalty (sampler.py:190-201) row by row."""
+    out = np.array(logits, dtype=np.float32, copy=True)
+    V = out.shape[1]
+    p = np.float32(penalty)
+    for i in range(out.shape[0]):
+        ids = np.asarray(past[i], dtype=np.int64)
+        ids = np.unique(np.where(ids < 0, ids + V, ids))
+        s = out[i, ids]
+        v = np.where(s > 0, s / p, s * p).astype(np.float32)
+        out[i, ids] = round_bf16(v) if dtype == "bf16" else v
+    return out

@@ -19,6 +19,10 @@ seeded inputs, what its own functions return:
   sampler.npz        Sampler.sample greedy ids (litevllm/layers/sampler.py:151-175)
                      with planted ties, and the temperature softmax the reference
                      computes before its multinomial draw (:178 / :133-135).
+  penalty.npz        _apply_repetition_penalty (sampler.py:190-201) on fp32 and bf16
+                     logits for penalties 1.3 and 0.8, past ids with duplicates and
+                     negative (wrapping) ids, and Sampler.sample's greedy ids after it
+                     (:168-175). Written by penalty_fixture() (own generator).
 
 Inputs are stored next to outputs (bf16 inputs as uint16 bit patterns), so
 the fixtures do not depend on any random generator.
@@ -145,7 +149,34 @@ def main(ref_root: str) -> None:
         q_out=q_ref.float().numpy(), k_out=k_ref.float().numpy(),
         q_out_dtype=str(q_ref.dtype),
     )
+    penalty_fixture(ref_root)
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
+
+
+def penalty_fixture(ref_root: str) -> None:
+    sys.path.insert(0, ref_root)
+    from litevllm.config import SamplingParams
+    from litevllm.layers.sampler import Sampler, _apply_repetition_penalty
+
+    g = torch.Generator().manual_seed(20261201)
+    B, V, L = 4, 1000, 12
+    logits = torch.randn((B, V), generator=g) * 3.0
+    past = torch.randint(0, V, (B, L), generator=g)
+    past[0, 3] = past[0, 7] = past[0, 1]     # duplicates: penalised once
+    past[1, 0] = -1                          # wraps to V - 1
+    past[1, 5] = -V                          # wraps to 0
+    past[2, :] = 42                          # one id only
+    logits[2, 42] = 0.0                      # score 0: multiplied (not > 0)
+    logits[3, past[3, 0]] = 80.0             # the row's max, penalised
+    out = {"logits": logits.numpy(), "past": past.numpy(),
+           "logits_bf16": bf16_bits(logits.bfloat16())}
+    for tag, pen in (("p13", 1.3), ("p08", 0.8)):
+        out[f"{tag}_f32"] = _apply_repetition_penalty(logits.clone(), past, pen).numpy()
+        out[f"{tag}_bf16"] = bf16_bits(_apply_repetition_penalty(logits.bfloat16(), past, pen))
+        out[f"{tag}_greedy"] = Sampler.sample(
+            logits, SamplingParams(temperature=0.0, repetition_penalty=pen, max_tokens=8),
+            past_token_ids=past).numpy()
+    np.savez_compressed(HERE / "penalty.npz", **out)
 
 
 if __name__ == "__main__":

@@ -144,3 +144,55 @@ def test_workspace_reused_across_batch_shapes(cuda):
         x = torch.randn((B, V), device=cuda).bfloat16()
         got = ops.sample(x).cpu().numpy()
         assert np.array_equal(got, osamp.greedy(x.float().cpu().numpy())), (B, V)
+
+
+@pytest.mark.parametrize("tag,pen", [("p13", 1.3), ("p08", 0.8)])
+def test_repetition_penalty_matches_reference_golden(cuda, tag, pen):
+    """Fused penalty vs the reference's _apply_repetition_penalty: bit-exact on
+    fp32 and bf16 logits; Sampler.sample with past ids gives the reference's
+    greedy ids."""
+    d = golden_io.load("penalty.npz")
+    past = torch.from_numpy(d["past"]).to(cuda)
+    x = torch.from_numpy(d["logits"]).to(cuda)
+    got = ops.repetition_penalty_(x.clone(), past, pen).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), d[f"{tag}_f32"].view(np.uint32))
+    xb = golden_io.bf16(d["logits_bf16"]).to(cuda)
+    gotb = ops.repetition_penalty_(xb.clone(), past, pen).cpu().view(torch.int16).numpy()
+    assert np.array_equal(gotb.view(np.uint16), d[f"{tag}_bf16"])
+    ids = Sampler.sample(x, SP(temperature=0.0, repetition_penalty=pen), past_token_ids=past)
+    assert np.array_equal(ids.cpu().numpy(), d[f"{tag}_greedy"])
+    assert torch.equal(x, torch.from_numpy(d["logits"]).to(cuda))  # caller's logits untouched
+
+
+@pytest.mark.parametrize("dtype,tag", [(torch.float32, "f32"), (torch.bfloat16, "bf16"),
+                                       (torch.float16, "f16")])
+def test_repetition_penalty_per_row_and_large(cuda, dtype, tag):
+    """Per-row penalties (1.0 leaves a row alone), long histories with many
+    duplicates, a vocabulary of 151936, against the oracle."""
+    g = torch.Generator().manual_seed(77)
+    B, V, L = 6, 151936, 3000
+    x = (torch.randn((B, V), generator=g) * 4).to(dtype)
+    past = torch.randint(-V, V, (B, L), generator=g)
+    past[:, ::7] = past[:, :1]  # many repeats of one id
+    pens = torch.tensor([1.3, 1.0, 0.7, 2.0, 1.05, 1.0])
+    got = ops.repetition_penalty_(x.to(cuda), past.to(cuda), pens.to(cuda)).float().cpu().numpy()
+    want = x.float().numpy().copy()
+    for b in range(B):
+        if pens[b].item() != 1.0:
+            row = osamp.repetition_penalty(x[b:b + 1].float().numpy(), past[b:b + 1].numpy(),
+                                           pens[b].item(), "bf16" if tag == "bf16" else "f32")
+            if tag == "f16":
+                row = row.astype(np.float16).astype(np.float32)
+            want[b] = row[0]
+    assert np.array_equal(got, want)
+
+
+def test_repetition_penalty_out_of_range_ids_flagged(cuda):
+    x = torch.randn((2, 100), device=cuda)
+    past = torch.tensor([[3, 100, 5], [-101, 7, 7]], device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    want = osamp.repetition_penalty(x.cpu().numpy(), [[3, 5], [7]], 1.5)
+    got = ops.repetition_penalty_(x.clone(), past, 1.5, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) & 16  # LK_STATUS_TOKEN_OOB
+    assert np.array_equal(got.cpu().numpy(), want)

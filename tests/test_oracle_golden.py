@@ -135,3 +135,18 @@ def test_rope_oracle_matches_reference():
     eps = float(d["eps"])
     assert torch.equal(orope.norm_rope(q, cos, sin, qw, eps), torch.from_numpy(d["q_out"]))
     assert torch.equal(orope.norm_rope(k, cos, sin, kw, eps), torch.from_numpy(d["k_out"]))
+
+
+@pytest.mark.parametrize("tag,pen", [("p13", 1.3), ("p08", 0.8)])
+def test_repetition_penalty_oracle_matches_reference(tag, pen):
+    """The oracle's penalty is bit-exact with the reference's
+    _apply_repetition_penalty on fp32 and bf16 logits (duplicates, negative
+    ids, a zero score, the row max penalised)."""
+    d = golden_io.load("penalty.npz")
+    got = osamp.repetition_penalty(d["logits"], d["past"], pen, "f32")
+    assert np.array_equal(got.view(np.uint32), d[f"{tag}_f32"].view(np.uint32))
+    lb = (d["logits_bf16"].astype(np.uint32) << 16).view(np.float32)
+    got = osamp.repetition_penalty(lb, d["past"], pen, "bf16")
+    assert np.array_equal(got.view(np.uint32) >> 16, d[f"{tag}_bf16"].astype(np.uint32))
+    assert np.array_equal(osamp.greedy(osamp.repetition_penalty(d["logits"], d["past"], pen)),
+                          d[f"{tag}_greedy"])
