@@ -392,14 +392,26 @@ LK_DEVINL int first_index_of(const uint4& raw, float vm) {
   return e;
 }
 
+// Running best over 16-byte vectors: only the value and the START of the
+// first vector that holds it are kept (strict comparison, increasing order);
+// the element inside that vector is found once, at the end, by
+// resolve_index. Searching it on every improvement costs more than the
+// whole scan: the compiler if-converts the search into every iteration.
 template <typename T>
 LK_DEVINL void argmax_vec(const uint4& raw, int base, float& best, int& besti) {
   const uint32_t m = pmax_nan<T>(pmax_nan<T>(raw.x, raw.y), pmax_nan<T>(raw.z, raw.w));
   const float vm = fmax_nan(half_lo<T>(m), half_hi<T>(m));
   if (beats_later(vm, best)) {
-    besti = base + first_index_of<T>(raw, vm);
+    besti = base;
     best = vm;
   }
+}
+
+// Vector start -> index of the first element equal to best (one reload).
+template <typename T>
+LK_DEVINL void resolve_index(const T* row, float best, int& besti) {
+  if (besti == 0x7fffffff) return;
+  besti += first_index_of<T>(__ldg(reinterpret_cast<const uint4*>(row + besti)), best);
 }
 
 template <typename T, int kU, int kMinBlocks, bool kCluster>
@@ -432,6 +444,7 @@ __global__ void __launch_bounds__(kSampThreads, kMinBlocks) argmax_kernel(const 
     for (int u = 0; u < kU; ++u)
       if (v + u * kStride < vend) argmax_vec<T>(raw[u], v + u * kStride, best, besti);
   }
+  resolve_index<T>(row, best, besti);
   for (int t = vend + threadIdx.x; t < v1; t += kSampThreads) {
     const float x = lk::Elem<T>::to_f(row[t]);
     if (beats_later(x, best)) {
@@ -552,6 +565,7 @@ __global__ void __launch_bounds__(kSampThreads) argmax_bulk_kernel(const SampleP
       issue(t + kNS, s);
     }
   }
+  resolve_index<T>(row, best, besti);
   for (int t = vend + threadIdx.x; t < v1; t += kSampThreads) {
     const float x = lk::Elem<T>::to_f(row[t]);
     if (beats_later(x, best)) {
