@@ -392,26 +392,27 @@ LK_DEVINL int first_index_of(const uint4& raw, float vm) {
   return e;
 }
 
-// Running best over 16-byte vectors: only the value and the START of the
-// first vector that holds it are kept (strict comparison, increasing order);
-// the element inside that vector is found once, at the end, by
-// resolve_index. Searching it on every improvement costs more than the
-// whole scan: the compiler if-converts the search into every iteration.
+// Running best over 16-byte vectors: the value, the START of the first
+// vector that holds it (strict comparison, increasing order) and that vector
+// itself; the element inside it is found once, at the end, by resolve_index.
+// Searching it on every improvement costs more than the whole scan: the
+// compiler if-converts the search into every iteration.
 template <typename T>
-LK_DEVINL void argmax_vec(const uint4& raw, int base, float& best, int& besti) {
+LK_DEVINL void argmax_vec(const uint4& raw, int base, float& best, int& besti, uint4& braw) {
   const uint32_t m = pmax_nan<T>(pmax_nan<T>(raw.x, raw.y), pmax_nan<T>(raw.z, raw.w));
   const float vm = fmax_nan(half_lo<T>(m), half_hi<T>(m));
   if (beats_later(vm, best)) {
     besti = base;
     best = vm;
+    braw = raw;
   }
 }
 
-// Vector start -> index of the first element equal to best (one reload).
+// Vector start -> index of the first element equal to best.
 template <typename T>
-LK_DEVINL void resolve_index(const T* row, float best, int& besti) {
+LK_DEVINL void resolve_index(const uint4& braw, float best, int& besti) {
   if (besti == 0x7fffffff) return;
-  besti += first_index_of<T>(__ldg(reinterpret_cast<const uint4*>(row + besti)), best);
+  besti += first_index_of<T>(braw, best);
 }
 
 template <typename T, int kU, int kMinBlocks, bool kCluster>
@@ -421,6 +422,7 @@ __global__ void __launch_bounds__(kSampThreads, kMinBlocks) argmax_kernel(const 
   const T* row = static_cast<const T*>(p.logits) + static_cast<int64_t>(b) * p.ld;
   float best = -INFINITY;
   int besti = 0x7fffffff;
+  uint4 braw = make_uint4(0u, 0u, 0u, 0u);
   const int vend = v0 + ((v1 - v0) / kVec) * kVec;
   constexpr int kStride = kSampThreads * kVec;
   int v = v0 + threadIdx.x * kVec;
@@ -429,7 +431,7 @@ __global__ void __launch_bounds__(kSampThreads, kMinBlocks) argmax_kernel(const 
 #pragma unroll
     for (int u = 0; u < kU; ++u) raw[u] = __ldcs(reinterpret_cast<const uint4*>(row + v + u * kStride));
 #pragma unroll
-    for (int u = 0; u < kU; ++u) argmax_vec<T>(raw[u], v + u * kStride, best, besti);
+    for (int u = 0; u < kU; ++u) argmax_vec<T>(raw[u], v + u * kStride, best, besti, braw);
   }
   if (v < vend) {
     // fewer than kU vectors left for this thread: one predicated batch, all
@@ -442,9 +444,9 @@ __global__ void __launch_bounds__(kSampThreads, kMinBlocks) argmax_kernel(const 
         raw[u] = __ldcs(reinterpret_cast<const uint4*>(row + v + u * kStride));
 #pragma unroll
     for (int u = 0; u < kU; ++u)
-      if (v + u * kStride < vend) argmax_vec<T>(raw[u], v + u * kStride, best, besti);
+      if (v + u * kStride < vend) argmax_vec<T>(raw[u], v + u * kStride, best, besti, braw);
   }
-  resolve_index<T>(row, best, besti);
+  resolve_index<T>(braw, best, besti);
   for (int t = vend + threadIdx.x; t < v1; t += kSampThreads) {
     const float x = lk::Elem<T>::to_f(row[t]);
     if (beats_later(x, best)) {
@@ -550,6 +552,7 @@ __global__ void __launch_bounds__(kSampThreads) argmax_bulk_kernel(const SampleP
     for (int t = 0; t < kNS && t < tiles; ++t) issue(t, t);
   float best = -INFINITY;
   int besti = 0x7fffffff;
+  uint4 braw = make_uint4(0u, 0u, 0u, 0u);
   for (int t = 0; t < tiles; ++t) {
     const int s = t % kNS;
     if (!lk::mbar_wait(&full[s], (t / kNS) & 1)) break;  // bounded; never expected
@@ -558,14 +561,14 @@ __global__ void __launch_bounds__(kSampThreads) argmax_bulk_kernel(const SampleP
     const int vbase = v0 + t * kTileVec * kVec;
 #pragma unroll 4
     for (int i = threadIdx.x; i < nv; i += kSampThreads)
-      argmax_vec<T>(tile[i], vbase + i * kVec, best, besti);
+      argmax_vec<T>(tile[i], vbase + i * kVec, best, besti, braw);
     __syncthreads();
     if (threadIdx.x == 0 && t + kNS < tiles) {
       lk::fence_proxy_async();
       issue(t + kNS, s);
     }
   }
-  resolve_index<T>(row, best, besti);
+  resolve_index<T>(braw, best, besti);
   for (int t = vend + threadIdx.x; t < v1; t += kSampThreads) {
     const float x = lk::Elem<T>::to_f(row[t]);
     if (beats_later(x, best)) {
