@@ -165,3 +165,22 @@ def test_decode_shared_prefix_with_cow_fork(cuda):
     ref_b = workloads.make_prefix_batch(B=128, seed=1, device=cuda)  # torch fork
     assert torch.equal(b.key_cache, ref_b.key_cache) and torch.equal(b.value_cache, ref_b.value_cache)
     _check(b, rows=[0, 1, 64, 127])
+
+
+@pytest.mark.parametrize("variant", ["LITEKERN_DECODE_ORDER=0", "LITEKERN_DECODE_HEADS_PER_CTA=4",
+                                     "LITEKERN_DECODE_HEADS_PER_CTA=2",
+                                     "LITEKERN_DECODE_HEADS_PER_CTA=1",
+                                     "LITEKERN_DECODE_PREFETCH=8"])
+def test_decode_kernel_options(variant):
+    """The decode options (read once per process from the environment)
+    against the oracle, in a child process."""
+    import os
+    import subprocess
+    import sys
+    key, val = variant.split("=")
+    env = dict(os.environ, **{key: val})
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-m", "tests.decode_variant_check"], cwd=root, env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert "ok" in r.stdout

@@ -196,3 +196,20 @@ def test_repetition_penalty_out_of_range_ids_flagged(cuda):
     torch.cuda.synchronize()
     assert int(status.item()) & 16  # LK_STATUS_TOKEN_OOB
     assert np.array_equal(got.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("variant", ["LITEKERN_SAMPLE_UNROLL=0", "LITEKERN_SAMPLE_UNROLL=4",
+                                     "LITEKERN_SAMPLE_UNROLL=16", "LITEKERN_SAMPLE_CHUNKS=5"])
+def test_sampler_kernel_options(variant):
+    """The greedy kernels kept as options (chosen once per process from the
+    environment) against the oracle, in a child process."""
+    import os
+    import subprocess
+    import sys
+    key, val = variant.split("=")
+    env = dict(os.environ, **{key: val})
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-m", "tests.sampler_variant_check"], cwd=root, env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert "ok" in r.stdout
