@@ -257,6 +257,18 @@ LK_DEVINL void named_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Named barrier that also ANDs a predicate over the participating threads.
+LK_DEVINL bool named_sync_and(int id, int count, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %3, 0;\n\t"
+      "barrier.cta.red.and.pred p, %1, %2, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"(count), "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0;
+}
+
 
 LK_DEVINL float warp_max(float v) {
 #pragma unroll

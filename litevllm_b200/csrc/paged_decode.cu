@@ -47,6 +47,7 @@ struct DecodeParams {
   float* part_ml;         // [B][num_splits][H][2]  (m in log2 domain, l)
   float* part_o;          // [B][num_splits][H][D]
   const int2* order;      // [B * num_splits]: (b * num_splits + split, ctx), longest first
+  int* work;              // streaming kernel's unit counter (zeroed by the ordering kernel)
 };
 
 // Launch order of the split kernel's (sequence, split) units: longest first.
@@ -61,7 +62,8 @@ constexpr int kOrderBuckets = 64;
 
 __global__ void __launch_bounds__(1024) decode_order_kernel(const int32_t* context_lens, int B,
                                                             int cap, int spp, int num_splits,
-                                                            int2* order) {
+                                                            int2* order, int* work) {
+  if (threadIdx.x == 0 && work) *work = 0;
   __shared__ int hist[kOrderBuckets + 1];
   __shared__ int cursor[kOrderBuckets + 1];
   __shared__ int total;
@@ -885,6 +887,349 @@ constexpr int64_t kMaxCounters = 65536;
 constexpr size_t kHeadBytes = 256 + kMaxCounters * 4;
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
+// ------------------------------------------------------------------------
+// Streaming split decode (the default): one CTA per SM takes (sequence,
+// split, head group) units, longest first, from the list decode_order_kernel
+// writes, through a counter that kernel zeroes. The producer warp publishes
+// each unit to the consumer warps through a 4-deep descriptor ring and keeps
+// the TMA stage ring streaming across unit boundaries, so a unit's block-table
+// reads and first loads overlap the previous unit's last stages: no CTA launch,
+// barrier setup or pipeline refill per unit. Splits write (m, l, o) partials and
+// the consumer warps of the last unit of a (sequence, head group) to finish
+// merge them, as in the split kernel (weights in shared memory, float4 loads).
+constexpr int kStreamUnits = 4;        // unit descriptor ring depth
+constexpr int kStreamMergeMax = 4096;  // (query head, split) weights held in shared memory
+
+template <typename T, int HPC, int NST>
+__global__ void __launch_bounds__((HPC + 1) * 32, 1)
+paged_decode_stream_kernel(const __grid_constant__ CUtensorMap kmap,
+                           const __grid_constant__ CUtensorMap vmap, const DecodeParams p,
+                           int num_entries) {
+  using Shape = DecodeShape<HPC, NST>;
+  constexpr int kCons = HPC * 32;  // consumer threads
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[NST];
+  __shared__ __align__(8) uint64_t empty_bar[NST];
+  __shared__ __align__(8) uint64_t unit_full[kStreamUnits];
+  __shared__ __align__(8) uint64_t unit_empty[kStreamUnits];
+  __shared__ int4 unit_ring[kStreamUnits];  // b, split, ctx, head group (b < 0: no more work)
+  __shared__ float s_w[kStreamMergeMax];
+  __shared__ int s_last;
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.G, groups = p.num_groups;
+  const int spp = p.stages_per_split;
+  const int cap = p.max_blocks * p.bs;
+  const int total = num_entries * groups;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < NST; ++s) {
+      lk::mbar_init(&full_bar[s], 1);
+      lk::mbar_init(&empty_bar[s], HPC);
+    }
+#pragma unroll
+    for (int s = 0; s < kStreamUnits; ++s) {
+      lk::mbar_init(&unit_full[s], 1);
+      lk::mbar_init(&unit_empty[s], HPC);
+    }
+    lk::fence_barrier_init();
+  }
+  __syncthreads();
+
+  // Stages of a unit: [st0, st1) of the sequence's ceil(ctx / 16) stages.
+  auto stage_range = [&](int ctx, int sp, int& st0, int& st1) {
+    int c = ctx > cap ? cap : (ctx < 0 ? 0 : ctx);
+    const int nst = (c + kTok - 1) / kTok;
+    st0 = sp * spp;
+    st1 = min(nst, st0 + spp);
+  };
+
+  if (warp == HPC) {
+    // ------------------------------------------------------- producer ---
+    if (lane == 0) {
+      lk::prefetch_tensormap(&kmap);
+      lk::prefetch_tensormap(&vmap);
+    }
+    const int64_t num_slots = p.num_blocks * p.bs;
+    const int oob = static_cast<int>(num_slots < 0x7fffffffLL ? num_slots : 0x7fffffffLL);
+    bool ok = true;
+    int it = 0;
+    for (int n = 0; ok; ++n) {
+      int idx = 0;
+      if (lane == 0) idx = atomicAdd(p.work, 1);
+      idx = __shfl_sync(0xffffffffu, idx, 0);
+      int4 u = make_int4(-1, 0, 0, 0);
+      if (idx < total) {
+        const int2 e = p.order[idx / groups];
+        if (e.x >= 0) u = make_int4(e.x / p.num_splits, e.x % p.num_splits, e.y, idx % groups);
+      }
+      if (lane == 0) {
+        const int s = n % kStreamUnits;
+        if (lk::mbar_wait(&unit_empty[s], ((n / kStreamUnits) & 1) ^ 1)) {
+          unit_ring[s] = u;
+          lk::mbar_arrive(&unit_full[s]);
+        } else {
+          atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
+          ok = false;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok || u.x < 0) break;
+      int st0, st1;
+      stage_range(u.z, u.y, st0, st1);
+      const int32_t* bt = p.block_tables + static_cast<int64_t>(u.x) * p.bt_stride;
+      const int h0 = u.w * HPC;
+      auto lookup = [&](int st) -> int {
+        if (st >= st1) return -1;
+        const int pos = st * kTok;
+        const int blk = __ldg(bt + pos / p.bs);
+        if (blk < 0 || blk >= p.num_blocks) {
+          atomicOr(p.status, LK_STATUS_BLOCK_OOB);
+          return oob;  // past the end: TMA reads zeros
+        }
+        return blk * p.bs + (pos % p.bs);
+      };
+      int nxt = lookup(st0 + lane);
+      for (int base = st0; base < st1 && ok; base += 32) {
+        const int cur = nxt;
+        nxt = lookup(base + 32 + lane);
+        const int cnt = min(32, st1 - base);
+        for (int i = 0; i < cnt; ++i, ++it) {
+          const int slot = __shfl_sync(0xffffffffu, cur, i);
+          if (lane == 0) {
+            const int s = it % NST;
+            if (!lk::mbar_wait(&empty_bar[s], ((it / NST) & 1) ^ 1)) {
+              atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
+              ok = false;
+            } else {
+              lk::mbar_arrive_expect_tx(&full_bar[s], Shape::kStageBytes);
+              uint8_t* dst = smem + s * Shape::kStageBytes;
+              lk::tma_load_3d(dst, &kmap, &full_bar[s], 0, slot, h0);
+              lk::tma_load_3d(dst + Shape::kBoxBytes, &kmap, &full_bar[s], 64, slot, h0);
+              lk::tma_load_3d(dst + 2 * Shape::kBoxBytes, &vmap, &full_bar[s], 0, slot, h0);
+              lk::tma_load_3d(dst + 3 * Shape::kBoxBytes, &vmap, &full_bar[s], 64, slot, h0);
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+          if (!ok) break;
+        }
+      }
+    }
+    return;
+  }
+
+  // ----------------------------------------------------------- consumers ---
+  const int g = lane >> 2, c = lane & 3;
+  const float sl2 = p.scale_log2;
+  bool ok = true;
+  int it = 0;
+  for (int n = 0;; ++n) {
+    int4 u = make_int4(-1, 0, 0, 0);
+    {
+      const int s = n % kStreamUnits;
+      if (ok && lk::mbar_wait(&unit_full[s], (n / kStreamUnits) & 1)) {
+        u = unit_ring[s];
+      } else {
+        ok = false;
+      }
+      __syncwarp();
+      if (lane == 0) lk::mbar_arrive(&unit_empty[s]);
+    }
+    // All consumer warps leave together (a warp that left alone would strand
+    // the others at the merge's named barriers).
+    ok = lk::named_sync_and(1, kCons, ok);
+    if (!ok || u.x < 0) break;
+    const int b = u.x, sp = u.y, hg = u.w;
+    if (u.z > cap && sp == 0 && threadIdx.x == 0) atomicOr(p.status, LK_STATUS_CTX_OOB);
+    int st0, st1;
+    stage_range(u.z, sp, st0, st1);
+    const int nst = (min(max(u.z, 0), cap) + kTok - 1) / kTok;
+    const int nsp = nst == 0 ? 1 : (nst + spp - 1) / spp;
+    T* out = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride;
+    const int kvh = hg * HPC + warp;
+    const int qh0 = kvh * G;
+    if (nst == 0) {
+      // softmax over an all -inf row is NaN in the reference; reproduce it.
+      for (int i = lane; i < G * kD; i += 32)
+        store_out<T>(out + qh0 * kD + i, __int_as_float(0x7fc00000));
+      continue;
+    }
+    uint32_t qb[8][2];
+    {
+      const T* qrow = static_cast<const T*>(p.q) + static_cast<int64_t>(b) * p.q_stride +
+                      static_cast<int64_t>(qh0 + g) * kD;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        qb[ks][0] = g < G ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * c) : 0u;
+        qb[ks][1] = g < G ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * c) : 0u;
+      }
+    }
+    DecodeState st;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) st.o[mt][0] = st.o[mt][1] = st.o[mt][2] = st.o[mt][3] = 0.f;
+    st.m0 = st.m1 = -INFINITY;
+    st.l0 = st.l1 = 0.f;
+    const uint32_t wbase = lk::smem_u32(smem) + warp * (kTok * 128);
+    for (int t = st0; t < st1; ++t, ++it) {
+      const int s = it % NST;
+      if (ok && !lk::mbar_wait(&full_bar[s], (it / NST) & 1)) {
+        if (lane == 0) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
+        ok = false;
+      }
+      if (ok) {
+        const uint32_t kb = wbase + s * Shape::kStageBytes;
+        decode_stage<T, Shape::kBoxBytes>(st, qb, kb, kb + 2 * Shape::kBoxBytes, t * kTok, u.z,
+                                          sl2, lane);
+      }
+      __syncwarp();
+      if (lane == 0) lk::mbar_arrive(&empty_bar[s]);
+    }
+    float l0 = st.l0, l1 = st.l1;
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    const int n0 = 2 * c, n1 = 2 * c + 1;
+    if (nsp == 1) {
+      const float r0 = 1.f / l0, r1 = 1.f / l1;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int d = mt * 16 + g;
+        if (n0 < G) {
+          store_out<T>(out + (qh0 + n0) * kD + d, st.o[mt][0] * r0);
+          store_out<T>(out + (qh0 + n0) * kD + d + 8, st.o[mt][2] * r0);
+        }
+        if (n1 < G) {
+          store_out<T>(out + (qh0 + n1) * kD + d, st.o[mt][1] * r1);
+          store_out<T>(out + (qh0 + n1) * kD + d + 8, st.o[mt][3] * r1);
+        }
+      }
+      continue;
+    }
+    const int64_t prow = (static_cast<int64_t>(b) * p.num_splits + sp) * p.H;
+    float* po = p.part_o + prow * kD;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      const int d = mt * 16 + g;
+      if (n0 < G) {
+        po[(qh0 + n0) * kD + d] = st.o[mt][0];
+        po[(qh0 + n0) * kD + d + 8] = st.o[mt][2];
+      }
+      if (n1 < G) {
+        po[(qh0 + n1) * kD + d] = st.o[mt][1];
+        po[(qh0 + n1) * kD + d + 8] = st.o[mt][3];
+      }
+    }
+    if (g == 0) {
+      float* pml = p.part_ml + prow * 2;
+      if (n0 < G) {
+        pml[(qh0 + n0) * 2] = st.m0;
+        pml[(qh0 + n0) * 2 + 1] = l0;
+      }
+      if (n1 < G) {
+        pml[(qh0 + n1) * 2] = st.m1;
+        pml[(qh0 + n1) * 2 + 1] = l1;
+      }
+    }
+    // Last unit of this (sequence, head group) to finish merges the splits.
+    __threadfence();
+    lk::named_sync(1, kCons);
+    if (threadIdx.x == 0) {
+      const int prev = atomicAdd(p.counters + b * groups + hg, 1);
+      s_last = (prev == nsp - 1);
+    }
+    lk::named_sync(1, kCons);
+    if (!s_last) continue;
+    __threadfence();
+    const int nq = HPC * G, qbase = hg * nq;
+    const int64_t rowb = static_cast<int64_t>(b) * p.num_splits;
+    if (nq * nsp <= kStreamMergeMax) {
+      for (int q = threadIdx.x; q < nq; q += kCons) {
+        const float* ml = p.part_ml + (rowb * p.H + qbase + q) * 2;
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < nsp; ++s2) M = fmaxf(M, __ldcg(ml + s2 * p.H * 2));
+        float L = 0.f;
+        for (int s2 = 0; s2 < nsp; ++s2) {
+          const float e = exp2f(__ldcg(ml + s2 * p.H * 2) - M);
+          s_w[q * nsp + s2] = e;
+          L += __ldcg(ml + s2 * p.H * 2 + 1) * e;
+        }
+        const float inv = 1.f / L;
+        for (int s2 = 0; s2 < nsp; ++s2) s_w[q * nsp + s2] *= inv;
+      }
+      lk::named_sync(1, kCons);
+      constexpr int kU = 4;
+      const int n4 = nq * kD / 4;
+      const float4* po4 = reinterpret_cast<const float4*>(p.part_o + (rowb * p.H + qbase) * kD);
+      const int64_t sstride4 = static_cast<int64_t>(p.H) * kD / 4;
+      for (int i0 = threadIdx.x; i0 < n4; i0 += kU * kCons) {
+        float4 acc[kU];
+#pragma unroll
+        for (int k = 0; k < kU; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int s2 = 0; s2 < nsp; ++s2) {
+          float4 v[kU];
+#pragma unroll
+          for (int k = 0; k < kU; ++k) {
+            const int i = i0 + k * kCons;
+            v[k] = i < n4 ? __ldcg(po4 + s2 * sstride4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int k = 0; k < kU; ++k) {
+            const int i = i0 + k * kCons;
+            const float wt = i < n4 ? s_w[(i * 4 / kD) * nsp + s2] : 0.f;
+            acc[k].x += v[k].x * wt;
+            acc[k].y += v[k].y * wt;
+            acc[k].z += v[k].z * wt;
+            acc[k].w += v[k].w * wt;
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < kU; ++k) {
+          const int i = i0 + k * kCons;
+          if (i < n4) {
+            T* o = out + qbase * kD + i * 4;
+            store_out<T>(o, acc[k].x);
+            store_out<T>(o + 1, acc[k].y);
+            store_out<T>(o + 2, acc[k].z);
+            store_out<T>(o + 3, acc[k].w);
+          }
+        }
+      }
+      lk::named_sync(1, kCons);  // s_w is rewritten by the next merge
+    } else {
+      for (int i = threadIdx.x; i < nq * kD; i += kCons) {
+        const int qh = qbase + i / kD, d = i % kD;
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < nsp; ++s2)
+          M = fmaxf(M, __ldcg(p.part_ml + ((rowb + s2) * p.H + qh) * 2));
+        float L = 0.f, acc = 0.f;
+        for (int s2 = 0; s2 < nsp; ++s2) {
+          const float* ml = p.part_ml + ((rowb + s2) * p.H + qh) * 2;
+          const float wt = exp2f(__ldcg(ml) - M);
+          L += __ldcg(ml + 1) * wt;
+          acc += __ldcg(p.part_o + ((rowb + s2) * p.H + qh) * kD + d) * wt;
+        }
+        store_out<T>(out + qh * kD + d, acc / L);
+      }
+    }
+    if (threadIdx.x == 0) p.counters[b * groups + hg] = 0;
+  }
+}
+
+// Streaming persistent split kernel instead of one CTA per unit
+// (LITEKERN_DECODE_STREAM, read once; 1 = on).
+bool stream_units() {
+  static int v = [] {
+    const char* e = getenv("LITEKERN_DECODE_STREAM");
+    return e && atoi(e) == 1 ? 1 : 0;
+  }();
+  return v != 0;
+}
+
 // KV heads per CTA: the largest of 8, 4, 2, 1 that divides H_kv, capped by the
 // LITEKERN_DECODE_HEADS_PER_CTA environment variable (read once; a tuning knob).
 int heads_cap() {
@@ -925,9 +1270,24 @@ int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, const DecodePara
   if (p.order != nullptr) {
     decode_order_kernel<<<1, 1024, 0, s>>>(p.context_lens, B, p.max_blocks * p.bs,
                                            p.stages_per_split, p.num_splits,
-                                           const_cast<int2*>(p.order));
+                                           const_cast<int2*>(p.order), p.work);
     const int rc = lk::check_launch();
     if (rc != LK_OK) return rc;
+  }
+  if (p.order != nullptr && stream_units()) {
+    static int configured_s[64] = {0};
+    if (dev >= 0 && dev < 64 && !configured_s[dev]) {
+      if (cudaFuncSetAttribute(paged_decode_stream_kernel<T, HPC, NST>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               Shape::kSmem) != cudaSuccess)
+        return LK_ERR_CUDA;
+      configured_s[dev] = 1;
+    }
+    const int64_t units = static_cast<int64_t>(B) * p.num_splits * p.num_groups;
+    const int grid = static_cast<int>(units < lk::num_sms() ? units : lk::num_sms());
+    paged_decode_stream_kernel<T, HPC, NST>
+        <<<grid, Shape::kThreads, Shape::kSmem, s>>>(km, vm, p, B * p.num_splits);
+    return lk::check_launch();
   }
   dim3 grid(B * p.num_splits, p.num_groups);
   paged_decode_kernel<T, HPC, NST><<<grid, Shape::kThreads, Shape::kSmem, s>>>(km, vm, p);
@@ -1112,6 +1472,7 @@ extern "C" int lk_paged_decode(void* out, int64_t out_token_stride, const void* 
                                 ? align256(ml_rows * H * 2 * 4) + align256(ml_rows * H * kD * 4)
                                 : 0;
   p.order = reinterpret_cast<const int2*>(ws + cnt_bytes + part_bytes);
+  p.work = reinterpret_cast<int*>(ws + 64);  // in the 256-byte status header
   if (!order_units()) p.order = nullptr;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (persistent) {
