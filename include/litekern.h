@@ -95,6 +95,9 @@ int lk_store_kv(const void* key, const void* value, void* k_cache, void* v_cache
  * fixed offset and every completed call leaves it zero again, so one
  * workspace serves consecutive calls of any shape on one stream. Calls that
  * overlap on the GPU must not share a workspace. B * (H_kv / 8) <= 65536.
+ * With num_splits >= 1 the call launches two kernels: a one-CTA ordering
+ * kernel writes the (sequence, split) units longest first into the workspace
+ * (8 bytes per unit), and the decode kernel's CTA i takes unit i.
  */
 int lk_paged_decode_num_splits(int32_t B, int32_t H_kv, int32_t max_blocks_per_seq,
                                int32_t block_size);
