@@ -170,17 +170,30 @@ LK_DEVINL void scan_chunk(const SampleParams& p, int b, int v0, int v1, float te
       uint4 raw[kU];
 #pragma unroll
       for (int u = 0; u < kU; ++u) raw[u] = __ldcs(reinterpret_cast<const uint4*>(row + v + u * kS));
+      if constexpr (MODE == 2) {
+        // in-kernel noise is compute-bound: one copy of the (large) body keeps
+        // the loop in the instruction cache
+#pragma unroll 1
+        for (int u = 0; u < kU; ++u) process(raw[u], v + u * kS);
+      } else {
 #pragma unroll
-      for (int u = 0; u < kU; ++u) process(raw[u], v + u * kS);
+        for (int u = 0; u < kU; ++u) process(raw[u], v + u * kS);
+      }
     }
     if (v < vend) {  // fewer than kU vectors left: one predicated batch
       uint4 raw[kU];
 #pragma unroll
       for (int u = 0; u < kU; ++u)
         if (v + u * kS < vend) raw[u] = __ldcs(reinterpret_cast<const uint4*>(row + v + u * kS));
+      if constexpr (MODE == 2) {
+#pragma unroll 1
+        for (int u = 0; u < kU; ++u)
+          if (v + u * kS < vend) process(raw[u], v + u * kS);
+      } else {
 #pragma unroll
-      for (int u = 0; u < kU; ++u)
-        if (v + u * kS < vend) process(raw[u], v + u * kS);
+        for (int u = 0; u < kU; ++u)
+          if (v + u * kS < vend) process(raw[u], v + u * kS);
+      }
     }
     vs = vend;
   }
