@@ -108,3 +108,17 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "absent.so")
     with pytest.raises(_lib.LiteKernError, match="no fallback"):
         _lib.lib()
+
+
+def test_repetition_penalty_rejects_bad_arguments():
+    lib = _lib.lib()
+    # B = 0 or L = 0: nothing to do
+    assert lib.lk_repetition_penalty(None, 0, 10, 10, None, 0, 0, None, None, 2, None) == 0
+    assert lib.lk_repetition_penalty(1, 2, 10, 10, 1, 4, 0, 1, None, 2, None) == 0
+    # row stride shorter than the row, history stride shorter than its length
+    assert lib.lk_repetition_penalty(1, 2, 10, 9, 1, 4, 4, 1, None, 2, None) == -1
+    assert lib.lk_repetition_penalty(1, 2, 10, 10, 1, 3, 4, 1, None, 2, None) == -1
+    # missing pointers, unknown dtype
+    assert lib.lk_repetition_penalty(None, 2, 10, 10, 1, 4, 4, 1, None, 2, None) == -1
+    assert lib.lk_repetition_penalty(1, 2, 10, 10, 1, 4, 4, None, None, 2, None) == -1
+    assert lib.lk_repetition_penalty(1, 2, 10, 10, 1, 4, 4, 1, None, 7, None) == -2
