@@ -114,6 +114,35 @@ int lk_paged_decode(void* out, int64_t out_token_stride,
                     int32_t dtype, void* stream);
 
 /*
+ * Decode for a batch whose rows all begin with the same prefix_tokens tokens
+ * (block_tables[b][0 .. prefix_tokens / block_size) equal to row 0's, as the
+ * reference's PrefixCache hands out shared blocks): the same result as
+ * lk_paged_decode (it restates Attention._decode_fast, attention.py:91-139),
+ * computed as the prefix part once for all rows -- every row's G query heads
+ * of a KV head against the prefix keys on the tensor cores, in key ranges --
+ * plus each row's own suffix on the split decode kernel, merged by log-sum-exp.
+ * No counterpart in the reference (its decode re-reads the shared blocks per
+ * row). Requires context_lens[b] >= prefix_tokens, prefix_tokens a multiple of
+ * block_size, H_kv a multiple of 8, G in {1, 2, 4, 8}. workspace: at least
+ * lk_paged_decode_shared_prefix_workspace_bytes(...) bytes, 256-byte aligned,
+ * zero-filled before first use (the same reuse rules as lk_paged_decode).
+ * Launches three kernels (prefix, ordering, suffix) and, on the first call on a
+ * stream, allocates the prefix kernel's 256-byte work counter.
+ */
+size_t lk_paged_decode_shared_prefix_workspace_bytes(int32_t B, int32_t H, int32_t H_kv,
+                                                      int32_t D, int32_t max_blocks_per_seq,
+                                                      int32_t block_size, int32_t prefix_tokens);
+int lk_paged_decode_shared_prefix(void* out, int64_t out_token_stride,
+                                  const void* q, int64_t q_token_stride,
+                                  const void* k_cache, const void* v_cache, int64_t num_blocks,
+                                  const int32_t* block_tables, int64_t block_table_stride,
+                                  const int32_t* context_lens,
+                                  int32_t B, int32_t H, int32_t H_kv, int32_t D,
+                                  int32_t block_size, int32_t max_blocks_per_seq, float scale,
+                                  int32_t prefix_tokens, void* workspace, size_t workspace_bytes,
+                                  int32_t dtype, void* stream);
+
+/*
  * Read back the status word the last decode call left in its workspace
  * (host copy; synchronises `stream`). Returns LK_STATUS_* bits or a negative
  * LK_ERR_* code.

@@ -40,6 +40,14 @@ SIGNATURES: dict[str, tuple] = {
          c_void_p, c_size_t, c_int32, c_void_p],
     ),
     "lk_paged_decode_status": (c_int32, [c_void_p, c_void_p]),
+    "lk_paged_decode_shared_prefix_workspace_bytes": (
+        c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32]),
+    "lk_paged_decode_shared_prefix": (
+        c_int32,
+        [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_int64,
+         c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_float, c_int32,
+         c_void_p, c_size_t, c_int32, c_void_p],
+    ),
     "lk_paged_prefill": (
         c_int32,
         [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_void_p,

@@ -27,4 +27,11 @@ int get_kv_tensor_map(CUtensorMap* out, const void* base, int64_t num_slots, int
 
 inline int dtype_size(int dtype) { return dtype == LK_DTYPE_F32 ? 4 : 2; }
 
+// Shared-prefix attention for lk_paged_decode_shared_prefix (paged_prefill.cu).
+int prefix_attention(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
+                     int64_t num_blocks, const int32_t* block_table_row, int B, int H, int H_kv,
+                     int block_size, int prefix_len, int prefix_split, int num_ranges,
+                     float scale, float* part_ml, float* part_o, int part_splits, int dtype,
+                     int32_t* status, cudaStream_t s);
+
 }  // namespace lk

@@ -48,6 +48,8 @@ struct DecodeParams {
   float* part_o;          // [B][num_splits][H][D]
   const int2* order;      // [B * num_splits]: (b * num_splits + split, ctx), longest first
   int* work;              // streaming kernel's unit counter (zeroed by the ordering kernel)
+  int first_stage;        // shared-prefix mode: stages before it are covered by prefix partials
+  int part_offset;        // ... which fill partial slots [0, part_offset) of each row
 };
 
 // Launch order of the split kernel's (sequence, split) units: longest first.
@@ -62,7 +64,7 @@ constexpr int kOrderBuckets = 64;
 
 __global__ void __launch_bounds__(1024) decode_order_kernel(const int32_t* context_lens, int B,
                                                             int cap, int spp, int num_splits,
-                                                            int2* order, int* work) {
+                                                            int2* order, int* work, int first) {
   if (threadIdx.x == 0 && work) *work = 0;
   __shared__ int hist[kOrderBuckets + 1];
   __shared__ int cursor[kOrderBuckets + 1];
@@ -74,10 +76,11 @@ __global__ void __launch_bounds__(1024) decode_order_kernel(const int32_t* conte
                   : (kOrderBuckets - 1) -
                         static_cast<int>(static_cast<int64_t>(n - 1) * kOrderBuckets / spp);
   };
-  auto stages = [&](int b) {
+  auto stages = [&](int b) {  // stages this kernel's units cover (past `first`)
     int ctx = context_lens[b];
     ctx = ctx < 0 ? 0 : (ctx > cap ? cap : ctx);
-    return (ctx + kTok - 1) / kTok;
+    const int n = (ctx + kTok - 1) / kTok - first;
+    return n < 0 ? 0 : n;
   };
   for (int b = threadIdx.x; b < B; b += blockDim.x) {
     const int nst = stages(b);
@@ -155,18 +158,23 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
   if (ctx < 0) ctx = 0;
   const int nst = (ctx + kTok - 1) / kTok;
   const int spp = p.stages_per_split;
-  const int nsp = nst == 0 ? 1 : (nst + spp - 1) / spp;
+  // Units cover the stages past first_stage (0 unless a shared prefix's
+  // partials already fill slots [0, part_offset)); nsp = this kernel's splits
+  // of the row, nparts = all partial slots the merge combines.
+  const int sst = nst > p.first_stage ? nst - p.first_stage : 0;
+  const int nsp = sst == 0 ? 1 : (sst + spp - 1) / spp;
+  const int nparts = p.part_offset + nsp;
   if (sp >= nsp) return;
 
   T* out = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride;
-  if (nst == 0) {
+  if (nst == 0 && p.part_offset == 0) {
     // softmax over an all -inf row is NaN in the reference; reproduce it.
     const int nq = HPC * G;
     for (int i = threadIdx.x; i < nq * kD; i += Shape::kThreads)
       store_out<T>(out + (hg * nq) * kD + i, __int_as_float(0x7fc00000));
     return;
   }
-  const int st0 = sp * spp;
+  const int st0 = p.first_stage + sp * spp;
   const int st1 = min(nst, st0 + spp);
 
   if (threadIdx.x == 0) {
@@ -353,7 +361,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
       l1 += __shfl_xor_sync(0xffffffffu, l1, off);
     }
     const int n0 = 2 * c, n1 = 2 * c + 1;
-    if (nsp == 1) {
+    if (nparts == 1) {
       const float r0 = 1.f / l0, r1 = 1.f / l1;
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) {
@@ -368,7 +376,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         }
       }
     } else {
-      const int64_t prow = (static_cast<int64_t>(b) * p.num_splits + sp) * p.H;
+      const int64_t prow = (static_cast<int64_t>(b) * p.num_splits + p.part_offset + sp) * p.H;
       float* po = p.part_o + prow * kD;
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) {
@@ -396,7 +404,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     }
   }
 
-  if (nsp == 1) return;
+  if (nparts == 1) return;
   // ---------------------------------------------- split-KV merge (last CTA) ---
   __threadfence();
   __syncthreads();
@@ -410,7 +418,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
   const int nq = HPC * G;
   const int qbase = hg * nq;
   const int64_t rowb = static_cast<int64_t>(b) * p.num_splits;
-  if (nq * nsp * 4 <= Shape::kSmem - 1024) {
+  if (nq * nparts * 4 <= Shape::kSmem - 1024) {
     // Weights w[q][s] = exp2(m_s - M) / L into the (idle) ring once, then
     // every split's partial rows as float4 with all loads of a thread in
     // flight together: the merge is a few L2 round trips, not one per output.
@@ -418,15 +426,15 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     for (int q = threadIdx.x; q < nq; q += Shape::kThreads) {
       const float* ml = p.part_ml + (rowb * p.H + qbase + q) * 2;
       float M = -INFINITY;
-      for (int s2 = 0; s2 < nsp; ++s2) M = fmaxf(M, __ldcg(ml + s2 * p.H * 2));
+      for (int s2 = 0; s2 < nparts; ++s2) M = fmaxf(M, __ldcg(ml + s2 * p.H * 2));
       float L = 0.f;
-      for (int s2 = 0; s2 < nsp; ++s2) {
+      for (int s2 = 0; s2 < nparts; ++s2) {
         const float e = exp2f(__ldcg(ml + s2 * p.H * 2) - M);
-        w[q * nsp + s2] = e;
+        w[q * nparts + s2] = e;
         L += __ldcg(ml + s2 * p.H * 2 + 1) * e;
       }
       const float inv = 1.f / L;
-      for (int s2 = 0; s2 < nsp; ++s2) w[q * nsp + s2] *= inv;
+      for (int s2 = 0; s2 < nparts; ++s2) w[q * nparts + s2] *= inv;
     }
     __syncthreads();
     constexpr int kU = 4;
@@ -438,7 +446,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
 #pragma unroll
       for (int u = 0; u < kU; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
-      for (int s2 = 0; s2 < nsp; ++s2) {
+      for (int s2 = 0; s2 < nparts; ++s2) {
         float4 v[kU];
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
@@ -448,7 +456,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
           const int i = i0 + u * Shape::kThreads;
-          const float wt = i < n4 ? w[(i * 4 / kD) * nsp + s2] : 0.f;
+          const float wt = i < n4 ? w[(i * 4 / kD) * nparts + s2] : 0.f;
           acc[u].x += v[u].x * wt;
           acc[u].y += v[u].y * wt;
           acc[u].z += v[u].z * wt;
@@ -471,9 +479,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     for (int i = threadIdx.x; i < nq * kD; i += Shape::kThreads) {
       const int qh = qbase + i / kD, d = i % kD;
       float M = -INFINITY;
-      for (int s = 0; s < nsp; ++s) M = fmaxf(M, __ldcg(p.part_ml + ((rowb + s) * p.H + qh) * 2));
+      for (int s = 0; s < nparts; ++s) M = fmaxf(M, __ldcg(p.part_ml + ((rowb + s) * p.H + qh) * 2));
       float L = 0.f, acc = 0.f;
-      for (int s = 0; s < nsp; ++s) {
+      for (int s = 0; s < nparts; ++s) {
         const float* ml = p.part_ml + ((rowb + s) * p.H + qh) * 2;
         const float wt = exp2f(__ldcg(ml) - M);
         L += __ldcg(ml + 1) * wt;
@@ -1270,11 +1278,11 @@ int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, const DecodePara
   if (p.order != nullptr) {
     decode_order_kernel<<<1, 1024, 0, s>>>(p.context_lens, B, p.max_blocks * p.bs,
                                            p.stages_per_split, p.num_splits,
-                                           const_cast<int2*>(p.order), p.work);
+                                           const_cast<int2*>(p.order), p.work, p.first_stage);
     const int rc = lk::check_launch();
     if (rc != LK_OK) return rc;
   }
-  if (p.order != nullptr && stream_units()) {
+  if (p.order != nullptr && stream_units() && p.part_offset == 0) {
     static int configured_s[64] = {0};
     if (dev >= 0 && dev < 64 && !configured_s[dev]) {
       if (cudaFuncSetAttribute(paged_decode_stream_kernel<T, HPC, NST>,
@@ -1456,6 +1464,8 @@ extern "C" int lk_paged_decode(void* out, int64_t out_token_stride, const void* 
   p.max_blocks = max_blocks_per_seq;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.prefetch = prefetch_distance();
+  p.first_stage = 0;
+  p.part_offset = 0;
   const bool persistent = num_splits < 0;
   p.num_splits = persistent ? 1 : num_splits;
   p.stages_per_split = static_cast<int>((max_stages + p.num_splits - 1) / p.num_splits);
@@ -1493,4 +1503,137 @@ extern "C" int lk_paged_decode_status(const void* workspace, void* stream) {
     return LK_ERR_CUDA;
   if (cudaStreamSynchronize(s) != cudaSuccess) return LK_ERR_CUDA;
   return v;
+}
+
+// --------------------------------------------------------- shared prefix ---
+namespace {
+
+// Plan of a shared-prefix decode: key ranges of the prefix for the tensor-core
+// pass, and splits of the suffix for the decode kernel.
+struct PrefixPlan {
+  int prefix_split, ranges;  // prefix keys per range, number of ranges
+  int spp, suffix_splits;    // suffix stages per split, splits per row
+  int part_splits;           // partial slots per row: ranges + suffix splits
+};
+
+PrefixPlan prefix_plan(int B, int H_kv, int max_blocks, int block_size, int prefix_tokens, int G) {
+  PrefixPlan pl;
+  const int sms = lk::num_sms();
+  const int rows_per_item = 256 / G;  // query rows of one prefix work item
+  const int items_per_range = ((B + rows_per_item - 1) / rows_per_item) * H_kv;
+  const int tiles = (prefix_tokens + 127) / 128;
+  int ranges = sms / (items_per_range > 0 ? items_per_range : 1);
+  if (const char* e = getenv("LITEKERN_PREFIX_RANGES")) ranges = atoi(e);
+  ranges = ranges < 1 ? 1 : (ranges > tiles ? tiles : ranges);
+  pl.prefix_split = ((tiles + ranges - 1) / ranges) * 128;
+  pl.ranges = (prefix_tokens + pl.prefix_split - 1) / pl.prefix_split;
+  const int64_t max_stages = (static_cast<int64_t>(max_blocks) * block_size + 15) / 16;
+  const int64_t suffix = max_stages - prefix_tokens / 16;
+  // About one wave of suffix units over the batch (measured on config 4: one
+  // 17-stage split per row beats 3 splits of <= 8 stages, whose ramps and
+  // extra partials cost more than the parallelism gains).
+  int want = sms / B;
+  if (want < 1) want = 1;
+  int64_t spp = suffix > 0 ? (suffix + want - 1) / want : 1;
+  if (spp < 8) spp = 8;
+  if (const char* e = getenv("LITEKERN_PREFIX_SPP")) spp = atoi(e) > 0 ? atoi(e) : spp;
+  pl.spp = static_cast<int>(spp);
+  pl.suffix_splits = suffix > 0 ? static_cast<int>((suffix + spp - 1) / spp) : 1;
+  pl.part_splits = pl.ranges + pl.suffix_splits;
+  return pl;
+}
+
+}  // namespace
+
+extern "C" size_t lk_paged_decode_shared_prefix_workspace_bytes(
+    int32_t B, int32_t H, int32_t H_kv, int32_t D, int32_t max_blocks_per_seq,
+    int32_t block_size, int32_t prefix_tokens) {
+  if (B <= 0 || H <= 0 || H_kv <= 0 || D <= 0 || H % H_kv != 0 || block_size <= 0 ||
+      prefix_tokens <= 0 || max_blocks_per_seq <= 0)
+    return 0;
+  const PrefixPlan pl =
+      prefix_plan(B, H_kv, max_blocks_per_seq, block_size, prefix_tokens, H / H_kv);
+  const size_t rows = static_cast<size_t>(B) * pl.part_splits;
+  return kHeadBytes + align256(rows * H * 2 * 4) + align256(rows * H * D * 4) +
+         align256(rows * sizeof(int2));
+}
+
+extern "C" int lk_paged_decode_shared_prefix(
+    void* out, int64_t out_token_stride, const void* q, int64_t q_token_stride,
+    const void* k_cache, const void* v_cache, int64_t num_blocks, const int32_t* block_tables,
+    int64_t block_table_stride, const int32_t* context_lens, int32_t B, int32_t H, int32_t H_kv,
+    int32_t D, int32_t block_size, int32_t max_blocks_per_seq, float scale,
+    int32_t prefix_tokens, void* workspace, size_t workspace_bytes, int32_t dtype, void* stream) {
+  if (B < 0 || H <= 0 || H_kv <= 0 || H % H_kv != 0 || num_blocks <= 0 || block_size <= 0 ||
+      max_blocks_per_seq <= 0)
+    return LK_ERR_INVALID_ARG;
+  if (B == 0) return LK_OK;
+  if (!out || !q || !k_cache || !v_cache || !block_tables || !context_lens)
+    return LK_ERR_INVALID_ARG;
+  if (dtype != LK_DTYPE_BF16 && dtype != LK_DTYPE_F16) return LK_ERR_UNSUPPORTED;
+  if (D != kD || block_size % kTok != 0 || H / H_kv > 8 || H_kv % 8 != 0) return LK_ERR_UNSUPPORTED;
+  if (prefix_tokens <= 0 || prefix_tokens % block_size != 0 ||
+      prefix_tokens > static_cast<int64_t>(max_blocks_per_seq) * block_size)
+    return LK_ERR_INVALID_ARG;
+  if (B > 65535 || static_cast<int64_t>(B) * H_kv > kMaxCounters) return LK_ERR_UNSUPPORTED;
+  if (num_blocks * block_size > 0x7fffffffLL) return LK_ERR_UNSUPPORTED;
+  if (((reinterpret_cast<uintptr_t>(q) & 3u) != 0) || (q_token_stride & 1) != 0)
+    return LK_ERR_ALIGNMENT;
+  const size_t need = lk_paged_decode_shared_prefix_workspace_bytes(
+      B, H, H_kv, D, max_blocks_per_seq, block_size, prefix_tokens);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return LK_ERR_WORKSPACE;
+  const PrefixPlan pl =
+      prefix_plan(B, H_kv, max_blocks_per_seq, block_size, prefix_tokens, H / H_kv);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const size_t rows = static_cast<size_t>(B) * pl.part_splits;
+  float* part_ml = reinterpret_cast<float*>(ws + kHeadBytes);
+  float* part_o = reinterpret_cast<float*>(ws + kHeadBytes + align256(rows * H * 2 * 4));
+  int2* order = reinterpret_cast<int2*>(ws + kHeadBytes + align256(rows * H * 2 * 4) +
+                                        align256(rows * H * D * 4));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* status = reinterpret_cast<int32_t*>(ws);
+
+  // 1. the prefix, once for all rows, on the tensor cores: partial slots [0, ranges)
+  int rc = lk::prefix_attention(q, q_token_stride, k_cache, v_cache, num_blocks, block_tables, B,
+                                H, H_kv, block_size, prefix_tokens, pl.prefix_split, pl.ranges,
+                                scale, part_ml, part_o, pl.part_splits, dtype, status, s);
+  if (rc != LK_OK) return rc;
+
+  // 2. each row's own suffix on the split decode kernel, merged with the prefix
+  const int hpc = 8;
+  const int64_t num_slots = num_blocks * block_size;
+  CUtensorMap km, vm;
+  rc = lk::get_kv_tensor_map(&km, k_cache, num_slots, H_kv, D, dtype, kTok, hpc);
+  if (rc != LK_OK) return rc;
+  rc = lk::get_kv_tensor_map(&vm, v_cache, num_slots, H_kv, D, dtype, kTok, hpc);
+  if (rc != LK_OK) return rc;
+  DecodeParams p;
+  p.out = out;
+  p.out_stride = out_token_stride;
+  p.q = q;
+  p.q_stride = q_token_stride;
+  p.block_tables = block_tables;
+  p.bt_stride = block_table_stride;
+  p.context_lens = context_lens;
+  p.num_blocks = num_blocks;
+  p.H = H;
+  p.G = H / H_kv;
+  p.bs = block_size;
+  p.max_blocks = max_blocks_per_seq;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.prefetch = 0;
+  p.stages_per_split = pl.spp;
+  p.num_splits = pl.part_splits;  // partial slots per row (and the unit encoding)
+  p.num_groups = H_kv / hpc;
+  p.status = status;
+  p.counters = reinterpret_cast<int32_t*>(ws + 256);
+  p.part_ml = part_ml;
+  p.part_o = part_o;
+  p.order = order;
+  p.work = reinterpret_cast<int*>(ws + 64);
+  p.first_stage = prefix_tokens / kTok;
+  p.part_offset = pl.ranges;
+  if (dtype == LK_DTYPE_BF16) return launch_decode<__nv_bfloat16, 8, 3>(km, vm, p, B, s);
+  return launch_decode<__half, 8, 3>(km, vm, p, B, s);
 }

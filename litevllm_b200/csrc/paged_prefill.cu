@@ -58,6 +58,14 @@ struct PrefillParams {
   int32_t* status;
   int num_seqs, H_kv, nqt;  // persistent ping-pong kernel: work-item grid
   int* sched;               // its work-item counter (zeroed per launch)
+  // Shared-prefix mode (decode rows against a prefix every row shares): the
+  // B query rows are one "chunk" (q_len = prefix_rows), keys [0, prefix_len)
+  // through block-table row 0 in key ranges of prefix_split tokens (num_seqs
+  // ranges), no causal mask; (m, l, o) partials go to part_ml / part_o at
+  // split slot = range index, in rows of part_splits slots.
+  int prefix_rows, prefix_len, prefix_split, part_splits;
+  float* part_ml;  // [rows][part_splits][H][2]
+  float* part_o;   // [rows][part_splits][H][D]
 };
 
 template <typename T>
@@ -732,7 +740,7 @@ constexpr int kPpKStage = 2 * kPpKHalf;    // one K (or V) tile: 32 KB
 constexpr int kPpThreads = 320;
 constexpr int kPpSmem = 2 * 2 * kTcQHalf + 4 * kPpKStage + 1024;  // Q_A, Q_B, 2 K + 2 V stages
 
-template <typename T>
+template <typename T, bool PREFIX>
 __global__ void __launch_bounds__(kPpThreads, 1)
 paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
@@ -764,13 +772,26 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
   // takes items from a global counter as it runs out of work and passes
   // them to the MMA thread and the softmax warps through item_ring.
   struct Item {
-    int q_start, q_len, pos0, prior, kv_end, ntiles, kvh, b;
+    int q_start, q_len, pos0, prior, kv_begin, kv_end, ntiles, kvh, b;
   };
   auto item = [&](int w) {
     Item it;
     const int qt = p.nqt - 1 - w / per_q, rem = w % per_q;
     it.kvh = rem % p.H_kv;
     it.b = rem / p.H_kv;
+    if constexpr (PREFIX) {  // b = key range; every row sees the whole range
+      it.q_start = 0;
+      it.q_len = p.prefix_rows;
+      it.pos0 = qt * BQ;
+      it.prior = 0;
+      it.kv_begin = it.b * p.prefix_split;
+      it.kv_end = min(p.prefix_len, it.kv_begin + p.prefix_split);
+      it.ntiles = it.pos0 < it.q_len && it.kv_end > it.kv_begin
+                      ? (it.kv_end - it.kv_begin + kPpKT - 1) / kPpKT
+                      : 0;
+      return it;
+    }
+    it.kv_begin = 0;
     it.q_start = p.cu_seqlens_q[it.b];
     it.q_len = p.cu_seqlens_q[it.b + 1] - it.q_start;
     it.pos0 = qt * BQ;
@@ -856,9 +877,10 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
       w = __shfl_sync(0xffffffffu, w, 0);
       if (!ok || w >= num_items) break;
       const Item it = item(w);
-      const int32_t* bt =
-          p.block_tables ? p.block_tables + static_cast<int64_t>(it.b) * p.bt_stride : nullptr;
-      auto slot_of = [&](int tok) -> int {
+      const int32_t* bt = p.block_tables ? p.block_tables + (PREFIX ? 0 : static_cast<int64_t>(it.b) * p.bt_stride)
+                                         : nullptr;
+      auto slot_of = [&](int tok) -> int {  // tok counts from the item's first key
+        tok += it.kv_begin;
         if (tok >= it.kv_end) return oob;
         if (!bt) return it.q_start + tok;
         const int blk = __ldg(bt + tok / p.bs);
@@ -1019,14 +1041,14 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
     while (w < num_items && ok) {
       const Item it = item(w);
       const int pos = it.pos0 + t / G, gh = t % G;
-      const int limit = it.prior + pos;  // last visible key of this row
+      const int limit = PREFIX ? it.kv_end - 1 : it.prior + pos;  // last visible key of this row
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; j < it.ntiles; ++j, ++g) {
         if (ok && !lk::mbar_wait(&s_full[u], g & 1)) ok = false;
         ok = __all_sync(0xffffffffu, ok);
         lk::tc::fence_after();
         // Pass 1: row maximum over the 128 scores, 64 columns per TMEM load.
-        const int kb = j * kPpKT;
+        const int kb = it.kv_begin + j * kPpKT;
         const bool diag = kb + kPpKT - 1 > limit;  // tile crosses the causal edge
         auto load_half = [&](int h, uint32_t (&sv)[2][32]) {
           lk::tc::ld32(tS + lane_base + 64 * h, sv[0]);
@@ -1115,6 +1137,28 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
       if (ok && lk::mbar_wait(&o_final, n_items & 1)) {
         if (wn < num_items) publish_q();
         lk::tc::fence_after();
+        if constexpr (PREFIX) {
+          // partial (m, l, unnormalised o) of row (sequence pos, head) for this key range
+          const int64_t prow =
+              (static_cast<int64_t>(pos) * p.part_splits + it.b) * p.H + it.kvh * G + gh;
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            uint32_t ov[32];
+            lk::tc::ld32(tO + lane_base + 32 * c4, ov);  // whole warp, every row
+            lk::tc::wait_ld();
+            if (pos < it.q_len) {
+              float4* po = reinterpret_cast<float4*>(p.part_o + prow * kD + c4 * 32);
+#pragma unroll
+              for (int c = 0; c < 8; ++c)
+                po[c] = make_float4(__uint_as_float(ov[4 * c]), __uint_as_float(ov[4 * c + 1]),
+                                    __uint_as_float(ov[4 * c + 2]), __uint_as_float(ov[4 * c + 3]));
+            }
+          }
+          if (pos < it.q_len) {
+            p.part_ml[prow * 2] = m_used;
+            p.part_ml[prow * 2 + 1] = l;
+          }
+        } else {
         const float inv = 1.f / l;
         T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(it.q_start + pos) * p.H * kD +
                   static_cast<int64_t>(it.kvh * G + gh) * kD;
@@ -1135,6 +1179,7 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
                   make_uint4(o4[0], o4[1], o4[2], o4[3]);
             }
           }
+        }
         }
       } else {
         ok = false;
@@ -1182,7 +1227,7 @@ int launch_prefill_pp(const CUtensorMap& km, const CUtensorMap& vm, PrefillParam
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(paged_prefill_pp_kernel<T>,
+    if (cudaFuncSetAttribute(paged_prefill_pp_kernel<T, false>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, kPpSmem) != cudaSuccess)
       return LK_ERR_CUDA;
     configured[dev] = 1;
@@ -1197,7 +1242,35 @@ int launch_prefill_pp(const CUtensorMap& km, const CUtensorMap& vm, PrefillParam
   const int64_t items = static_cast<int64_t>(p.nqt) * H_kv * num_seqs;
   if (items > 0x7fffffffLL) return LK_ERR_TOO_LARGE;
   const int grid = static_cast<int>(items < lk::num_sms() ? items : lk::num_sms());
-  paged_prefill_pp_kernel<T><<<grid, kPpThreads, kPpSmem, s>>>(km, vm, p);
+  paged_prefill_pp_kernel<T, false><<<grid, kPpThreads, kPpSmem, s>>>(km, vm, p);
+  return lk::check_launch();
+}
+
+// Shared-prefix mode of the ping-pong kernel: B decode rows (q [B, H, D]) of
+// every KV head against prefix keys [0, prefix_len) in ranges of prefix_split
+// tokens; writes (m, l, o) partials.
+template <typename T>
+int launch_prefix_pp(const CUtensorMap& km, const CUtensorMap& vm, PrefillParams p, int B,
+                     int H_kv, cudaStream_t s) {
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(paged_prefill_pp_kernel<T, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kPpSmem) != cudaSuccess)
+      return LK_ERR_CUDA;
+    configured[dev] = 1;
+  }
+  p.BQ = 256 / p.G;
+  p.nqt = (B + p.BQ - 1) / p.BQ;
+  p.H_kv = H_kv;
+  p.sched = sched_counter(s);
+  if (p.sched == nullptr) return LK_ERR_CUDA;
+  const int64_t items = static_cast<int64_t>(p.nqt) * H_kv * p.num_seqs;
+  if (items > 0x7fffffffLL) return LK_ERR_TOO_LARGE;
+  if (cudaMemsetAsync(p.sched, 0, sizeof(int), s) != cudaSuccess) return LK_ERR_CUDA;
+  const int grid = static_cast<int>(items < lk::num_sms() ? items : lk::num_sms());
+  paged_prefill_pp_kernel<T, true><<<grid, kPpThreads, kPpSmem, s>>>(km, vm, p);
   return lk::check_launch();
 }
 
@@ -1286,3 +1359,45 @@ extern "C" int lk_paged_prefill(void* out, const void* q, int64_t q_token_stride
     return launch_prefill<__nv_bfloat16>(km, vm, p, num_seqs, max_q_len, H_kv, s);
   return launch_prefill<__half>(km, vm, p, num_seqs, max_q_len, H_kv, s);
 }
+
+namespace lk {
+
+// Library-internal (no C export): the shared-prefix attention of
+// lk_paged_decode_shared_prefix, on the ping-pong tensor-core kernel.
+int prefix_attention(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
+                     int64_t num_blocks, const int32_t* block_table_row, int B, int H, int H_kv,
+                     int block_size, int prefix_len, int prefix_split, int num_ranges,
+                     float scale, float* part_ml, float* part_o, int part_splits, int dtype,
+                     int32_t* status, cudaStream_t s) {
+  const int G = H / H_kv;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return LK_ERR_UNSUPPORTED;
+  const int64_t num_slots = num_blocks * block_size;
+  CUtensorMap km, vm;
+  int rc = lk::get_kv_tensor_map(&km, k_cache, num_slots, H_kv, kD, dtype, 16, 1);
+  if (rc != LK_OK) return rc;
+  rc = lk::get_kv_tensor_map(&vm, v_cache, num_slots, H_kv, kD, dtype, 16, 1);
+  if (rc != LK_OK) return rc;
+  PrefillParams p{};
+  p.q = q;
+  p.q_stride = q_stride;
+  p.block_tables = block_table_row;
+  p.bt_stride = 0;
+  p.num_slots = num_slots;
+  p.num_blocks = num_blocks;
+  p.H = H;
+  p.G = G;
+  p.bs = block_size;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.status = status;
+  p.num_seqs = num_ranges;
+  p.prefix_rows = B;
+  p.prefix_len = prefix_len;
+  p.prefix_split = prefix_split;
+  p.part_splits = part_splits;
+  p.part_ml = part_ml;
+  p.part_o = part_o;
+  if (dtype == LK_DTYPE_BF16) return launch_prefix_pp<__nv_bfloat16>(km, vm, p, B, H_kv, s);
+  return launch_prefix_pp<__half>(km, vm, p, B, H_kv, s);
+}
+
+}  // namespace lk

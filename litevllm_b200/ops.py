@@ -194,6 +194,67 @@ def paged_decode(
     return out
 
 
+def paged_decode_shared_prefix(
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    context_lens: torch.Tensor,
+    scale: float,
+    prefix_tokens: int,
+    out: Optional[torch.Tensor] = None,
+    workspace: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """paged_decode for a batch whose rows share their first prefix_tokens
+    tokens (the same physical blocks at the start of every block-table row):
+    the shared part runs once, on the tensor cores, for all rows. Same result
+    as paged_decode (Attention._decode_fast, litevllm/layers/attention.py:91-139)."""
+    dev = _cuda(query, key_cache, value_cache, block_tables, context_lens, out, workspace)
+    if query.dim() != 3:
+        raise ValueError("query must be [B, H, D]")
+    B, H, D = query.shape
+    nb, bs, H_kv, Dk = key_cache.shape
+    if Dk != D or value_cache.shape != key_cache.shape:
+        raise ValueError("cache shape mismatch")
+    if not (key_cache.is_contiguous() and value_cache.is_contiguous()):
+        raise ValueError("caches must be contiguous")
+    if query.dtype != key_cache.dtype:
+        raise TypeError("query dtype must match the cache dtype")
+    if query.stride(2) != 1 or query.stride(1) != D:
+        raise ValueError("query must have unit d-stride and head stride D")
+    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or block_tables.shape[0] != B:
+        raise TypeError("block_tables must be int32 [B, max_blocks]")
+    block_tables = block_tables.contiguous()
+    if context_lens.dtype != torch.int32 or context_lens.numel() != B:
+        raise TypeError("context_lens must be int32 [B]")
+    context_lens = context_lens.contiguous()
+    code = _dtype_code(query)
+    if out is None:
+        out = torch.empty((B, H, D), dtype=query.dtype, device=dev)
+    if B == 0:
+        return out
+    max_blocks = block_tables.shape[1]
+    need = int(lib().lk_paged_decode_shared_prefix_workspace_bytes(B, H, H_kv, D, max_blocks, bs,
+                                                                    int(prefix_tokens)))
+    if need == 0:
+        raise ValueError("invalid shared-prefix decode shape")
+    if workspace is None:
+        workspace = WORKSPACES.get(dev, "decode", need)
+    elif workspace.numel() * workspace.element_size() < need:
+        raise ValueError(f"workspace too small: need {need} bytes")
+    with _on(dev):
+        check(
+            lib().lk_paged_decode_shared_prefix(
+                out.data_ptr(), out.stride(0), query.data_ptr(), query.stride(0),
+                key_cache.data_ptr(), value_cache.data_ptr(), nb, block_tables.data_ptr(),
+                block_tables.stride(0), context_lens.data_ptr(), B, H, H_kv, D, bs, max_blocks,
+                float(scale), int(prefix_tokens), workspace.data_ptr(),
+                workspace.numel() * workspace.element_size(), code, _stream(dev),
+            )
+        )
+    return out
+
+
 def decode_status(workspace: Optional[torch.Tensor] = None, device=None) -> int:
     """Read (and clear) the LK_STATUS_* bits the decode kernels left in their
     workspace. Synchronises the current stream."""

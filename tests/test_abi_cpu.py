@@ -136,3 +136,24 @@ def test_integration_stub_binds_against_the_library():
     assert callable(ns["store_kvcache"]) and callable(ns["decode"])
     assert ns["_lk"].lk_status_string(0) == b"ok"
     assert ns["_lk"].lk_paged_decode_workspace_bytes(256, 32, 8, 128, 2) > 256 + 65536 * 4
+
+
+def test_shared_prefix_decode_rejects_bad_arguments():
+    lib = _lib.lib()
+    ws = lib.lk_paged_decode_shared_prefix_workspace_bytes
+    assert ws(128, 32, 8, 128, 144, 16, 2032) > 256 + 65536 * 4
+    assert ws(128, 32, 8, 128, 144, 16, 0) == 0          # no prefix
+    assert ws(128, 30, 8, 128, 144, 16, 2032) == 0       # H not a multiple of H_kv
+    f = lib.lk_paged_decode_shared_prefix
+    P = 1 << 20  # aligned stand-in pointers: nothing is launched on these paths
+    args = [P, 4096, P, 4096, P, P, 1000, P, 144, P, 128, 32, 8, 128, 16, 144, 0.088, 2032, None,
+            0, 2, None]
+    assert f(*args) == -4                                    # no workspace
+    bad = list(args); bad[17] = 2030                         # prefix not a multiple of bs
+    assert f(*bad) == -1
+    bad = list(args); bad[17] = 144 * 16 + 16                # prefix longer than the table
+    assert f(*bad) == -1
+    bad = list(args); bad[12] = 4; bad[11] = 16              # H_kv not a multiple of 8
+    assert f(*bad) == -2
+    bad = list(args); bad[10] = 0                            # B = 0: nothing to do
+    assert f(*bad) == 0
