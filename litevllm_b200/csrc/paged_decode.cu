@@ -1523,7 +1523,11 @@ PrefixPlan prefix_plan(int B, int H_kv, int max_blocks, int block_size, int pref
   const int items_per_range = ((B + rows_per_item - 1) / rows_per_item) * H_kv;
   const int tiles = (prefix_tokens + 127) / 128;
   int ranges = sms / (items_per_range > 0 ? items_per_range : 1);
-  if (const char* e = getenv("LITEKERN_PREFIX_RANGES")) ranges = atoi(e);
+  static const int ranges_env = [] {
+    const char* e = getenv("LITEKERN_PREFIX_RANGES");
+    return e ? atoi(e) : 0;
+  }();
+  if (ranges_env > 0) ranges = ranges_env;
   ranges = ranges < 1 ? 1 : (ranges > tiles ? tiles : ranges);
   pl.prefix_split = ((tiles + ranges - 1) / ranges) * 128;
   pl.ranges = (prefix_tokens + pl.prefix_split - 1) / pl.prefix_split;
@@ -1536,7 +1540,11 @@ PrefixPlan prefix_plan(int B, int H_kv, int max_blocks, int block_size, int pref
   if (want < 1) want = 1;
   int64_t spp = suffix > 0 ? (suffix + want - 1) / want : 1;
   if (spp < 8) spp = 8;
-  if (const char* e = getenv("LITEKERN_PREFIX_SPP")) spp = atoi(e) > 0 ? atoi(e) : spp;
+  static const int spp_env = [] {
+    const char* e = getenv("LITEKERN_PREFIX_SPP");
+    return e ? atoi(e) : 0;
+  }();
+  if (spp_env > 0) spp = spp_env;
   pl.spp = static_cast<int>(spp);
   pl.suffix_splits = suffix > 0 ? static_cast<int>((suffix + spp - 1) / spp) : 1;
   pl.part_splits = pl.ranges + pl.suffix_splits;
