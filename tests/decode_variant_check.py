@@ -1,6 +1,7 @@
 """Child-process check used by test_gpu_decode.test_decode_kernel_options:
-ragged decode batches (split and unsplit, several GQA ratios) with whichever
-decode options the environment selects, against the fp32 oracle."""
+ragged decode batches (split and unsplit, several GQA ratios) and a
+shared-prefix batch with whichever decode options the environment selects,
+against the fp32 oracle."""
 
 import torch
 
@@ -21,6 +22,13 @@ def main() -> None:
         ref = pa.decode(b.query.float(), b.key_cache.float(), b.value_cache.float(),
                         b.block_tables, b.context_lens, b.scale)
         assert_attn_close(out, ref)
+    # shared-prefix decode (config 4 shape, fewer rows)
+    b = workloads.make_prefix_batch(24, seed=2, device=dev)
+    out = ops.paged_decode_shared_prefix(b.query, b.key_cache, b.value_cache, b.block_tables,
+                                         b.context_lens, b.scale, 127 * 16)
+    ref = pa.decode(b.query.float(), b.key_cache.float(), b.value_cache.float(), b.block_tables,
+                    b.context_lens, b.scale, rows=[0, 5, 23])
+    assert_attn_close(out[[0, 5, 23]], ref)
     print("ok")
 
 
