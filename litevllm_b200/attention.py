@@ -15,6 +15,22 @@ import torch.nn as nn
 
 from . import ops
 
+# Shared-prefix hint for the current decode step, set by the engine hook that
+# builds the step's block tables (engine_hooks.prepare_inputs): the tensor it
+# applies to and the number of leading tokens every row shares (full blocks).
+# Attention.forward uses the shared-prefix decode only for that exact tensor.
+_SHARED_PREFIX = {"table": None, "tokens": 0}
+# Below these, the per-row decode kernel is as fast.
+SHARED_PREFIX_MIN_TOKENS = 256
+SHARED_PREFIX_MIN_ROWS = 4
+
+
+def set_shared_prefix_hint(block_tables: Optional[torch.Tensor], prefix_tokens: int) -> None:
+    """Declare that every row of `block_tables` starts with the same
+    `prefix_tokens` tokens (whole, filled blocks); None clears the hint."""
+    _SHARED_PREFIX["table"] = block_tables
+    _SHARED_PREFIX["tokens"] = int(prefix_tokens) if block_tables is not None else 0
+
 
 class PagedAttention:
     """Static helpers with the reference's names (attention.py:14-65)."""
@@ -96,6 +112,17 @@ class Attention(nn.Module):
                 block_tables=block_table, context_lens=context_lens,
             )
 
+        pref = _SHARED_PREFIX["tokens"]
+        if (
+            pref >= SHARED_PREFIX_MIN_TOKENS
+            and block_table is _SHARED_PREFIX["table"]
+            and query.shape[0] >= SHARED_PREFIX_MIN_ROWS
+            and key_cache.shape[2] % 8 == 0
+        ):
+            # the rows share their first `pref` tokens: compute them once
+            return ops.paged_decode_shared_prefix(
+                query, key_cache, value_cache, block_table, context_lens, self.scale, pref
+            )
         return ops.paged_decode(
             query, key_cache, value_cache, block_table, context_lens, self.scale
         )

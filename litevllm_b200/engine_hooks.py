@@ -25,6 +25,7 @@ import sys
 import numpy as np
 import torch
 
+from .attention import set_shared_prefix_hint
 from .sampler import Sampler
 
 
@@ -33,6 +34,22 @@ def _fast_params(params, logits_dtype) -> bool:
         return False
     filtered = getattr(params, "top_k", -1) > 0 or getattr(params, "top_p", 1.0) < 1.0
     return not filtered or logits_dtype in (torch.bfloat16, torch.float16)
+
+
+def shared_prefix_tokens(tables, ctx_lens, bs: int) -> int:
+    """Tokens at the start of every row that live in the same physical blocks,
+    whole blocks that every row has filled."""
+    if len(tables) < 2:
+        return 0
+    n = min(min(t.shape[0] for t in tables), min(int(c) // bs for c in ctx_lens))
+    first = tables[0]
+    for t in tables[1:]:
+        if n == 0:
+            break
+        diff = np.nonzero(t[:n] != first[:n])[0]
+        if diff.size:
+            n = int(diff[0])
+    return n * bs
 
 
 def prepare_inputs(self, seq_groups, block_manager):
@@ -76,6 +93,7 @@ def prepare_inputs(self, seq_groups, block_manager):
     input_ids, positions, slot_mapping = dev64[:n], dev64[n:2 * n], dev64[2 * n:]
     if is_prefill:
         block_tables = context_lens = None
+        set_shared_prefix_hint(None, 0)
     else:
         max_blocks = max((t.shape[0] for t in tables), default=0)
         tab = np.zeros((len(tables), max_blocks), dtype=np.int32)
@@ -89,6 +107,11 @@ def prepare_inputs(self, seq_groups, block_manager):
         nb = len(tables) * max_blocks
         block_tables = d32[:nb].view(len(tables), max_blocks)
         context_lens = d32[nb:]
+        # Leading blocks every decode row shares (the PrefixCache hands the same
+        # physical blocks to sequences with a common prefix), counted only while
+        # every row has filled them: the shared-prefix decode computes that part
+        # once for the batch.
+        set_shared_prefix_hint(block_tables, shared_prefix_tokens(tables, ctx_lens, bs))
     return InputMetadata(input_ids=input_ids, positions=positions, slot_mapping=slot_mapping,
                          block_tables=block_tables, context_lens=context_lens,
                          is_prefill=is_prefill, seq_ids=seq_ids)

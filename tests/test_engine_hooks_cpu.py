@@ -87,6 +87,10 @@ def test_prepare_inputs_matches_reference_prefill_and_decode(ref, monkeypatch):
     got = engine_hooks.prepare_inputs(runner, groups, sched.block_manager)
     _same(got, want)
     assert not got.is_prefill and got.block_tables.shape[0] == 3
+    # the shared-prefix hint belongs to this step's table (no shared blocks here)
+    from litevllm_b200 import attention
+    assert attention._SHARED_PREFIX["table"] is got.block_tables
+    assert attention._SHARED_PREFIX["tokens"] == 0
 
 
 def test_process_outputs_matches_reference(ref, monkeypatch):
@@ -111,3 +115,17 @@ def test_process_outputs_matches_reference(ref, monkeypatch):
                 for g in groups for s in g.seqs]
 
     assert run(engine_hooks.process_outputs) == run(ref.LLMEngine._process_outputs)
+
+
+def test_shared_prefix_tokens_counts_whole_shared_filled_blocks():
+    import numpy as np
+    from litevllm_b200.engine_hooks import shared_prefix_tokens
+
+    a = np.array([5, 9, 2, 7, 1])
+    b = np.array([5, 9, 2, 8])
+    c = np.array([5, 9, 2, 7, 4, 6])
+    assert shared_prefix_tokens([a, b, c], [80, 64, 90], 16) == 48      # 3 shared blocks
+    assert shared_prefix_tokens([a, b, c], [80, 40, 90], 16) == 32      # row 1 filled only 2
+    assert shared_prefix_tokens([a, c], [80, 90], 16) == 64             # 4 shared, all filled
+    assert shared_prefix_tokens([a], [80], 16) == 0                     # one row: nothing shared
+    assert shared_prefix_tokens([a, np.array([6, 9])], [80, 32], 16) == 0

@@ -240,3 +240,24 @@ def test_shared_prefix_decode_config4_and_fp16(cuda):
     out = ops.paged_decode_shared_prefix(q, kc, vc, bt, ctx, 128 ** -0.5, 320)
     ref = pa.decode(q.float(), kc.float(), vc.float(), bt, ctx, 128 ** -0.5)
     assert_attn_close(out, ref)
+
+
+def test_attention_forward_uses_the_shared_prefix_hint(cuda):
+    """The engine hook's hint routes Attention.forward's decode to the
+    shared-prefix kernel for that step's table only; results agree."""
+    from litevllm_b200 import attention as att
+    b = workloads.make_prefix_batch(32, seed=4, device=cuda)
+    layer = att.Attention(32, 128, 8)
+    plain = layer.forward(b.query, b.key, b.value, b.key_cache, b.value_cache, b.block_tables,
+                          None, b.context_lens, is_prefill=False)
+    att.set_shared_prefix_hint(b.block_tables, 127 * 16)
+    try:
+        hinted = layer.forward(b.query, b.key, b.value, b.key_cache, b.value_cache,
+                               b.block_tables, None, b.context_lens, is_prefill=False)
+        other = b.block_tables.clone()  # another tensor: the hint does not apply
+        again = layer.forward(b.query, b.key, b.value, b.key_cache, b.value_cache, other, None,
+                              b.context_lens, is_prefill=False)
+    finally:
+        att.set_shared_prefix_hint(None, 0)
+    assert_attn_close(hinted, plain.float(), max_abs=1e-2, mean_rel=5e-3)
+    assert torch.equal(again, plain)
