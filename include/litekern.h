@@ -122,7 +122,8 @@ int lk_paged_decode(void* out, int64_t out_token_stride,
  * of a KV head against the prefix keys on the tensor cores, in key ranges --
  * plus each row's own suffix on the split decode kernel, merged by log-sum-exp.
  * No counterpart in the reference (its decode re-reads the shared blocks per
- * row). Requires context_lens[b] >= prefix_tokens, prefix_tokens a multiple of
+ * row). Requires context_lens[b] >= prefix_tokens (a shorter row sets
+ * LK_STATUS_CTX_OOB in the workspace status word), prefix_tokens a multiple of
  * block_size, H_kv a multiple of 8, G in {1, 2, 4, 8}. workspace: at least
  * lk_paged_decode_shared_prefix_workspace_bytes(...) bytes, 256-byte aligned,
  * zero-filled before first use (the same reuse rules as lk_paged_decode).

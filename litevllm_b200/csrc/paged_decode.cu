@@ -161,6 +161,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
   // Units cover the stages past first_stage (0 unless a shared prefix's
   // partials already fill slots [0, part_offset)); nsp = this kernel's splits
   // of the row, nparts = all partial slots the merge combines.
+  if (p.part_offset > 0 && ctx < p.first_stage * kTok && sp == 0 && hg == 0 &&
+      threadIdx.x == 0)
+    atomicOr(p.status, LK_STATUS_CTX_OOB);  // shared prefix longer than this row's context
   const int sst = nst > p.first_stage ? nst - p.first_stage : 0;
   const int nsp = sst == 0 ? 1 : (sst + spp - 1) / spp;
   const int nparts = p.part_offset + nsp;

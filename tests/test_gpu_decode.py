@@ -261,3 +261,12 @@ def test_attention_forward_uses_the_shared_prefix_hint(cuda):
         att.set_shared_prefix_hint(None, 0)
     assert_attn_close(hinted, plain.float(), max_abs=1e-2, mean_rel=5e-3)
     assert torch.equal(again, plain)
+
+
+def test_shared_prefix_longer_than_a_row_is_flagged(cuda):
+    q, kc, vc, bt, ctx = _shared_prefix_batch(cuda, 6, 10, [5, 40, 0, 7, 9, 30], seed=12)
+    ctx[2] = 100  # shorter than the declared 160-token prefix
+    ws = torch.zeros(ops.lib().lk_paged_decode_shared_prefix_workspace_bytes(
+        6, 32, 8, 128, bt.shape[1], 16, 160), dtype=torch.uint8, device=cuda)
+    ops.paged_decode_shared_prefix(q, kc, vc, bt, ctx, 128 ** -0.5, 160, workspace=ws)
+    assert ops.decode_status(ws) & 8  # LK_STATUS_CTX_OOB
