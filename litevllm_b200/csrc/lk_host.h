@@ -32,6 +32,6 @@ int prefix_attention(const void* q, int64_t q_stride, const void* k_cache, const
                      int64_t num_blocks, const int32_t* block_table_row, int B, int H, int H_kv,
                      int block_size, int prefix_len, int prefix_split, int num_ranges,
                      float scale, float* part_ml, float* part_o, int part_splits, int dtype,
-                     int32_t* status, cudaStream_t s);
+                     int32_t* status, int* zeroed_counter, cudaStream_t s);
 
 }  // namespace lk

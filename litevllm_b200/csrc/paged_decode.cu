@@ -64,8 +64,10 @@ constexpr int kOrderBuckets = 64;
 
 __global__ void __launch_bounds__(1024) decode_order_kernel(const int32_t* context_lens, int B,
                                                             int cap, int spp, int num_splits,
-                                                            int2* order, int* work, int first) {
+                                                            int2* order, int* work, int first,
+                                                            int* work2) {
   if (threadIdx.x == 0 && work) *work = 0;
+  if (threadIdx.x == 0 && work2) *work2 = 0;
   __shared__ int hist[kOrderBuckets + 1];
   __shared__ int cursor[kOrderBuckets + 1];
   __shared__ int total;
@@ -1266,7 +1268,7 @@ int heads_per_cta(int H_kv) {
 
 template <typename T, int HPC, int NST>
 int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, const DecodeParams& p, int B,
-                  cudaStream_t s) {
+                  cudaStream_t s, bool order_done = false) {
   using Shape = DecodeShape<HPC, NST>;
   static int configured[64] = {0};
   int dev = 0;
@@ -1278,10 +1280,11 @@ int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, const DecodePara
       return LK_ERR_CUDA;
     configured[dev] = 1;
   }
-  if (p.order != nullptr) {
+  if (p.order != nullptr && !order_done) {
     decode_order_kernel<<<1, 1024, 0, s>>>(p.context_lens, B, p.max_blocks * p.bs,
                                            p.stages_per_split, p.num_splits,
-                                           const_cast<int2*>(p.order), p.work, p.first_stage);
+                                           const_cast<int2*>(p.order), p.work, p.first_stage,
+                                           nullptr);
     const int rc = lk::check_launch();
     if (rc != LK_OK) return rc;
   }
@@ -1605,13 +1608,21 @@ extern "C" int lk_paged_decode_shared_prefix(
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int32_t* status = reinterpret_cast<int32_t*>(ws);
 
-  // 1. the prefix, once for all rows, on the tensor cores: partial slots [0, ranges)
-  int rc = lk::prefix_attention(q, q_token_stride, k_cache, v_cache, num_blocks, block_tables, B,
-                                H, H_kv, block_size, prefix_tokens, pl.prefix_split, pl.ranges,
-                                scale, part_ml, part_o, pl.part_splits, dtype, status, s);
+  // 1. the suffix units' launch order (also zeroes both kernels' work counters)
+  int* prefix_counter = reinterpret_cast<int*>(ws + 128);  // in the status header
+  decode_order_kernel<<<1, 1024, 0, s>>>(context_lens, B, max_blocks_per_seq * block_size,
+                                         pl.spp, pl.part_splits, order,
+                                         reinterpret_cast<int*>(ws + 64), prefix_tokens / kTok,
+                                         prefix_counter);
+  int rc = lk::check_launch();
+  if (rc != LK_OK) return rc;
+  // 2. the prefix, once for all rows, on the tensor cores: partial slots [0, ranges)
+  rc = lk::prefix_attention(q, q_token_stride, k_cache, v_cache, num_blocks, block_tables, B, H,
+                            H_kv, block_size, prefix_tokens, pl.prefix_split, pl.ranges, scale,
+                            part_ml, part_o, pl.part_splits, dtype, status, prefix_counter, s);
   if (rc != LK_OK) return rc;
 
-  // 2. each row's own suffix on the split decode kernel, merged with the prefix
+  // 3. each row's own suffix on the split decode kernel, merged with the prefix
   const int hpc = 8;
   const int64_t num_slots = num_blocks * block_size;
   CUtensorMap km, vm;
@@ -1645,6 +1656,6 @@ extern "C" int lk_paged_decode_shared_prefix(
   p.work = reinterpret_cast<int*>(ws + 64);
   p.first_stage = prefix_tokens / kTok;
   p.part_offset = pl.ranges;
-  if (dtype == LK_DTYPE_BF16) return launch_decode<__nv_bfloat16, 8, 3>(km, vm, p, B, s);
-  return launch_decode<__half, 8, 3>(km, vm, p, B, s);
+  if (dtype == LK_DTYPE_BF16) return launch_decode<__nv_bfloat16, 8, 3>(km, vm, p, B, s, true);
+  return launch_decode<__half, 8, 3>(km, vm, p, B, s, true);
 }

@@ -1251,7 +1251,7 @@ int launch_prefill_pp(const CUtensorMap& km, const CUtensorMap& vm, PrefillParam
 // tokens; writes (m, l, o) partials.
 template <typename T>
 int launch_prefix_pp(const CUtensorMap& km, const CUtensorMap& vm, PrefillParams p, int B,
-                     int H_kv, cudaStream_t s) {
+                     int H_kv, int* zeroed_counter, cudaStream_t s) {
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1264,11 +1264,15 @@ int launch_prefix_pp(const CUtensorMap& km, const CUtensorMap& vm, PrefillParams
   p.BQ = 256 / p.G;
   p.nqt = (B + p.BQ - 1) / p.BQ;
   p.H_kv = H_kv;
-  p.sched = sched_counter(s);
-  if (p.sched == nullptr) return LK_ERR_CUDA;
   const int64_t items = static_cast<int64_t>(p.nqt) * H_kv * p.num_seqs;
   if (items > 0x7fffffffLL) return LK_ERR_TOO_LARGE;
-  if (cudaMemsetAsync(p.sched, 0, sizeof(int), s) != cudaSuccess) return LK_ERR_CUDA;
+  if (zeroed_counter != nullptr) {  // zeroed earlier on this stream by the caller
+    p.sched = zeroed_counter;
+  } else {
+    p.sched = sched_counter(s);
+    if (p.sched == nullptr) return LK_ERR_CUDA;
+    if (cudaMemsetAsync(p.sched, 0, sizeof(int), s) != cudaSuccess) return LK_ERR_CUDA;
+  }
   const int grid = static_cast<int>(items < lk::num_sms() ? items : lk::num_sms());
   paged_prefill_pp_kernel<T, true><<<grid, kPpThreads, kPpSmem, s>>>(km, vm, p);
   return lk::check_launch();
@@ -1368,7 +1372,7 @@ int prefix_attention(const void* q, int64_t q_stride, const void* k_cache, const
                      int64_t num_blocks, const int32_t* block_table_row, int B, int H, int H_kv,
                      int block_size, int prefix_len, int prefix_split, int num_ranges,
                      float scale, float* part_ml, float* part_o, int part_splits, int dtype,
-                     int32_t* status, cudaStream_t s) {
+                     int32_t* status, int* zeroed_counter, cudaStream_t s) {
   const int G = H / H_kv;
   if (G != 1 && G != 2 && G != 4 && G != 8) return LK_ERR_UNSUPPORTED;
   const int64_t num_slots = num_blocks * block_size;
@@ -1396,8 +1400,9 @@ int prefix_attention(const void* q, int64_t q_stride, const void* k_cache, const
   p.part_splits = part_splits;
   p.part_ml = part_ml;
   p.part_o = part_o;
-  if (dtype == LK_DTYPE_BF16) return launch_prefix_pp<__nv_bfloat16>(km, vm, p, B, H_kv, s);
-  return launch_prefix_pp<__half>(km, vm, p, B, H_kv, s);
+  if (dtype == LK_DTYPE_BF16)
+    return launch_prefix_pp<__nv_bfloat16>(km, vm, p, B, H_kv, zeroed_counter, s);
+  return launch_prefix_pp<__half>(km, vm, p, B, H_kv, zeroed_counter, s);
 }
 
 }  // namespace lk
