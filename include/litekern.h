@@ -124,7 +124,7 @@ int lk_paged_decode(void* out, int64_t out_token_stride,
  * No counterpart in the reference (its decode re-reads the shared blocks per
  * row). Requires context_lens[b] >= prefix_tokens (a shorter row sets
  * LK_STATUS_CTX_OOB in the workspace status word), prefix_tokens a multiple of
- * block_size, H_kv a multiple of 8, G in {1, 2, 4, 8}. workspace: at least
+ * block_size, G in {1, 2, 4, 8}. workspace: at least
  * lk_paged_decode_shared_prefix_workspace_bytes(...) bytes, 256-byte aligned,
  * zero-filled before first use (the same reuse rules as lk_paged_decode).
  * Launches three kernels (prefix, ordering, suffix) and, on the first call on a

@@ -117,7 +117,6 @@ class Attention(nn.Module):
             pref >= SHARED_PREFIX_MIN_TOKENS
             and block_table is _SHARED_PREFIX["table"]
             and query.shape[0] >= SHARED_PREFIX_MIN_ROWS
-            and key_cache.shape[2] % 8 == 0
         ):
             # the rows share their first `pref` tokens: compute them once
             return ops.paged_decode_shared_prefix(

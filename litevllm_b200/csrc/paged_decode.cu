@@ -1310,12 +1310,12 @@ int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, const DecodePara
 
 template <typename T>
 int dispatch_decode(int hpc, const CUtensorMap& km, const CUtensorMap& vm, const DecodeParams& p,
-                    int B, cudaStream_t s) {
+                    int B, cudaStream_t s, bool order_done = false) {
   switch (hpc) {
-    case 8: return launch_decode<T, 8, 3>(km, vm, p, B, s);
-    case 4: return launch_decode<T, 4, 6>(km, vm, p, B, s);
-    case 2: return launch_decode<T, 2, 8>(km, vm, p, B, s);
-    default: return launch_decode<T, 1, 8>(km, vm, p, B, s);
+    case 8: return launch_decode<T, 8, 3>(km, vm, p, B, s, order_done);
+    case 4: return launch_decode<T, 4, 6>(km, vm, p, B, s, order_done);
+    case 2: return launch_decode<T, 2, 8>(km, vm, p, B, s, order_done);
+    default: return launch_decode<T, 1, 8>(km, vm, p, B, s, order_done);
   }
 }
 
@@ -1585,7 +1585,7 @@ extern "C" int lk_paged_decode_shared_prefix(
   if (!out || !q || !k_cache || !v_cache || !block_tables || !context_lens)
     return LK_ERR_INVALID_ARG;
   if (dtype != LK_DTYPE_BF16 && dtype != LK_DTYPE_F16) return LK_ERR_UNSUPPORTED;
-  if (D != kD || block_size % kTok != 0 || H / H_kv > 8 || H_kv % 8 != 0) return LK_ERR_UNSUPPORTED;
+  if (D != kD || block_size % kTok != 0 || H / H_kv > 8) return LK_ERR_UNSUPPORTED;
   if (prefix_tokens <= 0 || prefix_tokens % block_size != 0 ||
       prefix_tokens > static_cast<int64_t>(max_blocks_per_seq) * block_size)
     return LK_ERR_INVALID_ARG;
@@ -1623,7 +1623,7 @@ extern "C" int lk_paged_decode_shared_prefix(
   if (rc != LK_OK) return rc;
 
   // 3. each row's own suffix on the split decode kernel, merged with the prefix
-  const int hpc = 8;
+  const int hpc = heads_per_cta(H_kv);
   const int64_t num_slots = num_blocks * block_size;
   CUtensorMap km, vm;
   rc = lk::get_kv_tensor_map(&km, k_cache, num_slots, H_kv, D, dtype, kTok, hpc);
@@ -1656,6 +1656,6 @@ extern "C" int lk_paged_decode_shared_prefix(
   p.work = reinterpret_cast<int*>(ws + 64);
   p.first_stage = prefix_tokens / kTok;
   p.part_offset = pl.ranges;
-  if (dtype == LK_DTYPE_BF16) return launch_decode<__nv_bfloat16, 8, 3>(km, vm, p, B, s, true);
-  return launch_decode<__half, 8, 3>(km, vm, p, B, s, true);
+  if (dtype == LK_DTYPE_BF16) return dispatch_decode<__nv_bfloat16>(hpc, km, vm, p, B, s, true);
+  return dispatch_decode<__half>(hpc, km, vm, p, B, s, true);
 }

@@ -153,7 +153,7 @@ def test_shared_prefix_decode_rejects_bad_arguments():
     assert f(*bad) == -1
     bad = list(args); bad[17] = 144 * 16 + 16                # prefix longer than the table
     assert f(*bad) == -1
-    bad = list(args); bad[12] = 4; bad[11] = 16              # H_kv not a multiple of 8
+    bad = list(args); bad[12] = 2                            # G = 16 unsupported
     assert f(*bad) == -2
     bad = list(args); bad[10] = 0                            # B = 0: nothing to do
     assert f(*bad) == 0

@@ -270,3 +270,12 @@ def test_shared_prefix_longer_than_a_row_is_flagged(cuda):
         6, 32, 8, 128, bt.shape[1], 16, 160), dtype=torch.uint8, device=cuda)
     ops.paged_decode_shared_prefix(q, kc, vc, bt, ctx, 128 ** -0.5, 160, workspace=ws)
     assert ops.decode_status(ws) & 8  # LK_STATUS_CTX_OOB
+
+
+@pytest.mark.parametrize("H,H_kv", [(32, 4), (8, 2), (4, 1), (16, 16)])
+def test_shared_prefix_decode_head_groupings(cuda, H, H_kv):
+    suffix = [3, 0, 77, 250, 16, 1]
+    q, kc, vc, bt, ctx = _shared_prefix_batch(cuda, 6, 12, suffix, H=H, H_kv=H_kv, seed=H + H_kv)
+    out = ops.paged_decode_shared_prefix(q, kc, vc, bt, ctx, 128 ** -0.5, 12 * 16)
+    ref = pa.decode(q.float(), kc.float(), vc.float(), bt, ctx, 128 ** -0.5)
+    assert_attn_close(out, ref)
