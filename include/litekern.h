@@ -174,6 +174,29 @@ int lk_paged_prefill(void* out, const void* q, int64_t q_token_stride,
                      float scale, int32_t dtype, int32_t* status, void* stream);
 
 /*
+ * lk_paged_prefill with a caller-owned workspace (same arguments and results;
+ * workspace NULL = lk_paged_prefill). The workspace (256-byte aligned, at
+ * least lk_paged_prefill_workspace_bytes() for key splits, any size from
+ * 197 KiB for the plan alone; no zero-fill needed, the planning kernel clears
+ * what it uses) holds the launch's work plan — (sequence, query tile) pairs
+ * ordered most key tiles first — and lets the tail of a launch with at most
+ * four waves of work items cut its longest late items into two key-range
+ * pieces, merged exactly in a fixed order (fp32 partials), so the last wave
+ * is made of shorter items. One workspace per stream. Without a workspace the
+ * plan lives in a small buffer the library keeps per (device, stream) and no
+ * item is cut.
+ */
+size_t lk_paged_prefill_workspace_bytes(void);
+int lk_paged_prefill_ws(void* out, const void* q, int64_t q_token_stride,
+                        const void* k_cache, const void* v_cache, int64_t num_blocks,
+                        const int32_t* block_tables, int64_t block_table_stride,
+                        const int32_t* cu_seqlens_q, const int32_t* context_lens,
+                        int32_t num_seqs, int32_t max_q_len,
+                        int32_t H, int32_t H_kv, int32_t D, int32_t block_size,
+                        float scale, int32_t dtype, void* workspace, size_t workspace_bytes,
+                        int32_t* status, void* stream);
+
+/*
  * Vocab-wide sampler. Replaces Sampler.sample's greedy path
  * (litevllm/layers/sampler.py:174-175 -> _argmax_kernel :60-84) and its
  * temperature path (:178, :187: softmax(logits / T) then torch.multinomial)

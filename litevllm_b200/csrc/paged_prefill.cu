@@ -58,6 +58,15 @@ struct PrefillParams {
   int32_t* status;
   int num_seqs, H_kv, nqt;  // persistent ping-pong kernel: work-item grid
   int* sched;               // its work-item counter (zeroed per launch)
+  // Work units of the ping-pong kernel, most key tiles first (NULL: tile-major
+  // order over nqt x num_seqs pairs). Unit = pair | piece << 14 | split << 16,
+  // pair = sequence * nqt + query tile; piece 0 = all key tiles, 1 / 2 = the
+  // first / second half of them (a key-split pair, merged through split_*).
+  const int* order;
+  const int* units_count;  // number of units in order
+  int* split_cnt;          // [split items][softmax warp][arrivals, ready]
+  float* split_ml;         // [split items][piece][256 rows][2] (m, l)
+  float* split_o;          // [split items][piece][256 rows][D] unnormalised o
   // Shared-prefix mode (decode rows against a prefix every row shares): the
   // B query rows are one "chunk" (q_len = prefix_rows), keys [0, prefix_len)
   // through block-table row 0 in key ranges of prefix_split tokens (num_seqs
@@ -752,7 +761,7 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
   __shared__ __align__(8) uint64_t q_full[2];     // [sub-tile]
   __shared__ __align__(8) uint64_t s_full[2];     // [sub-tile]
   __shared__ __align__(8) uint64_t p_full[2][2];  // [sub-tile][key half]
-  __shared__ __align__(8) uint64_t o_final;
+  __shared__ __align__(8) uint64_t o_final[2];   // [sub-tile]: its last PV completed
   __shared__ __align__(8) uint64_t item_full[2];   // work-item ring, depth 2
   __shared__ __align__(8) uint64_t item_empty[2];
   __shared__ int item_ring[2];
@@ -765,7 +774,8 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.G, BQ = p.BQ;
   const int per_q = p.H_kv * p.num_seqs;
-  const int num_items = p.nqt * per_q;
+  const int num_items =
+      (!PREFIX && p.order != nullptr) ? __ldg(p.units_count) * p.H_kv : p.nqt * per_q;
 
   // Work item w: all items of query tile nqt - 1 first, then nqt - 2, ...
   // (later tiles see more keys under the causal mask). The producer warp
@@ -776,9 +786,20 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
   };
   auto item = [&](int w) {
     Item it;
-    const int qt = p.nqt - 1 - w / per_q, rem = w % per_q;
-    it.kvh = rem % p.H_kv;
-    it.b = rem / p.H_kv;
+    int qt, piece = 0;
+    if (!PREFIX && p.order != nullptr) {
+      const int un = __ldg(p.order + w / p.H_kv);
+      const int pr = un & 0x3fff;
+      piece = (un >> 14) & 3;
+      it.kvh = w % p.H_kv;
+      it.b = pr / p.nqt;
+      qt = pr % p.nqt;
+    } else {
+      qt = p.nqt - 1 - w / per_q;
+      const int rem = w % per_q;
+      it.kvh = rem % p.H_kv;
+      it.b = rem / p.H_kv;
+    }
     if constexpr (PREFIX) {  // b = key range; every row sees the whole range
       it.q_start = 0;
       it.q_len = p.prefix_rows;
@@ -805,6 +826,15 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
     }
     it.kv_end = it.prior + min(it.q_len, it.pos0 + BQ);
     it.ntiles = it.pos0 < it.q_len ? (it.kv_end + kPpKT - 1) / kPpKT : 0;
+    if (piece != 0) {  // key-split pair: first or second half of the key tiles
+      const int a = (it.ntiles + 1) / 2;
+      if (piece == 1) {
+        it.ntiles = a;
+      } else {
+        it.kv_begin = a * kPpKT;
+        it.ntiles -= a;
+      }
+    }
     return it;
   };
 
@@ -819,7 +849,8 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
       lk::mbar_init(&p_full[i][0], 4);
       lk::mbar_init(&p_full[i][1], 4);
     }
-    lk::mbar_init(&o_final, 1);
+    lk::mbar_init(&o_final[0], 1);
+    lk::mbar_init(&o_final[1], 1);
     for (int i = 0; i < 2; ++i) {
       lk::mbar_init(&item_full[i], 1);
       lk::mbar_init(&item_empty[i], 9);  // the MMA thread + 8 softmax warps
@@ -997,11 +1028,11 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
             issue_pv(u, g, j == 0, 1);
             if (u == 1) lk::tc::commit(&v_empty[st]);
             if (more) issue_s(u, g + 1);  // S_u(j+1) after PV_u(j): P_u(j) is read first
+            else lk::tc::commit(&o_final[u]);  // O_u complete: its epilogue need not wait for the other sub-tile
           }
           if (!ok) break;
           if (more) lk::tc::commit(&k_empty[st ^ 1]);
         }
-        lk::tc::commit(&o_final);
         ++n_items;
       }
       if (!ok && p.status) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
@@ -1134,7 +1165,7 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
       // threads, i.e. for the end of the epilogue.
       const int wn = next_item(n_items + 1, ok);
       if (wn < num_items) load_q(item(wn));
-      if (ok && lk::mbar_wait(&o_final, n_items & 1)) {
+      if (ok && lk::mbar_wait(&o_final[u], n_items & 1)) {
         if (wn < num_items) publish_q();
         lk::tc::fence_after();
         if constexpr (PREFIX) {
@@ -1158,24 +1189,115 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
             p.part_ml[prow * 2] = m_used;
             p.part_ml[prow * 2 + 1] = l;
           }
+        } else if (p.order != nullptr && (__ldg(p.order + w / p.H_kv) >> 14) != 0) {
+          // Key-split pair, per warp (32 rows): the piece that arrives first
+          // writes its (m, l, unnormalised o) to the workspace and raises a
+          // ready flag; the one that arrives second waits for the flag (the
+          // first is resident and past all its waits: only stores remain;
+          // the wait is bounded all the same), reads that partial and merges
+          // it with its own O from TMEM. The merge puts piece 1's term first
+          // whichever piece runs it, so the bits do not depend on the order.
+          // Partials are [piece][16-byte d chunk][256 rows]: a warp's store
+          // or load of one chunk covers 512 contiguous bytes.
+          const int un = __ldg(p.order + w / p.H_kv);
+          const int64_t slot = static_cast<int64_t>(un >> 16) * p.H_kv + it.kvh;
+          const int piece = (un >> 14) & 3;
+          int* cnt = p.split_cnt + (slot * 8 + warp) * 2;  // [arrivals, ready]
+          int arrival = 0;
+          if (lane == 0) arrival = atomicAdd(cnt, 1);
+          arrival = __shfl_sync(0xffffffffu, arrival, 0);
+          if (arrival == 0) {
+            float4* po = reinterpret_cast<float4*>(p.split_o) + (slot * 2 + (piece - 1)) * 32 * 256 + t;
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4) {
+              uint32_t ov[32];
+              lk::tc::ld32(tO + lane_base + 32 * c4, ov);  // whole warp, every row
+              lk::tc::wait_ld();
+#pragma unroll
+              for (int c = 0; c < 8; ++c)
+                __stcg(po + (c4 * 8 + c) * 256,
+                       make_float4(__uint_as_float(ov[4 * c]), __uint_as_float(ov[4 * c + 1]),
+                                   __uint_as_float(ov[4 * c + 2]), __uint_as_float(ov[4 * c + 3])));
+            }
+            __stcg(reinterpret_cast<float2*>(p.split_ml) + (slot * 2 + (piece - 1)) * 256 + t,
+                   make_float2(m_used, l));
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) atomicExch(cnt + 1, 1);
+          } else {
+            bool ready = true;
+            if (lane == 0) {
+              const uint64_t t0 = lk::globaltimer_ns();
+              while (atomicAdd(cnt + 1, 0) == 0) {
+                if (lk::globaltimer_ns() - t0 > lk::kWaitTimeoutNs) {
+                  ready = false;
+                  if (p.status) atomicOr(p.status, LK_STATUS_WAIT_TIMEOUT);
+                  break;
+                }
+                __nanosleep(64);
+              }
+              cnt[0] = 0;  // both pieces have arrived: leave the counters zero
+              cnt[1] = 0;
+            }
+            ready = __shfl_sync(0xffffffffu, ready ? 1 : 0, 0) != 0;
+            __threadfence();
+            const float2 mo = __ldcg(reinterpret_cast<const float2*>(p.split_ml) +
+                                     (slot * 2 + (2 - piece)) * 256 + t);
+            const float2 ml1 = piece == 1 ? make_float2(m_used, l) : mo;
+            const float2 ml2 = piece == 1 ? mo : make_float2(m_used, l);
+            const float mm = fmaxf(ml1.x, ml2.x);  // finite: piece 1 always sees key 0
+            const float a1 = exp2f(ml1.x - mm), a2 = exp2f(ml2.x - mm);
+            const float inv = 1.f / (ml1.y * a1 + ml2.y * a2);
+            const float w1 = a1 * inv, w2 = a2 * inv;
+            const float4* oo = reinterpret_cast<const float4*>(p.split_o) +
+                               (slot * 2 + (2 - piece)) * 32 * 256 + t;
+            T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(it.q_start + pos) * p.H * kD +
+                      static_cast<int64_t>(it.kvh * G + gh) * kD;
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4) {
+              uint32_t ov[32];
+              lk::tc::ld32(tO + lane_base + 32 * c4, ov);  // whole warp, every row
+              lk::tc::wait_ld();
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                const float4 y0 = __ldcg(oo + (c4 * 8 + 2 * c) * 256);
+                const float4 y1 = __ldcg(oo + (c4 * 8 + 2 * c + 1) * 256);
+                const float yv[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
+                uint32_t o4[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float s0 = __uint_as_float(ov[c * 8 + 2 * e]);
+                  const float s1 = __uint_as_float(ov[c * 8 + 2 * e + 1]);
+                  const float p0 = piece == 1 ? s0 : yv[2 * e], q0 = piece == 1 ? yv[2 * e] : s0;
+                  const float p1 = piece == 1 ? s1 : yv[2 * e + 1], q1 = piece == 1 ? yv[2 * e + 1] : s1;
+                  o4[e] = lk::pack2<T>(p0 * w1 + q0 * w2, p1 * w1 + q1 * w2);
+                }
+                if (ready && pos < it.q_len)
+                  *reinterpret_cast<uint4*>(orow + c4 * 32 + c * 8) =
+                      make_uint4(o4[0], o4[1], o4[2], o4[3]);
+              }
+            }
+          }
         } else {
         const float inv = 1.f / l;
         T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(it.q_start + pos) * p.H * kD +
                   static_cast<int64_t>(it.kvh * G + gh) * kD;
+        // two 32-column TMEM loads in flight per wait (the loop's registers are free here)
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint32_t ov[32];
-          lk::tc::ld32(tO + lane_base + 32 * c4, ov);  // whole warp, every row
+        for (int c8 = 0; c8 < 2; ++c8) {
+          uint32_t ov[2][32];
+          lk::tc::ld32(tO + lane_base + 64 * c8, ov[0]);  // whole warp, every row
+          lk::tc::ld32(tO + lane_base + 64 * c8 + 32, ov[1]);
           lk::tc::wait_ld();
           if (pos < it.q_len) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 8; ++c) {
               uint32_t o4[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e)
-                o4[e] = lk::pack2<T>(__uint_as_float(ov[c * 8 + 2 * e]) * inv,
-                                     __uint_as_float(ov[c * 8 + 2 * e + 1]) * inv);
-              *reinterpret_cast<uint4*>(orow + c4 * 32 + c * 8) =
+                o4[e] = lk::pack2<T>(__uint_as_float(ov[c >> 2][(c & 3) * 8 + 2 * e]) * inv,
+                                     __uint_as_float(ov[c >> 2][(c & 3) * 8 + 2 * e + 1]) * inv);
+              *reinterpret_cast<uint4*>(orow + c8 * 64 + c * 8) =
                   make_uint4(o4[0], o4[1], o4[2], o4[3]);
             }
           }
@@ -1198,9 +1320,199 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
   if (warp == 9) lk::tc::dealloc(tmem, 512);
 }
 
-// Work-item counter of the persistent kernel, one per (device, stream) so
-// that launches on different streams never share one; zeroed before each
-// launch on the launch stream.
+// Work plan of the ping-pong kernel, made on the device by one CTA before
+// each launch (it also zeroes the work-item counter, so it replaces the
+// counter's memset).
+//  * Longest first. Items of one (sequence, query tile) pair have the same
+//    number of key tiles for every KV head, and that number grows with the
+//    sequence's prior context, not only with the query tile: a tile-major
+//    order leaves SMs that drew a long item early to draw a second long one
+//    at the end. Pairs are counted into key-tile buckets, scanned from the
+//    longest bucket down and scattered.
+//  * Key split of the tail. When the launch has at most four waves of items,
+//    pairs whose items start after the first wave and have at least half the
+//    key tiles of the longest pair (and >= 4) are
+//    cut into two pieces of half the tiles each (merged through the
+//    workspace by whichever piece ends second), and the pieces are ordered
+//    with the rest by length: the last wave is then made of shorter items.
+//    At most cap_split pairs are cut (the workspace's room), the earliest in
+//    the longest-first order.
+// Within a bucket the order is arbitrary: items are independent, only the
+// timing depends on it.
+constexpr int kOrderCap = 16384;     // pairs the plan can order (pair ids fit 14 bits)
+constexpr int kOrderBuckets = 1024;  // key-tile counts >= 1023 share the last bucket
+constexpr int kPlanHeaderBytes = 256;
+constexpr size_t kPlanBytes = kPlanHeaderBytes + sizeof(int) * 3 * kOrderCap;  // + pairs + units
+constexpr size_t kSplitItemBytes = 16 * sizeof(int) + 2 * 256 * 2 * sizeof(float) +
+                                   2 * 256 * kD * sizeof(float);
+
+// Exclusive scan over the 1024 threads of the block; *total gets the sum.
+LK_DEVINL int block_exclusive_scan(int v, int* warp_tot, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_tot[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int t = warp_tot[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    warp_tot[lane] = t;  // inclusive
+  }
+  __syncthreads();
+  const int r = x - v + (warp > 0 ? warp_tot[warp - 1] : 0);
+  *total = warp_tot[31];
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(1024)
+prefill_plan_kernel(const int32_t* __restrict__ cu_seqlens_q,
+                    const int32_t* __restrict__ context_lens, int num_seqs, int nqt, int BQ,
+                    int H_kv, int num_sms, int cap_split, int* __restrict__ header,
+                    int* __restrict__ pairs, int* __restrict__ units,
+                    int* __restrict__ split_cnt) {
+  __shared__ int hist[kOrderBuckets];
+  __shared__ int warp_tot[32];
+  __shared__ int n_valid;
+  const int tid = threadIdx.x;
+  const int n = num_seqs * nqt;
+  hist[tid] = 0;
+  if (tid == 0) {
+    header[0] = 0;  // work-item counter of the launch that follows
+    n_valid = 0;
+  }
+  for (int i = tid; i < 16 * cap_split * H_kv; i += 1024) split_cnt[i] = 0;
+  __syncthreads();
+  auto ntiles = [&](int pr) {
+    const int b = pr / nqt, qt = pr % nqt;
+    const int q_start = __ldg(cu_seqlens_q + b), q_len = __ldg(cu_seqlens_q + b + 1) - q_start;
+    const int pos0 = qt * BQ;
+    if (pos0 >= q_len) return 0;
+    const int prior = context_lens ? max(__ldg(context_lens + b) - q_len, 0) : 0;
+    return (prior + min(q_len, pos0 + BQ) + 127) / 128;
+  };
+  auto bucket = [](int nt) { return kOrderBuckets - 1 - min(nt, kOrderBuckets - 1); };
+  int total;
+  // 1. pairs, longest first
+  for (int pr = tid; pr < n; pr += 1024) {
+    const int nt = ntiles(pr);
+    if (nt > 0) atomicAdd(&n_valid, 1);
+    atomicAdd(&hist[bucket(nt)], 1);
+  }
+  __syncthreads();
+  hist[tid] = block_exclusive_scan(hist[tid], warp_tot, &total);
+  __syncthreads();
+  for (int pr = tid; pr < n; pr += 1024) pairs[atomicAdd(&hist[bucket(ntiles(pr))], 1)] = pr;
+  __syncthreads();
+  // 2. which pairs to cut (contiguous positions per thread, so split ids
+  // follow the longest-first order); the id + 1 goes to bits 14.. of the pair
+  const bool enable = cap_split > 0 && static_cast<int64_t>(n_valid) * H_kv <= 4LL * num_sms;
+  const int seg = (n + 1023) / 1024, k0 = min(n, tid * seg), k1 = min(n, k0 + seg);
+  const int min_cut = n > 0 ? max(4, (ntiles(pairs[0] & 0x3fff) + 1) / 2) : 4;
+  auto cut = [&](int k, int nt) {
+    return enable && static_cast<int64_t>(k + 1) * H_kv > num_sms && nt >= min_cut;
+  };
+  int cnt = 0;
+  for (int k = k0; k < k1; ++k) cnt += cut(k, ntiles(pairs[k])) ? 1 : 0;
+  int sid = block_exclusive_scan(cnt, warp_tot, &total);
+  const int nsplit = min(total, cap_split);
+  for (int k = k0; k < k1; ++k) {
+    const int pr = pairs[k];
+    if (cut(k, ntiles(pr))) {
+      if (sid < cap_split) pairs[k] = pr | ((sid + 1) << 14);
+      ++sid;
+    }
+  }
+  hist[tid] = 0;
+  __syncthreads();
+  // 3. units (whole pairs and pieces), longest first
+  for (int k = tid; k < n; k += 1024) {
+    const int e = pairs[k], nt = ntiles(e & 0x3fff);
+    if (e >> 14) {
+      atomicAdd(&hist[bucket((nt + 1) / 2)], 1);
+      atomicAdd(&hist[bucket(nt / 2)], 1);
+    } else {
+      atomicAdd(&hist[bucket(nt)], 1);
+    }
+  }
+  __syncthreads();
+  hist[tid] = block_exclusive_scan(hist[tid], warp_tot, &total);
+  __syncthreads();
+  for (int k = tid; k < n; k += 1024) {
+    const int e = pairs[k], pr = e & 0x3fff, nt = ntiles(pr), s1 = e >> 14;
+    if (s1) {
+      const int id = (s1 - 1) << 16;
+      units[atomicAdd(&hist[bucket((nt + 1) / 2)], 1)] = pr | (1 << 14) | id;
+      units[atomicAdd(&hist[bucket(nt / 2)], 1)] = pr | (2 << 14) | id;
+    } else {
+      units[atomicAdd(&hist[bucket(nt)], 1)] = pr;
+    }
+  }
+  if (tid == 0) header[1] = n + nsplit;
+}
+
+// Longest-first plan on (LITEKERN_PREFILL_ORDER=0 turns it off) and key
+// splits of the tail on (LITEKERN_PREFILL_SPLIT=0 turns them off); read once.
+bool env_on(const char* name) {
+  const char* e = getenv(name);
+  return !(e && atoi(e) == 0);
+}
+bool use_prefill_order() {
+  static int v = env_on("LITEKERN_PREFILL_ORDER") ? 1 : 0;
+  return v != 0;
+}
+bool use_prefill_split() {
+  static int v = env_on("LITEKERN_PREFILL_SPLIT") ? 1 : 0;
+  return v != 0;
+}
+
+// Where the plan and the key-split partials live: the caller's workspace, or
+// (no workspace: no splits) a buffer kept per (device, stream) so that
+// launches on different streams never share one.
+struct PrefillWs {
+  int* header;  // [0] work-item counter, [1] number of units
+  int* pairs;
+  int* units;
+  int* split_cnt;
+  float* split_ml;
+  float* split_o;
+  int cap_split_items;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+size_t prefill_ws_bytes(int cap) {
+  return kPlanBytes + align256(sizeof(int) * 16 * cap) + align256(sizeof(float) * 2 * 256 * 2 * cap) +
+         sizeof(float) * 2 * 256 * kD * cap;
+}
+
+PrefillWs prefill_ws_layout(void* ws, size_t bytes) {
+  PrefillWs w{};
+  uint8_t* b = static_cast<uint8_t*>(ws);
+  w.header = reinterpret_cast<int*>(b);
+  w.pairs = w.header + kPlanHeaderBytes / sizeof(int);
+  w.units = w.pairs + kOrderCap;
+  int cap = bytes > kPlanBytes ? static_cast<int>((bytes - kPlanBytes) / kSplitItemBytes) : 0;
+  cap = min(cap, lk::num_sms());
+  while (cap > 0 && prefill_ws_bytes(cap) > bytes) --cap;
+  w.cap_split_items = cap;
+  uint8_t* c = b + kPlanBytes;
+  w.split_cnt = reinterpret_cast<int*>(c);
+  c += align256(sizeof(int) * 16 * cap);
+  w.split_ml = reinterpret_cast<float*>(c);
+  c += align256(sizeof(float) * 2 * 256 * 2 * cap);
+  w.split_o = reinterpret_cast<float*>(c);
+  return w;
+}
+
 int* sched_counter(cudaStream_t s) {
   struct Entry {
     int dev;
@@ -1215,14 +1527,15 @@ int* sched_counter(cudaStream_t s) {
   for (const Entry& e : table)
     if (e.dev == dev && e.stream == s) return e.ptr;
   int* ptr = nullptr;
-  if (cudaMalloc(&ptr, 256) != cudaSuccess) return nullptr;
+  if (cudaMalloc(&ptr, kPlanBytes) != cudaSuccess) return nullptr;
   table.push_back({dev, s, ptr});
   return ptr;
 }
 
 template <typename T>
 int launch_prefill_pp(const CUtensorMap& km, const CUtensorMap& vm, PrefillParams p,
-                      int num_seqs, int max_q_len, int H_kv, cudaStream_t s) {
+                      int num_seqs, int max_q_len, int H_kv, void* workspace,
+                      size_t workspace_bytes, cudaStream_t s) {
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1234,14 +1547,41 @@ int launch_prefill_pp(const CUtensorMap& km, const CUtensorMap& vm, PrefillParam
   }
   p.BQ = 256 / p.G;
   p.nqt = (max_q_len + p.BQ - 1) / p.BQ;
-  p.sched = sched_counter(s);
-  if (p.sched == nullptr) return LK_ERR_CUDA;
-  if (cudaMemsetAsync(p.sched, 0, sizeof(int), s) != cudaSuccess) return LK_ERR_CUDA;
   p.num_seqs = num_seqs;
   p.H_kv = H_kv;
   const int64_t items = static_cast<int64_t>(p.nqt) * H_kv * num_seqs;
   if (items > 0x7fffffffLL) return LK_ERR_TOO_LARGE;
-  const int grid = static_cast<int>(items < lk::num_sms() ? items : lk::num_sms());
+  PrefillWs w{};
+  if (workspace != nullptr) {
+    w = prefill_ws_layout(workspace, workspace_bytes);
+  } else {
+    w.header = sched_counter(s);
+    if (w.header == nullptr) return LK_ERR_CUDA;
+    w.pairs = w.header + kPlanHeaderBytes / sizeof(int);
+    w.units = w.pairs + kOrderCap;
+  }
+  p.sched = w.header;
+  p.order = nullptr;
+  p.units_count = nullptr;
+  p.split_cnt = w.split_cnt;
+  p.split_ml = w.split_ml;
+  p.split_o = w.split_o;
+  const int64_t pairs = static_cast<int64_t>(p.nqt) * num_seqs;
+  if (pairs <= kOrderCap && use_prefill_order()) {
+    const int cap_split = use_prefill_split() ? w.cap_split_items / H_kv : 0;
+    prefill_plan_kernel<<<1, 1024, 0, s>>>(
+        p.cu_seqlens_q, (p.block_tables && p.context_lens) ? p.context_lens : nullptr,
+        num_seqs, p.nqt, p.BQ, H_kv, lk::num_sms(), cap_split, w.header, w.pairs, w.units,
+        w.split_cnt);
+    p.order = w.units;
+    p.units_count = w.header + 1;
+  } else if (cudaMemsetAsync(p.sched, 0, sizeof(int), s) != cudaSuccess) {
+    return LK_ERR_CUDA;
+  }
+  // A split turns one pair into two units: at most twice the pairs' items.
+  const int64_t max_items = p.order ? 2 * items : items;
+  if (max_items > 0x7fffffffLL) return LK_ERR_TOO_LARGE;
+  const int grid = static_cast<int>(max_items < lk::num_sms() ? max_items : lk::num_sms());
   paged_prefill_pp_kernel<T, false><<<grid, kPpThreads, kPpSmem, s>>>(km, vm, p);
   return lk::check_launch();
 }
@@ -1264,6 +1604,11 @@ int launch_prefix_pp(const CUtensorMap& km, const CUtensorMap& vm, PrefillParams
   p.BQ = 256 / p.G;
   p.nqt = (B + p.BQ - 1) / p.BQ;
   p.H_kv = H_kv;
+  p.order = nullptr;
+  p.units_count = nullptr;
+  p.split_cnt = nullptr;
+  p.split_ml = nullptr;
+  p.split_o = nullptr;
   const int64_t items = static_cast<int64_t>(p.nqt) * H_kv * p.num_seqs;
   if (items > 0x7fffffffLL) return LK_ERR_TOO_LARGE;
   if (zeroed_counter != nullptr) {  // zeroed earlier on this stream by the caller
@@ -1299,13 +1644,21 @@ bool use_mma_sync() {
 
 }  // namespace
 
-extern "C" int lk_paged_prefill(void* out, const void* q, int64_t q_token_stride,
-                                const void* k_cache, const void* v_cache, int64_t num_blocks,
-                                const int32_t* block_tables, int64_t block_table_stride,
-                                const int32_t* cu_seqlens_q, const int32_t* context_lens,
-                                int32_t num_seqs, int32_t max_q_len, int32_t H, int32_t H_kv,
-                                int32_t D, int32_t block_size, float scale, int32_t dtype,
-                                int32_t* status, void* stream) {
+extern "C" size_t lk_paged_prefill_workspace_bytes(void) {
+  return prefill_ws_bytes(lk::num_sms());
+}
+
+extern "C" int lk_paged_prefill_ws(void* out, const void* q, int64_t q_token_stride,
+                                   const void* k_cache, const void* v_cache, int64_t num_blocks,
+                                   const int32_t* block_tables, int64_t block_table_stride,
+                                   const int32_t* cu_seqlens_q, const int32_t* context_lens,
+                                   int32_t num_seqs, int32_t max_q_len, int32_t H, int32_t H_kv,
+                                   int32_t D, int32_t block_size, float scale, int32_t dtype,
+                                   void* workspace, size_t workspace_bytes, int32_t* status,
+                                   void* stream) {
+  if (workspace != nullptr &&
+      ((reinterpret_cast<uintptr_t>(workspace) & 255u) || workspace_bytes < kPlanBytes))
+    return workspace_bytes < kPlanBytes ? LK_ERR_INVALID_ARG : LK_ERR_ALIGNMENT;
   if (num_seqs < 0 || max_q_len < 0 || H <= 0 || H_kv <= 0 || H % H_kv != 0 || num_blocks <= 0)
     return LK_ERR_INVALID_ARG;
   if (num_seqs == 0 || max_q_len == 0) return LK_OK;
@@ -1332,7 +1685,7 @@ extern "C" int lk_paged_prefill(void* out, const void* q, int64_t q_token_stride
   if (rc != LK_OK) return rc;
   rc = lk::get_kv_tensor_map(&vm, v_cache, num_slots, H_kv, D, dtype, 16, 1);
   if (rc != LK_OK) return rc;
-  PrefillParams p;
+  PrefillParams p{};
   p.out = out;
   p.q = q;
   p.q_stride = q_token_stride;
@@ -1351,8 +1704,10 @@ extern "C" int lk_paged_prefill(void* out, const void* q, int64_t q_token_stride
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (!use_mma_sync() && use_pingpong()) {
     if (dtype == LK_DTYPE_BF16)
-      return launch_prefill_pp<__nv_bfloat16>(km, vm, p, num_seqs, max_q_len, H_kv, s);
-    return launch_prefill_pp<__half>(km, vm, p, num_seqs, max_q_len, H_kv, s);
+      return launch_prefill_pp<__nv_bfloat16>(km, vm, p, num_seqs, max_q_len, H_kv, workspace,
+                                              workspace_bytes, s);
+    return launch_prefill_pp<__half>(km, vm, p, num_seqs, max_q_len, H_kv, workspace,
+                                     workspace_bytes, s);
   }
   if (!use_mma_sync()) {
     if (dtype == LK_DTYPE_BF16)
@@ -1362,6 +1717,18 @@ extern "C" int lk_paged_prefill(void* out, const void* q, int64_t q_token_stride
   if (dtype == LK_DTYPE_BF16)
     return launch_prefill<__nv_bfloat16>(km, vm, p, num_seqs, max_q_len, H_kv, s);
   return launch_prefill<__half>(km, vm, p, num_seqs, max_q_len, H_kv, s);
+}
+
+extern "C" int lk_paged_prefill(void* out, const void* q, int64_t q_token_stride,
+                                const void* k_cache, const void* v_cache, int64_t num_blocks,
+                                const int32_t* block_tables, int64_t block_table_stride,
+                                const int32_t* cu_seqlens_q, const int32_t* context_lens,
+                                int32_t num_seqs, int32_t max_q_len, int32_t H, int32_t H_kv,
+                                int32_t D, int32_t block_size, float scale, int32_t dtype,
+                                int32_t* status, void* stream) {
+  return lk_paged_prefill_ws(out, q, q_token_stride, k_cache, v_cache, num_blocks, block_tables,
+                             block_table_stride, cu_seqlens_q, context_lens, num_seqs, max_q_len,
+                             H, H_kv, D, block_size, scale, dtype, nullptr, 0, status, stream);
 }
 
 namespace lk {

@@ -278,6 +278,7 @@ def paged_prefill(
     context_lens: Optional[torch.Tensor] = None,
     out: Optional[torch.Tensor] = None,
     status: Optional[torch.Tensor] = None,
+    workspace: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """Causal attention for prefill chunks over prior paged context.
 
@@ -288,7 +289,7 @@ def paged_prefill(
     every sequence starts at position 0 (Attention._prefill,
     litevllm/layers/attention.py:141-151).
     """
-    dev = _cuda(query, key_cache, value_cache, cu_seqlens_q, block_tables, context_lens, out, status)
+    dev = _cuda(query, key_cache, value_cache, cu_seqlens_q, block_tables, context_lens, out, status, workspace)
     if query.dim() != 3:
         raise ValueError("query must be [T, H, D]")
     T, H, D = query.shape
@@ -328,13 +329,20 @@ def paged_prefill(
         raise ValueError("bad out tensor")
     if S <= 0 or T == 0:
         return out
+    need = int(lib().lk_paged_prefill_workspace_bytes())
+    if workspace is None:
+        # one per stream: the plan and the split partials belong to one launch at a time
+        workspace = WORKSPACES.get(dev, f"prefill:{_stream(dev)}", need)
+    elif workspace.numel() * workspace.element_size() < need:
+        raise ValueError(f"workspace too small: need {need} bytes")
     with _on(dev):
         check(
-            lib().lk_paged_prefill(
+            lib().lk_paged_prefill_ws(
                 out.data_ptr(), query.data_ptr(), query.stride(0), key_cache.data_ptr(),
                 value_cache.data_ptr(), num, _ptr(block_tables), bt_stride,
                 cu_seqlens_q.data_ptr(), _ptr(context_lens), S, int(max_q_len), H, H_kv, D, bs,
-                float(scale), code, _ptr(status), _stream(dev),
+                float(scale), code, workspace.data_ptr(),
+                workspace.numel() * workspace.element_size(), _ptr(status), _stream(dev),
             )
         )
     return out

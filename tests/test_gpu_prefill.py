@@ -137,7 +137,9 @@ def test_prefill_block_out_of_range_flags_status(cuda):
 
 @pytest.mark.parametrize("variant", ["LITEKERN_PREFILL_KERNEL=single",
                                      "LITEKERN_PREFILL_KERNEL=pingpong",
-                                     "LITEKERN_PREFILL_MMA_SYNC=1"])
+                                     "LITEKERN_PREFILL_MMA_SYNC=1",
+                                     "LITEKERN_PREFILL_ORDER=0",
+                                     "LITEKERN_PREFILL_SPLIT=0"])
 def test_prefill_kernel_options(variant):
     """The kernels kept as options (chosen once per process from the
     environment) against the oracle, in a child process."""
@@ -151,3 +153,84 @@ def test_prefill_kernel_options(variant):
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     assert "ok" in r.stdout
+
+
+def test_prefill_more_pairs_than_the_order_buffer(cuda):
+    """More (sequence, query tile) pairs than the longest-first order buffer
+    holds (16384): the kernel falls back to tile-major order. One-token
+    sequences in contiguous mode attend to their own key only, so each output
+    row is that token's value row exactly."""
+    n, H = 16500, 8
+    g = torch.Generator(device=cuda).manual_seed(12)
+    q = torch.randn((n, H, 128), device=cuda, generator=g).bfloat16()
+    k = torch.randn((n, H, 128), device=cuda, generator=g).bfloat16()
+    v = torch.randn((n, H, 128), device=cuda, generator=g).bfloat16()
+    cu = torch.arange(n + 1, dtype=torch.int32, device=cuda)
+    out = ops.paged_prefill(q, k, v, cu, 1, 128 ** -0.5)
+    assert torch.equal(out, v)
+    # and just under the limit, ordered
+    m = 16000
+    out = ops.paged_prefill(q[:m], k[:m], v[:m], cu[: m + 1], 1, 128 ** -0.5)
+    assert torch.equal(out, v[:m])
+
+
+def _units_planned(dev):
+    """Units of the last prefill plan on the current stream (workspace header)."""
+    ws = ops.WORKSPACES.get(dev, f"prefill:{torch.cuda.current_stream(dev).cuda_stream}", 0)
+    return int(ws[4:8].view(torch.int32).item())
+
+
+@pytest.mark.parametrize("H,H_kv", [(32, 8), (8, 8), (64, 8), (16, 2)])
+def test_prefill_key_split_tail(cuda, H, H_kv):
+    """Few waves of items on very different priors: the plan cuts the late
+    long pairs into two key-range pieces (more units than pairs) and the
+    merged rows match the oracle, including rows that see no key of the
+    second piece."""
+    q_lens, prior = [512] * 4, [1986, 2952, 408, 2864]
+    _paged_case(cuda, q_lens, prior, H=H, H_kv=H_kv, seed=H + H_kv)
+    BQ = 256 // (H // H_kv)
+    pairs = 4 * ((512 + BQ - 1) // BQ)
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    if sms < pairs * H_kv <= 4 * sms:  # a second wave, at most four: the tail is cut
+        assert _units_planned(cuda) > pairs
+    else:
+        assert _units_planned(cuda) == pairs
+
+
+def test_prefill_key_split_is_deterministic(cuda):
+    """Either piece may end second; the merge order is fixed, so repeated
+    launches give identical bits."""
+    b, out = _paged_case(cuda, [512] * 4, [1986, 2952, 408, 2864], seed=31)
+    for _ in range(5):
+        again = ops.paged_prefill(b.query, b.key_cache, b.value_cache, b.cu_seqlens_q, 512,
+                                  b.scale, block_tables=b.block_tables,
+                                  context_lens=b.context_lens)
+        assert torch.equal(again, out)
+
+
+def test_prefill_workspace_too_small_raises(cuda):
+    b = workloads.make_prefill_batch([64], [0], seed=32, device=cuda)
+    small = torch.zeros(200 * 1024, dtype=torch.uint8, device=cuda)
+    with pytest.raises(ValueError):
+        ops.paged_prefill(b.query, b.key_cache, b.value_cache, b.cu_seqlens_q, 64, b.scale,
+                          block_tables=b.block_tables, context_lens=b.context_lens,
+                          workspace=small)
+
+
+def test_prefill_entry_without_workspace(cuda):
+    """lk_paged_prefill (no workspace: plan in the library's per-stream
+    buffer, no key splits) on the tail-split case, straight through the C ABI."""
+    from litevllm_b200._lib import LK_DTYPE_BF16, check, lib
+    q_lens, prior = [512] * 4, [1986, 2952, 408, 2864]
+    b = workloads.make_prefill_batch(q_lens, prior, seed=33, device=cuda)
+    ops.store_kvcache(b.key, b.value, b.key_cache, b.value_cache, b.slot_mapping)
+    out = torch.empty_like(b.query)
+    nb, bs, H_kv, D = b.key_cache.shape
+    check(lib().lk_paged_prefill(
+        out.data_ptr(), b.query.data_ptr(), b.query.stride(0), b.key_cache.data_ptr(),
+        b.value_cache.data_ptr(), nb, b.block_tables.data_ptr(), b.block_tables.stride(0),
+        b.cu_seqlens_q.data_ptr(), b.context_lens.data_ptr(), 4, 512, b.query.shape[1], H_kv, D,
+        bs, b.scale, LK_DTYPE_BF16, None, torch.cuda.current_stream().cuda_stream))
+    ref = pa.prefill(b.query.float(), b.key_cache.float(), b.value_cache.float(), b.block_tables,
+                     b.context_lens, b.cu_seqlens_q, b.scale)
+    assert_attn_close(out, ref)
