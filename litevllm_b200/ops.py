@@ -57,10 +57,11 @@ def _on(dev: torch.device):
 
 
 class _Workspaces:
-    """Zero-initialised scratch buffers, one per (device, purpose).
+    """Zero-initialised scratch buffers, one per (device, purpose, stream).
 
     The kernels leave their counter regions zero after every call, so a
-    buffer is reused across calls on one stream without re-clearing.
+    buffer is reused across calls on one stream without re-clearing; calls on
+    different streams may run at the same time, so each stream has its own.
     """
 
     def __init__(self) -> None:
@@ -178,7 +179,7 @@ def paged_decode(
         num_splits = decode_num_splits(B, H_kv, max_blocks, bs)
     need = decode_workspace_bytes(B, H, H_kv, D, num_splits)
     if workspace is None:
-        workspace = WORKSPACES.get(dev, "decode", need)
+        workspace = WORKSPACES.get(dev, f"decode:{_stream(dev)}", need)
     elif workspace.numel() * workspace.element_size() < need:
         raise ValueError(f"workspace too small: need {need} bytes")
     with _on(dev):
@@ -239,7 +240,7 @@ def paged_decode_shared_prefix(
     if need == 0:
         raise ValueError("invalid shared-prefix decode shape")
     if workspace is None:
-        workspace = WORKSPACES.get(dev, "decode", need)
+        workspace = WORKSPACES.get(dev, f"decode:{_stream(dev)}", need)
     elif workspace.numel() * workspace.element_size() < need:
         raise ValueError(f"workspace too small: need {need} bytes")
     with _on(dev):
@@ -257,10 +258,10 @@ def paged_decode_shared_prefix(
 
 def decode_status(workspace: Optional[torch.Tensor] = None, device=None) -> int:
     """Read (and clear) the LK_STATUS_* bits the decode kernels left in their
-    workspace. Synchronises the current stream."""
+    workspace (by default the current stream's). Synchronises the current stream."""
     if workspace is None:
         dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
-        workspace = WORKSPACES.get(dev, "decode", 256)
+        workspace = WORKSPACES.get(dev, f"decode:{_stream(dev)}", 256)
     v = int(workspace[:4].view(torch.int32).item())
     workspace[:4].zero_()
     return v
@@ -390,7 +391,7 @@ def sample(
         return out
     need = int(lib().lk_sample_workspace_bytes(B, V))
     if workspace is None:
-        workspace = WORKSPACES.get(dev, "sample", need)
+        workspace = WORKSPACES.get(dev, f"sample:{_stream(dev)}", need)
     with _on(dev):
         check(
             lib().lk_sample(

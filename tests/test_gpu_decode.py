@@ -118,6 +118,25 @@ def test_decode_config5_long_context_subset(cuda):
     _check(b)
 
 
+def test_decode_two_streams_concurrently(cuda):
+    """Split decodes on two streams at once: each stream has its own default
+    workspace (counters, partials, ordering), so neither corrupts the other."""
+    cases = [workloads.make_decode_batch(2, 64, seed=s, device=cuda) for s in (41, 42)]
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    for _ in range(3):
+        outs = []
+        for b, st in zip(cases, streams):
+            with torch.cuda.stream(st):
+                outs.append(ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables,
+                                             b.context_lens, b.scale, num_splits=4))
+    torch.cuda.synchronize()
+    for b, out in zip(cases, outs):
+        ref = pa.decode(b.query.float(), b.key_cache.float(), b.value_cache.float(),
+                        b.block_tables, b.context_lens, b.scale)
+        assert_attn_close(out, ref)
+
+
 def test_decode_out_of_range_block_flags_status(cuda):
     b = workloads.make_decode_batch(2, 2, seed=17, device=cuda, ctx=[40, 40])
     nb = b.key_cache.shape[0]

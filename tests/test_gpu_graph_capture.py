@@ -25,10 +25,11 @@ def test_decode_step_graph_replay_matches_eager(cuda):
                          b.scale, num_splits=nsplit, out=out)
         ops.sample(logits, None, out=ids)
 
-    step()  # first calls: workspaces, tensor maps, function attributes
-    torch.cuda.synchronize()
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()  # first calls on the capture stream: workspaces, tensor maps, function attributes
+    torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.stream(s):
         with torch.cuda.graph(g):
@@ -57,10 +58,11 @@ def test_shared_prefix_decode_graph_replay(cuda):
         ops.paged_decode_shared_prefix(b.query, b.key_cache, b.value_cache, b.block_tables,
                                        b.context_lens, b.scale, 127 * 16, out=out)
 
-    step()
-    torch.cuda.synchronize()
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.stream(s):
         with torch.cuda.graph(g):

@@ -25,9 +25,9 @@ def test_prefill_matches_reference_golden(cuda, tag):
     assert_attn_close(out, torch.from_numpy(d[f"{tag}_out"]))
 
 
-def _paged_case(cuda, q_lens, prior, H=32, H_kv=8, seed=0, dtype=torch.bfloat16):
+def _paged_case(cuda, q_lens, prior, H=32, H_kv=8, seed=0, dtype=torch.bfloat16, bs=16):
     b = workloads.make_prefill_batch(q_lens, prior, seed=seed, H=H, H_kv=H_kv, dtype=dtype,
-                                     device=cuda)
+                                     bs=bs, device=cuda)
     ops.store_kvcache(b.key, b.value, b.key_cache, b.value_cache, b.slot_mapping)
     out = ops.paged_prefill(b.query, b.key_cache, b.value_cache, b.cu_seqlens_q, max(q_lens),
                             b.scale, block_tables=b.block_tables, context_lens=b.context_lens)
@@ -234,3 +234,14 @@ def test_prefill_entry_without_workspace(cuda):
     ref = pa.prefill(b.query.float(), b.key_cache.float(), b.value_cache.float(), b.block_tables,
                      b.context_lens, b.cu_seqlens_q, b.scale)
     assert_attn_close(out, ref)
+
+
+def test_prefill_block_size_32(cuda):
+    """32-slot blocks: each block-table entry covers two 16-slot TMA boxes."""
+    _paged_case(cuda, [100, 37, 300], [45, 500, 0], seed=34, bs=32)
+
+
+def test_prefill_key_split_fp16(cuda):
+    """The key-split merge in fp16 (pieces merged in fp32, rounded once)."""
+    _paged_case(cuda, [512] * 4, [1986, 2952, 408, 2864], seed=35, dtype=torch.float16)
+    assert _units_planned(cuda) > 32
