@@ -8,12 +8,38 @@ runs the liblitekern CUDA kernels; there is no PyTorch or CPU fallback.
 
 from __future__ import annotations
 
-from typing import Optional
+import os
+from typing import Callable, Optional
 
 import torch
 import torch.nn as nn
 
 from . import ops
+
+# Mixed steps run the decode rows on a side stream next to the prefill chunks
+# (LITEKERN_MIXED_OVERLAP=0: one after the other on the caller's stream).
+MIXED_OVERLAP = os.environ.get("LITEKERN_MIXED_OVERLAP", "1") != "0"
+_SIDE_STREAMS: dict = {}
+
+
+def run_overlapped(first: Callable[[], None], second: Callable[[], None]) -> None:
+    """Run first() on the current stream and second() on a per-device side
+    stream forked from it, then join: the current stream continues only when
+    both are done. first() is launched first, so its grid takes the SMs and
+    second()'s blocks fill each SM as first()'s blocks retire (the persistent
+    prefill kernel's tail, where items run out unevenly, is then not idle).
+    Tensors second() reads or writes need no record_stream: the join orders
+    every later use on the current stream after them."""
+    main = torch.cuda.current_stream()
+    dev = main.device
+    side = _SIDE_STREAMS.get(dev)
+    if side is None:
+        side = _SIDE_STREAMS[dev] = torch.cuda.Stream(device=dev)
+    side.wait_stream(main)
+    first()
+    with torch.cuda.stream(side):
+        second()
+    main.wait_stream(side)
 
 # Shared-prefix hint for the current decode step, set by the engine hook that
 # builds the step's block tables (engine_hooks.prepare_inputs): the tensor it
@@ -146,21 +172,33 @@ class Attention(nn.Module):
         Rows [0, num_prefill_tokens) of query belong to the first
         num_prefill_seqs sequences (chunks, packed by cu_seqlens_q); the
         remaining rows are one decode token per sequence. All K/V are stored
-        first, then the prefill kernel and the decode kernel run back to back
-        on the same stream.
+        first; then the prefill kernel runs on the caller's stream and the
+        decode kernel on a side stream next to it (run_overlapped), joined
+        before returning.
         """
         if slot_mapping is not None:
             ops.store_kvcache(key, value, key_cache, value_cache, slot_mapping)
         out = torch.empty_like(query)
         P, TP = num_prefill_seqs, num_prefill_tokens
-        if P > 0:
+
+        def prefill():
             ops.paged_prefill(
                 query[:TP], key_cache, value_cache, cu_seqlens_q[: P + 1], max_q_len, self.scale,
                 block_tables=block_table[:P], context_lens=context_lens[:P], out=out[:TP],
             )
-        if query.shape[0] > TP:
+
+        def decode():
             ops.paged_decode(
                 query[TP:], key_cache, value_cache, block_table[P:], context_lens[P:], self.scale,
                 out=out[TP:],
             )
+
+        has_p, has_d = P > 0, query.shape[0] > TP
+        if has_p and has_d and MIXED_OVERLAP:
+            run_overlapped(prefill, decode)
+        else:
+            if has_p:
+                prefill()
+            if has_d:
+                decode()
         return out

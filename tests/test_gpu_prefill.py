@@ -82,6 +82,28 @@ def test_mixed_step_prefill_plus_decode(cuda):
     assert_attn_close(out, ref)
 
 
+def test_mixed_step_overlapped_equals_sequential(cuda, monkeypatch):
+    """forward_mixed's two-stream form (decode on a side stream next to the
+    prefill) gives the same bits as running them one after the other, and is
+    joined before returning (the result is read on the caller's stream)."""
+    from litevllm_b200 import attention as attn_mod
+    q_lens = [512, 300, 64] + [1] * 40
+    prior = [1000, 2900, 0] + list(range(50, 50 + 40 * 37, 37))
+    b = workloads.make_prefill_batch(q_lens, prior, seed=36, device=cuda)
+    attn = Attention(32, 128, 8)
+    args = (b.query, b.key, b.value, b.key_cache, b.value_cache, b.block_tables, b.slot_mapping,
+            b.context_lens, b.cu_seqlens_q)
+    kw = dict(num_prefill_seqs=3, num_prefill_tokens=876, max_q_len=512)
+    monkeypatch.setattr(attn_mod, "MIXED_OVERLAP", True)
+    over = attn.forward_mixed(*args, **kw)
+    monkeypatch.setattr(attn_mod, "MIXED_OVERLAP", False)
+    seq = attn.forward_mixed(*args, **kw)  # stores the same K/V again: idempotent
+    assert torch.equal(over, seq)
+    ref = pa.prefill(b.query.float(), b.key_cache.float(), b.value_cache.float(), b.block_tables,
+                     b.context_lens, b.cu_seqlens_q, b.scale)
+    assert_attn_close(over, ref)
+
+
 def test_prefill_many_ragged_items(cuda):
     """Far more work items than SMs, ragged chunk lengths and priors: every
     item is taken once from the persistent kernel's counter, and the query
