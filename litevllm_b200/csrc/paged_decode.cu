@@ -66,51 +66,60 @@ __global__ void __launch_bounds__(1024) decode_order_kernel(const int32_t* conte
                                                             int cap, int spp, int num_splits,
                                                             int2* order, int* work, int first,
                                                             int* work2) {
+  static_assert(kOrderBuckets + 1 <= 96, "one warp scans the buckets, three per lane");
   if (threadIdx.x == 0 && work) *work = 0;
   if (threadIdx.x == 0 && work2) *work2 = 0;
-  __shared__ int hist[kOrderBuckets + 1];
-  __shared__ int cursor[kOrderBuckets + 1];
+  __shared__ int hist[96];
+  __shared__ int cursor[96];
   __shared__ int total;
-  for (int i = threadIdx.x; i <= kOrderBuckets; i += blockDim.x) hist[i] = 0;
-  __syncthreads();
+  const int tid = threadIdx.x;
+  if (tid < 96) hist[tid] = 0;
   auto bucket = [&](int n) {
     return n <= 0 ? kOrderBuckets
                   : (kOrderBuckets - 1) -
                         static_cast<int>(static_cast<int64_t>(n - 1) * kOrderBuckets / spp);
   };
-  auto stages = [&](int b) {  // stages this kernel's units cover (past `first`)
-    int ctx = context_lens[b];
+  auto stages = [&](int ctx) {  // stages this kernel's units cover (past `first`)
     ctx = ctx < 0 ? 0 : (ctx > cap ? cap : ctx);
     const int n = (ctx + kTok - 1) / kTok - first;
     return n < 0 ? 0 : n;
   };
-  for (int b = threadIdx.x; b < B; b += blockDim.x) {
-    const int nst = stages(b);
+  // Each thread's first sequence stays in registers between the passes
+  // (one global read for B <= 1024).
+  const int ctx0 = tid < B ? context_lens[tid] : 0;
+  __syncthreads();
+  for (int b = tid; b < B; b += blockDim.x) {
+    const int nst = stages(b == tid ? ctx0 : context_lens[b]);
     const int nsp = nst == 0 ? 1 : (nst + spp - 1) / spp;
     for (int sp = 0; sp < nsp; ++sp)
       atomicAdd(&hist[bucket(nst == 0 ? 0 : min(spp, nst - sp * spp))], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0;
-    for (int i = 0; i <= kOrderBuckets; ++i) {
-      cursor[i] = acc;
-      acc += hist[i];
+  if (tid < 32) {  // exclusive scan of the 65 buckets: three per lane
+    const int h0 = hist[3 * tid], h1 = hist[3 * tid + 1], h2 = hist[3 * tid + 2];
+    int x = h0 + h1 + h2;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (tid >= o) x += y;
     }
-    total = acc;
+    const int base = x - (h0 + h1 + h2);
+    cursor[3 * tid] = base;
+    cursor[3 * tid + 1] = base + h0;
+    cursor[3 * tid + 2] = base + h0 + h1;
+    if (tid == 31) total = x;
   }
   __syncthreads();
-  for (int b = threadIdx.x; b < B; b += blockDim.x) {
-    const int nst = stages(b);
+  for (int b = tid; b < B; b += blockDim.x) {
+    const int ctx_raw = b == tid ? ctx0 : context_lens[b];
+    const int nst = stages(ctx_raw);
     const int nsp = nst == 0 ? 1 : (nst + spp - 1) / spp;
-    const int ctx_raw = context_lens[b];
     for (int sp = 0; sp < nsp; ++sp) {
       const int pos = atomicAdd(&cursor[bucket(nst == 0 ? 0 : min(spp, nst - sp * spp))], 1);
       order[pos] = make_int2(b * num_splits + sp, ctx_raw);
     }
   }
-  for (int i = total + threadIdx.x; i < B * num_splits; i += blockDim.x)
-    order[i] = make_int2(-1, 0);
+  for (int i = total + tid; i < B * num_splits; i += blockDim.x) order[i] = make_int2(-1, 0);
 }
 
 template <int HPC, int NST> struct DecodeShape {
