@@ -42,6 +42,14 @@ template <> LK_DEVINL uint32_t pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// ------------------------------------------- programmatic dependent launch ---
+// A kernel launched with lk::launch_after_previous may start while the kernel
+// before it in the stream still runs. pdl_wait() blocks until that kernel has
+// completed and its memory is visible (a no-op for an ordinary launch);
+// pdl_launch_dependents() lets the next such kernel start launching now.
+LK_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+LK_DEVINL void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------ timeouts ---
 // Every spin-wait in these kernels is bounded by wall time read from the
 // global nanosecond timer; on expiry the waiter reports failure instead of

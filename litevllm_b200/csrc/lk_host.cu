@@ -6,6 +6,8 @@
 
 #include "lk_host.h"
 
+#include <stdlib.h>
+
 namespace lk {
 
 int num_sms() {
@@ -20,6 +22,14 @@ int num_sms() {
     cache[dev] = n;
   }
   return cache[dev];
+}
+
+bool pdl_enabled() {
+  static int v = [] {
+    const char* e = getenv("LITEKERN_PDL");
+    return (e && atoi(e) == 0) ? 0 : 1;
+  }();
+  return v != 0;
 }
 
 int check_launch() {

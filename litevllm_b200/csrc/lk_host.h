@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/litekern.h"
 
 namespace lk {
@@ -26,6 +28,30 @@ int get_kv_tensor_map(CUtensorMap* out, const void* base, int64_t num_slots, int
                       int dtype, int box_slots, int box_heads);
 
 inline int dtype_size(int dtype) { return dtype == LK_DTYPE_F32 ? 4 : 2; }
+
+// Programmatic dependent launch on (LITEKERN_PDL=0 turns it off; read once).
+bool pdl_enabled();
+
+// Launch `kernel` so that it may start while the previous kernel in the
+// stream is still running (programmatic stream serialization). The kernel
+// must call lk::pdl_wait() before it touches memory the previous kernels
+// write and before it ends (so that its completion implies theirs). Falls back
+// to an ordinary stream-ordered launch when PDL is off.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_after_previous(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                  cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Shared-prefix attention for lk_paged_decode_shared_prefix (paged_prefill.cu).
 int prefix_attention(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,

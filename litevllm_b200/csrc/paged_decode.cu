@@ -67,6 +67,11 @@ __global__ void __launch_bounds__(1024) decode_order_kernel(const int32_t* conte
                                                             int2* order, int* work, int first,
                                                             int* work2) {
   static_assert(kOrderBuckets + 1 <= 96, "one warp scans the buckets, three per lane");
+  // Launched with lk::launch_after_previous: let the split kernel start
+  // launching, then wait for the previous kernel (the step's KV store) before
+  // touching memory, so this grid's completion implies the store's.
+  lk::pdl_launch_dependents();
+  lk::pdl_wait();
   if (threadIdx.x == 0 && work) *work = 0;
   if (threadIdx.x == 0 && work2) *work2 = 0;
   __shared__ int hist[96];
@@ -148,6 +153,9 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
 
+  // Launched with lk::launch_after_previous after the ordering kernel: wait
+  // for it (and through it for the KV store) before reading anything.
+  lk::pdl_wait();
   int2 unit;
   if (p.order != nullptr) {
     unit = p.order[blockIdx.x];
@@ -1290,12 +1298,14 @@ int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, const DecodePara
     configured[dev] = 1;
   }
   if (p.order != nullptr && !order_done) {
-    decode_order_kernel<<<1, 1024, 0, s>>>(p.context_lens, B, p.max_blocks * p.bs,
-                                           p.stages_per_split, p.num_splits,
-                                           const_cast<int2*>(p.order), p.work, p.first_stage,
-                                           nullptr);
-    const int rc = lk::check_launch();
-    if (rc != LK_OK) return rc;
+    // Both launches may start before the kernel ahead of them in the stream
+    // ends (its launch latency and the split kernel's prologue overlap the KV
+    // store and the ordering); each waits for its predecessor before reading.
+    if (lk::launch_after_previous(decode_order_kernel, dim3(1), dim3(1024), 0, s, p.context_lens,
+                                  B, p.max_blocks * p.bs, p.stages_per_split, p.num_splits,
+                                  const_cast<int2*>(p.order), p.work, p.first_stage,
+                                  static_cast<int*>(nullptr)) != cudaSuccess)
+      return LK_ERR_CUDA;
   }
   if (p.order != nullptr && stream_units() && p.part_offset == 0) {
     static int configured_s[64] = {0};
@@ -1313,7 +1323,9 @@ int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, const DecodePara
     return lk::check_launch();
   }
   dim3 grid(B * p.num_splits, p.num_groups);
-  paged_decode_kernel<T, HPC, NST><<<grid, Shape::kThreads, Shape::kSmem, s>>>(km, vm, p);
+  if (lk::launch_after_previous(paged_decode_kernel<T, HPC, NST>, grid, dim3(Shape::kThreads),
+                                Shape::kSmem, s, km, vm, p) != cudaSuccess)
+    return LK_ERR_CUDA;
   return lk::check_launch();
 }
 

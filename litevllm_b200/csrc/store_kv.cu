@@ -22,6 +22,9 @@ store_kv_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__ val
                 const int64_t* __restrict__ slot_mapping, int64_t key_stride_b,
                 int64_t value_stride_b, int64_t row_bytes, int64_t num_slots,
                 int32_t* __restrict__ status) {
+  // The decode step's ordering kernel may start launching now: it waits for
+  // this grid to complete before it reads or writes anything.
+  lk::pdl_launch_dependents();
   const int t = blockIdx.x;
   const int64_t slot = slot_mapping[t];
   if (slot < 0 || slot >= num_slots) {
