@@ -154,8 +154,11 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
 
   // Launched with lk::launch_after_previous after the ordering kernel: wait
-  // for it (and through it for the KV store) before reading anything.
+  // for it (and through it for the KV store) before reading anything. The
+  // kernel after this one (the sampler) may then start launching: its blocks
+  // wait for this grid to complete, and take SMs as the last wave drains.
   lk::pdl_wait();
+  lk::pdl_launch_dependents();
   int2 unit;
   if (p.order != nullptr) {
     unit = p.order[blockIdx.x];

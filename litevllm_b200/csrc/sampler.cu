@@ -250,6 +250,7 @@ LK_DEVINL void block_reduce(float& k, int& i) {
 
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(kSampThreads, kSampCtasPerSm) sample_kernel(const SampleParams p) {
+  lk::pdl_wait();  // launched to overlap the kernel ahead of it: wait for it before reading
   const int ch = blockIdx.x, b = blockIdx.y;
   const float temp = p.temps ? p.temps[b] : 0.f;
   const int v0 = ch * p.chunk, v1 = min(p.V, v0 + p.chunk);
@@ -432,6 +433,7 @@ LK_DEVINL void resolve_index(const uint4& braw, float best, int& besti) {
 
 template <typename T, int kU, int kMinBlocks, bool kCluster>
 __global__ void __launch_bounds__(kSampThreads, kMinBlocks) argmax_kernel(const SampleParams p) {
+  lk::pdl_wait();  // launched to overlap the kernel ahead of it: wait for it before reading
   const int ch = blockIdx.x, b = blockIdx.y;
   const int v0 = ch * p.chunk, v1 = min(p.V, v0 + p.chunk);
   const T* row = static_cast<const T*>(p.logits) + static_cast<int64_t>(b) * p.ld;
@@ -690,13 +692,16 @@ int launch_sample(const SampleParams& p, int B, bool vec, cudaStream_t s) {
         cfg.blockDim = dim3(kSampThreads);
         cfg.dynamicSmemBytes = 0;
         cfg.stream = s;
-        cudaLaunchAttribute attr[1];
+        cudaLaunchAttribute attr[2];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = p.nchunks;
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
+        // may start while the kernel ahead of it runs; waits for it first thing
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        cfg.numAttrs = lk::pdl_enabled() ? 2 : 1;
         cudaError_t e;
         switch (sample_unroll()) {
           case 4: e = launch_cluster(argmax_kernel<T, 4, 6, true>, cfg, p); break;
@@ -705,12 +710,22 @@ int launch_sample(const SampleParams& p, int B, bool vec, cudaStream_t s) {
         }
         return e == cudaSuccess ? LK_OK : LK_ERR_CUDA;
       }
+      cudaError_t e;
       switch (sample_unroll()) {
-        case 4: argmax_kernel<T, 4, 6, false><<<grid, kSampThreads, 0, s>>>(p); break;
-        case 16: argmax_kernel<T, 16, 2, false><<<grid, kSampThreads, 0, s>>>(p); break;
-        default: argmax_kernel<T, 8, 4, false><<<grid, kSampThreads, 0, s>>>(p); break;
+        case 4:
+          e = lk::launch_after_previous(argmax_kernel<T, 4, 6, false>, grid, dim3(kSampThreads), 0,
+                                        s, p);
+          break;
+        case 16:
+          e = lk::launch_after_previous(argmax_kernel<T, 16, 2, false>, grid, dim3(kSampThreads),
+                                        0, s, p);
+          break;
+        default:
+          e = lk::launch_after_previous(argmax_kernel<T, 8, 4, false>, grid, dim3(kSampThreads), 0,
+                                        s, p);
+          break;
       }
-      return lk::check_launch();
+      return e == cudaSuccess ? LK_OK : LK_ERR_CUDA;
     }
   }
   if constexpr (!std::is_same<T, float>::value) {
@@ -728,9 +743,10 @@ int launch_sample(const SampleParams& p, int B, bool vec, cudaStream_t s) {
       return lk::check_launch();
     }
   }
-  if (vec) sample_kernel<T, true><<<grid, kSampThreads, 0, s>>>(p);
-  else sample_kernel<T, false><<<grid, kSampThreads, 0, s>>>(p);
-  return lk::check_launch();
+  const cudaError_t e =
+      vec ? lk::launch_after_previous(sample_kernel<T, true>, grid, dim3(kSampThreads), 0, s, p)
+          : lk::launch_after_previous(sample_kernel<T, false>, grid, dim3(kSampThreads), 0, s, p);
+  return e == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 
 }  // namespace
