@@ -191,7 +191,7 @@ def test_decode_shared_prefix_with_cow_fork(cuda):
                                      "LITEKERN_DECODE_HEADS_PER_CTA=1",
                                      "LITEKERN_DECODE_PREFETCH=8", "LITEKERN_DECODE_STREAM=1",
                                      "LITEKERN_PREFIX_RANGES=1", "LITEKERN_PREFIX_RANGES=16",
-                                     "LITEKERN_PREFIX_SPP=8"])
+                                     "LITEKERN_PREFIX_SPP=8", "LITEKERN_PDL=0"])
 def test_decode_kernel_options(variant):
     """The decode options (read once per process from the environment)
     against the oracle, in a child process."""

@@ -199,7 +199,7 @@ def test_repetition_penalty_out_of_range_ids_flagged(cuda):
 
 
 @pytest.mark.parametrize("variant", ["LITEKERN_SAMPLE_UNROLL=0", "LITEKERN_SAMPLE_UNROLL=4",
-                                     "LITEKERN_SAMPLE_UNROLL=16", "LITEKERN_SAMPLE_CHUNKS=5"])
+                                     "LITEKERN_SAMPLE_UNROLL=16", "LITEKERN_SAMPLE_CHUNKS=5", "LITEKERN_PDL=0"])
 def test_sampler_kernel_options(variant):
     """The greedy kernels kept as options (chosen once per process from the
     environment) against the oracle, in a child process."""
