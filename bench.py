@@ -147,7 +147,12 @@ class ClockSampler:
             time.sleep(0.0005)
 
     def __enter__(self):
+        # The launching thread holds the GIL while it enqueues steps; with the
+        # default 5 ms switch interval a region of a few ms yields one sample.
+        # A short interval lets the poller run between launches.
+        self._switch = sys.getswitchinterval()
         if self.ok:
+            sys.setswitchinterval(1e-4)
             self._t = threading.Thread(target=self._run, daemon=True)
             self._t.start()
         return self
@@ -156,6 +161,7 @@ class ClockSampler:
         self._stop.set()
         if self._t:
             self._t.join()
+        sys.setswitchinterval(self._switch)
 
     def summary(self):
         if not self.samples:
