@@ -82,9 +82,12 @@ int lk_store_kv(const void* key, const void* value, void* k_cache, void* v_cache
  *   out[b,h,:] = softmax_s(scale * q[b,h] . k[b,s,h/G]) @ v[b,s,h/G],
  *   s < context_lens[b], G = H / H_kv.
  * q / out: [B, H, D] (token stride q_token_stride / out_token_stride elements,
- * head stride D). dtype F16 or BF16; D = 128; block_size a multiple of 16;
- * G <= 8. A context_len of 0 yields NaN rows, like the reference's softmax
- * over an all -inf row.
+ * head stride D). The split kernel takes dtype F16 or BF16, D = 128,
+ * block_size a multiple of 16 and G <= 8; other shapes (fp32, other head dims
+ * or block sizes, larger G) run lk_paged_attention_generic, which uses only
+ * the workspace's status word (at least 4 bytes) and ignores num_splits. A
+ * context_len of 0 yields NaN rows, like the reference's softmax over an all
+ * -inf row.
  * num_splits: a positive value runs the split-KV kernel with that many
  * splits per sequence; 0 picks the split count lk_paged_decode_num_splits
  * returns; -1 runs the persistent stage-balanced kernel (one CTA per SM, the
@@ -161,8 +164,9 @@ int lk_paged_decode_status(const void* workspace, void* stream);
  * and the chunk's own, already stored) come from the paged cache. With
  * block_tables == NULL, k_cache / v_cache are the contiguous [T, H_kv, D] keys
  * and values of the chunk (context_lens may then be NULL, meaning prior = 0):
- * this is exactly the reference's _prefill. dtype F16 or BF16; D = 128;
- * G in {1,2,4,8}; block_size a multiple of 16 in paged mode.
+ * this is exactly the reference's _prefill. The tensor-core kernel takes
+ * dtype F16 or BF16, D = 128, G in {1,2,4,8} and (paged mode) block_size a
+ * multiple of 16; other shapes run lk_paged_attention_generic.
  * status (may be NULL) receives LK_STATUS_* bits.
  */
 int lk_paged_prefill(void* out, const void* q, int64_t q_token_stride,
@@ -172,6 +176,37 @@ int lk_paged_prefill(void* out, const void* q, int64_t q_token_stride,
                      int32_t num_seqs, int32_t max_q_len,
                      int32_t H, int32_t H_kv, int32_t D, int32_t block_size,
                      float scale, int32_t dtype, int32_t* status, void* stream);
+
+/*
+ * Generic paged attention on the CUDA cores, for the shapes the tuned kernels
+ * do not take: fp32 / f16 / bf16 storage, D in {32, 64, 96, 128, 256}, any
+ * block_size, G = H / H_kv up to 32. lk_paged_decode and lk_paged_prefill(_ws)
+ * call it themselves for such shapes (fp32 models, head_dim 64 Llamas, 8-slot
+ * blocks); it is exported so that a caller may also pick it directly. It
+ * restates the reference's Attention._decode_fast
+ * (litevllm/layers/attention.py:91-139) and Attention._prefill (:141-151) with
+ * the prior-context generalisation of lk_paged_prefill: query token i of
+ * sequence b (rows cu_seqlens_q[b].. of q / out) sits at position
+ * prior + i, prior = context_lens[b] - q_len, and attends keys j <= prior + i.
+ * cu_seqlens_q == NULL means decode: one query per sequence (row b,
+ * max_q_len 1) at position context_lens[b] - 1, and block_tables is then
+ * required. block_tables == NULL means contiguous keys ([T, H_kv, D], key j of
+ * sequence b at row cu_seqlens_q[b] + j, prior 0; num_blocks = T).
+ * max_blocks_per_seq > 0 bounds context_lens (larger ones are clamped and
+ * flagged LK_STATUS_CTX_OOB); 0 = no bound. Out-of-range block ids read
+ * zeros and set LK_STATUS_BLOCK_OOB in *status (may be NULL). Scores, softmax
+ * and the PV sum are fp32; a row with no keys (context 0) is NaN. No
+ * workspace, no allocation; one launch.
+ */
+int lk_paged_attention_generic(void* out, int64_t out_token_stride,
+                               const void* q, int64_t q_token_stride,
+                               const void* k_cache, const void* v_cache, int64_t num_blocks,
+                               const int32_t* block_tables, int64_t block_table_stride,
+                               const int32_t* cu_seqlens_q, const int32_t* context_lens,
+                               int32_t num_seqs, int32_t max_q_len,
+                               int32_t H, int32_t H_kv, int32_t D, int32_t block_size,
+                               int32_t max_blocks_per_seq, float scale, int32_t dtype,
+                               int32_t* status, void* stream);
 
 /*
  * lk_paged_prefill with a caller-owned workspace (same arguments and results;

@@ -143,6 +143,8 @@ class Attention(nn.Module):
             pref >= SHARED_PREFIX_MIN_TOKENS
             and block_table is _SHARED_PREFIX["table"]
             and query.shape[0] >= SHARED_PREFIX_MIN_ROWS
+            and ops.tuned_attention_shape(query.dtype, self.head_dim, key_cache.shape[1],
+                                          self.num_kv_groups)
         ):
             # the rows share their first `pref` tokens: compute them once
             return ops.paged_decode_shared_prefix(

@@ -1457,9 +1457,21 @@ extern "C" int lk_paged_decode(void* out, int64_t out_token_stride, const void* 
   if (B == 0) return LK_OK;
   if (!out || !q || !k_cache || !v_cache || !block_tables || !context_lens)
     return LK_ERR_INVALID_ARG;
-  if (dtype != LK_DTYPE_BF16 && dtype != LK_DTYPE_F16) return LK_ERR_UNSUPPORTED;
-  if (D != kD || block_size % kTok != 0 || H / H_kv > 8) return LK_ERR_UNSUPPORTED;
   if (B > 65535 || max_blocks_per_seq == 0) return LK_ERR_INVALID_ARG;
+  if ((dtype != LK_DTYPE_BF16 && dtype != LK_DTYPE_F16) || D != kD || block_size % kTok != 0 ||
+      H / H_kv > 8) {
+    // Shapes the split kernel does not take (fp32 caches, other head dims or
+    // block sizes, G > 8) run the generic CUDA-core kernel; its status bits
+    // go to the workspace's status word like the split kernel's (the rest of
+    // the workspace is unused).
+    if (!workspace || workspace_bytes < 4 || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+      return LK_ERR_WORKSPACE;
+    return lk_paged_attention_generic(out, out_token_stride, q, q_token_stride, k_cache, v_cache,
+                                      num_blocks, block_tables, block_table_stride, nullptr,
+                                      context_lens, B, 1, H, H_kv, D, block_size,
+                                      max_blocks_per_seq, scale, dtype,
+                                      static_cast<int32_t*>(workspace), stream);
+  }
   if (static_cast<int64_t>(B) * H_kv > kMaxCounters) return LK_ERR_UNSUPPORTED;
   if (num_blocks * block_size > 0x7fffffffLL) return LK_ERR_UNSUPPORTED;
   if (((reinterpret_cast<uintptr_t>(q) & 3u) != 0) || (q_token_stride & 1) != 0)

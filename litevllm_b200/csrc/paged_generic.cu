@@ -1,0 +1,332 @@
+// Generic paged attention on the CUDA cores: the shapes the tuned kernels do
+// not take. Those kernels (paged_decode.cu, paged_prefill.cu) want 16-bit
+// caches, head_dim 128, block sizes that are multiples of 16 and, for
+// prefill, G in {1, 2, 4, 8}. A model that runs in fp32 (the reference's CPU
+// configuration), a Llama with head_dim 64 (Llama-3.2-1B, TinyLlama), or a
+// cache with 8-slot blocks calls the same entry points and lands here.
+//
+// One kernel serves decode and prefill: query token i of sequence b sits at
+// absolute position prior_b + i, prior_b = context_lens[b] - q_len_b, and
+// attends keys j <= prior_b + i (decode: q_len 1, so every key < context_len;
+// the reference's Attention._decode_fast, litevllm/layers/attention.py:91-139;
+// prefill: the causal chunk over prior paged context, Attention._prefill
+// :141-151 at prior 0). Scores, softmax and the PV sum are fp32 whatever the
+// storage type; GQA maps query head h to KV head h / G (attention.py:124).
+//
+// Layout: CTA = (KV head, tile of query tokens, sequence), 128 threads. The
+// tile's G * QT query rows (QT = 32 / G tokens) sit in shared memory as fp32;
+// 32-token K and V tiles are gathered through the block table into shared
+// memory (coalesced along d) and converted to fp32. Each warp owns up to 8
+// rows: lane j scores key j of the tile against a row, a warp max / sum gives
+// the online-softmax update, and lane l accumulates output elements
+// l, l + 32, ... of the row (D / 32 per lane) in registers.
+#include <algorithm>
+#include <mutex>
+
+#include "lk_common.cuh"
+#include "lk_host.h"
+
+namespace {
+
+constexpr int kGThreads = 128;
+constexpr int kGWarps = kGThreads / 32;
+constexpr int kGRows = 32;                 // query rows (token x head) per CTA
+constexpr int kGRowsPerWarp = kGRows / kGWarps;
+constexpr int kGKeys = 32;                 // keys per shared-memory tile
+
+struct GenericParams {
+  void* out;
+  int64_t out_stride;  // elements between query tokens of out
+  const void* q;
+  int64_t q_stride;    // elements between query tokens of q
+  const void* k;
+  const void* v;
+  int64_t num_slots;   // slots in the cache (paged) or key rows (contiguous)
+  int64_t num_blocks;
+  const int32_t* block_tables;  // NULL: contiguous keys, slot = cu_seqlens_q[b] + j
+  int64_t bt_stride;
+  const int32_t* cu_seqlens_q;  // NULL: one query per sequence (decode), row b
+  const int32_t* context_lens;  // NULL: prior 0 (context = the chunk)
+  int32_t* status;
+  int H, H_kv, G, bs;
+  int max_keys;        // > 0: context_lens beyond it are flagged and clamped
+  int qt;              // query tokens per CTA
+  float scale_log2;
+};
+
+template <typename T>
+__device__ __forceinline__ float ld_f(const T* p) {
+  return lk::Elem<T>::to_f(*p);
+}
+
+template <typename T>
+__device__ __forceinline__ void st_f(T* p, float x);
+template <>
+__device__ __forceinline__ void st_f<float>(float* p, float x) { *p = x; }
+template <>
+__device__ __forceinline__ void st_f<__half>(__half* p, float x) { *p = __float2half_rn(x); }
+template <>
+__device__ __forceinline__ void st_f<__nv_bfloat16>(__nv_bfloat16* p, float x) {
+  *p = __float2bfloat16_rn(x);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p) {
+  constexpr int DV = D / 32;  // output elements per lane and row
+  extern __shared__ float gsm[];
+  float* Qs = gsm;                          // [kGRows][D]
+  float* Ks = Qs + kGRows * D;              // [kGKeys][D + 1] (padded: lane j reads row j)
+  float* Vs = Ks + kGKeys * (D + 1);        // [kGKeys][D]
+  int* slots = reinterpret_cast<int*>(Vs + kGKeys * D);  // [kGKeys], -1 = zeros
+
+  const int kvh = blockIdx.x, tile = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.G;
+
+  int q_start, q_len;
+  if (p.cu_seqlens_q) {
+    q_start = p.cu_seqlens_q[b];
+    q_len = p.cu_seqlens_q[b + 1] - q_start;
+  } else {
+    q_start = b;
+    q_len = 1;
+  }
+  const int i0 = tile * p.qt;
+  if (i0 >= q_len) return;
+  const int ntok = min(p.qt, q_len - i0);
+  const int nrows = ntok * G;
+
+  int ctx = p.context_lens ? p.context_lens[b] : q_len;
+  if (p.max_keys > 0 && ctx > p.max_keys) {
+    if (threadIdx.x == 0 && tile == 0 && kvh == 0 && p.status)
+      atomicOr(p.status, LK_STATUS_CTX_OOB);
+    ctx = p.max_keys;
+  }
+  int prior = ctx - q_len;
+  if (prior < 0) {
+    // A decode row with context 0 has no keys (its output is NaN, as the
+    // reference's softmax over an all -inf row); a prefill chunk longer than
+    // its context is malformed.
+    if (p.cu_seqlens_q && threadIdx.x == 0 && tile == 0 && kvh == 0 && p.status)
+      atomicOr(p.status, LK_STATUS_CTX_OOB);
+    prior = p.cu_seqlens_q ? 0 : -1;
+  }
+  // keys [0, kv_end) feed this tile's rows
+  const int kv_end = max(0, prior + i0 + ntok);
+
+  // Q rows of the tile: row r = (token i0 + r / G, head kvh * G + r % G).
+  const T* q = static_cast<const T*>(p.q);
+  for (int e = threadIdx.x; e < nrows * D; e += kGThreads) {
+    const int r = e / D, d = e - r * D;
+    const int tok = q_start + i0 + r / G, h = kvh * G + r % G;
+    Qs[e] = ld_f(q + tok * p.q_stride + static_cast<int64_t>(h) * D + d);
+  }
+
+  float m[kGRowsPerWarp], l[kGRowsPerWarp], o[kGRowsPerWarp][DV];
+#pragma unroll
+  for (int k = 0; k < kGRowsPerWarp; ++k) {
+    m[k] = -INFINITY;
+    l[k] = 0.f;
+#pragma unroll
+    for (int t = 0; t < DV; ++t) o[k][t] = 0.f;
+  }
+
+  const T* kc = static_cast<const T*>(p.k);
+  const T* vc = static_cast<const T*>(p.v);
+  const int64_t slot_stride = static_cast<int64_t>(p.H_kv) * D;
+  const int32_t* bt = p.block_tables ? p.block_tables + b * p.bt_stride : nullptr;
+
+  for (int j0 = 0; j0 < kv_end; j0 += kGKeys) {
+    __syncthreads();  // the previous tile's K / V are consumed
+    if (threadIdx.x < kGKeys) {
+      const int j = j0 + threadIdx.x;
+      int slot = -1;
+      if (j < kv_end) {
+        if (bt) {
+          const int blk = bt[j / p.bs];
+          if (blk < 0 || blk >= p.num_blocks) {
+            if (p.status) atomicOr(p.status, LK_STATUS_BLOCK_OOB);
+          } else {
+            slot = blk * p.bs + j % p.bs;
+          }
+        } else {
+          const int64_t s = static_cast<int64_t>(q_start) + j;
+          if (s < p.num_slots) slot = static_cast<int>(s);
+          else if (p.status) atomicOr(p.status, LK_STATUS_BLOCK_OOB);
+        }
+      }
+      slots[threadIdx.x] = slot;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < kGKeys * D; e += kGThreads) {
+      const int jj = e / D, d = e - jj * D;
+      const int slot = slots[jj];
+      float kx = 0.f, vx = 0.f;
+      if (slot >= 0) {
+        const int64_t off = slot * slot_stride + static_cast<int64_t>(kvh) * D + d;
+        kx = ld_f(kc + off);
+        vx = ld_f(vc + off);
+      }
+      Ks[jj * (D + 1) + d] = kx;
+      Vs[jj * D + d] = vx;
+    }
+    __syncthreads();
+
+#pragma unroll
+    for (int k = 0; k < kGRowsPerWarp; ++k) {
+      const int r = warp + k * kGWarps;
+      if (r < nrows) {
+        const int pos = prior + i0 + r / G;  // this row's last visible key
+        const int j = j0 + lane;
+        const float* qr = Qs + r * D;
+        const float* kr = Ks + lane * (D + 1);
+        float s = 0.f;
+#pragma unroll 8
+        for (int d = 0; d < D; ++d) s = fmaf(qr[d], kr[d], s);
+        const bool valid = j <= pos && j < kv_end;
+        s = valid ? s * p.scale_log2 : -INFINITY;
+        float mt = s;
+#pragma unroll
+        for (int w = 16; w > 0; w >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, w));
+        const float mn = fmaxf(m[k], mt);
+        if (mn != -INFINITY) {  // the row has a visible key by now
+          const float alpha = exp2f(m[k] - mn);
+          const float pj = valid ? exp2f(s - mn) : 0.f;
+          float ps = pj;
+#pragma unroll
+          for (int w = 16; w > 0; w >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, w);
+          l[k] = l[k] * alpha + ps;
+#pragma unroll
+          for (int t = 0; t < DV; ++t) o[k][t] *= alpha;
+#pragma unroll 4
+          for (int jj = 0; jj < kGKeys; ++jj) {
+            const float pb = __shfl_sync(0xffffffffu, pj, jj);
+            const float* vr = Vs + jj * D + lane;
+#pragma unroll
+            for (int t = 0; t < DV; ++t) o[k][t] = fmaf(pb, vr[32 * t], o[k][t]);
+          }
+          m[k] = mn;
+        }
+      }
+    }
+  }
+
+  T* out = static_cast<T*>(p.out);
+#pragma unroll
+  for (int k = 0; k < kGRowsPerWarp; ++k) {
+    const int r = warp + k * kGWarps;
+    if (r < nrows) {
+      const int tok = q_start + i0 + r / G, h = kvh * G + r % G;
+      const float inv = l[k] > 0.f ? 1.f / l[k] : __int_as_float(0x7fc00000);  // no key: NaN
+      T* orow = out + tok * p.out_stride + static_cast<int64_t>(h) * D;
+#pragma unroll
+      for (int t = 0; t < DV; ++t) st_f<T>(orow + lane + 32 * t, o[k][t] * inv);
+    }
+  }
+}
+
+size_t generic_smem_bytes(int D) {
+  return (static_cast<size_t>(kGRows) * D + static_cast<size_t>(kGKeys) * (D + 1) +
+          static_cast<size_t>(kGKeys) * D) * sizeof(float) + kGKeys * sizeof(int);
+}
+
+template <typename T, int D>
+int launch_generic_d(const GenericParams& p, int num_seqs, int max_q_len, cudaStream_t s) {
+  auto kern = generic_attn_kernel<T, D>;
+  const size_t smem = generic_smem_bytes(D);
+  // Shared memory above 48 KB is opted into once per device.
+  static std::mutex mu;
+  static bool done[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LK_ERR_CUDA;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev]) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(smem)) != cudaSuccess)
+        return LK_ERR_CUDA;
+      done[dev] = true;
+    }
+  }
+  dim3 grid(p.H_kv, (max_q_len + p.qt - 1) / p.qt, num_seqs);
+  kern<<<grid, kGThreads, smem, s>>>(p);
+  return lk::check_launch();
+}
+
+template <typename T>
+int launch_generic(const GenericParams& p, int D, int num_seqs, int max_q_len, cudaStream_t s) {
+  switch (D) {
+    case 32: return launch_generic_d<T, 32>(p, num_seqs, max_q_len, s);
+    case 64: return launch_generic_d<T, 64>(p, num_seqs, max_q_len, s);
+    case 96: return launch_generic_d<T, 96>(p, num_seqs, max_q_len, s);
+    case 128: return launch_generic_d<T, 128>(p, num_seqs, max_q_len, s);
+    case 256: return launch_generic_d<T, 256>(p, num_seqs, max_q_len, s);
+    default: return LK_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace
+
+extern "C" int lk_paged_attention_generic(
+    void* out, int64_t out_token_stride, const void* q, int64_t q_token_stride,
+    const void* k_cache, const void* v_cache, int64_t num_blocks, const int32_t* block_tables,
+    int64_t block_table_stride, const int32_t* cu_seqlens_q, const int32_t* context_lens,
+    int32_t num_seqs, int32_t max_q_len, int32_t H, int32_t H_kv, int32_t D, int32_t block_size,
+    int32_t max_blocks_per_seq, float scale, int32_t dtype, int32_t* status, void* stream) {
+  if (num_seqs < 0 || max_q_len < 0 || H <= 0 || H_kv <= 0 || H % H_kv != 0 || num_blocks <= 0 ||
+      max_blocks_per_seq < 0)
+    return LK_ERR_INVALID_ARG;
+  if (num_seqs == 0 || max_q_len == 0) return LK_OK;
+  if (!out || !q || !k_cache || !v_cache) return LK_ERR_INVALID_ARG;
+  if (!cu_seqlens_q && max_q_len != 1) return LK_ERR_INVALID_ARG;
+  if (!block_tables && !cu_seqlens_q) return LK_ERR_INVALID_ARG;
+  if (dtype != LK_DTYPE_F32 && dtype != LK_DTYPE_F16 && dtype != LK_DTYPE_BF16)
+    return LK_ERR_UNSUPPORTED;
+  const int G = H / H_kv;
+  if (G > kGRows || (D != 32 && D != 64 && D != 96 && D != 128 && D != 256))
+    return LK_ERR_UNSUPPORTED;
+  if (num_seqs > 65535 || H_kv > 65535) return LK_ERR_INVALID_ARG;
+  int64_t num_slots;
+  if (block_tables) {
+    if (block_size <= 0) return LK_ERR_INVALID_ARG;
+    num_slots = num_blocks * block_size;
+  } else {
+    num_slots = num_blocks;
+  }
+  if (num_slots > 0x7fffffffLL) return LK_ERR_UNSUPPORTED;
+  const int64_t max_keys =
+      block_tables && max_blocks_per_seq > 0 ? static_cast<int64_t>(max_blocks_per_seq) * block_size : 0;
+  if (max_keys > 0x7fffffffLL) return LK_ERR_UNSUPPORTED;
+  const int esz = lk::dtype_size(dtype);
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out) |
+       reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) &
+      (esz - 1))
+    return LK_ERR_ALIGNMENT;
+  GenericParams p;
+  p.out = out;
+  p.out_stride = out_token_stride;
+  p.q = q;
+  p.q_stride = q_token_stride;
+  p.k = k_cache;
+  p.v = v_cache;
+  p.num_slots = num_slots;
+  p.num_blocks = block_tables ? num_blocks : 0;
+  p.block_tables = block_tables;
+  p.bt_stride = block_table_stride;
+  p.cu_seqlens_q = cu_seqlens_q;
+  p.context_lens = block_tables ? context_lens : nullptr;  // contiguous mode: prior 0
+  p.status = status;
+  p.H = H;
+  p.H_kv = H_kv;
+  p.G = G;
+  p.bs = block_size;
+  p.max_keys = static_cast<int>(max_keys);
+  p.qt = kGRows / G;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case LK_DTYPE_BF16: return launch_generic<__nv_bfloat16>(p, D, num_seqs, max_q_len, s);
+    case LK_DTYPE_F16: return launch_generic<__half>(p, D, num_seqs, max_q_len, s);
+    default: return launch_generic<float>(p, D, num_seqs, max_q_len, s);
+  }
+}

@@ -1663,10 +1663,18 @@ extern "C" int lk_paged_prefill_ws(void* out, const void* q, int64_t q_token_str
     return LK_ERR_INVALID_ARG;
   if (num_seqs == 0 || max_q_len == 0) return LK_OK;
   if (!out || !q || !k_cache || !v_cache || !cu_seqlens_q) return LK_ERR_INVALID_ARG;
-  if (dtype != LK_DTYPE_BF16 && dtype != LK_DTYPE_F16) return LK_ERR_UNSUPPORTED;
-  const int G = H / H_kv;
-  if (D != kD || (G != 1 && G != 2 && G != 4 && G != 8)) return LK_ERR_UNSUPPORTED;
   if (num_seqs > 65535 || H_kv > 65535) return LK_ERR_INVALID_ARG;
+  const int G = H / H_kv;
+  if ((dtype != LK_DTYPE_BF16 && dtype != LK_DTYPE_F16) || D != kD ||
+      (G != 1 && G != 2 && G != 4 && G != 8) || (block_tables && block_size % 16 != 0)) {
+    // Shapes the tensor-core kernel does not take (fp32, other head dims, G,
+    // or block sizes) run the generic CUDA-core kernel (no workspace needed).
+    return lk_paged_attention_generic(out, static_cast<int64_t>(H) * D, q, q_token_stride,
+                                      k_cache, v_cache, num_blocks, block_tables,
+                                      block_table_stride, cu_seqlens_q, context_lens, num_seqs,
+                                      max_q_len, H, H_kv, D, block_size, 0, scale, dtype, status,
+                                      stream);
+  }
   // Paged mode: num_blocks blocks of block_size slots. Contiguous mode: the
   // key tensor holds num_blocks tokens (block_size is ignored).
   int64_t num_slots;

@@ -166,7 +166,7 @@ def paged_decode(
     if context_lens.dtype != torch.int32 or context_lens.numel() != B:
         raise TypeError("context_lens must be int32 [B]")
     context_lens = context_lens.contiguous()
-    code = _dtype_code(query)
+    code = _dtype_code(query, (torch.float32, torch.float16, torch.bfloat16))
     if out is None:
         out = torch.empty((B, H, D), dtype=query.dtype, device=dev)
     elif out.shape != (B, H, D) or out.dtype != query.dtype or out.stride(2) != 1 or out.stride(1) != D:
@@ -323,7 +323,7 @@ def paged_prefill(
         raise TypeError("cu_seqlens_q must be int32")
     cu_seqlens_q = cu_seqlens_q.contiguous()
     S = cu_seqlens_q.numel() - 1
-    code = _dtype_code(query)
+    code = _dtype_code(query, (torch.float32, torch.float16, torch.bfloat16))
     if out is None:
         out = torch.empty((T, H, D), dtype=query.dtype, device=dev)
     elif out.shape != (T, H, D) or not out.is_contiguous():
@@ -344,6 +344,70 @@ def paged_prefill(
                 cu_seqlens_q.data_ptr(), _ptr(context_lens), S, int(max_q_len), H, H_kv, D, bs,
                 float(scale), code, workspace.data_ptr(),
                 workspace.numel() * workspace.element_size(), _ptr(status), _stream(dev),
+            )
+        )
+    return out
+
+
+def tuned_attention_shape(dtype: torch.dtype, head_dim: int, block_size: int, G: int) -> bool:
+    """True when the tuned decode / prefill / shared-prefix kernels take this
+    shape; other shapes run the generic CUDA-core kernel (fp32 caches, head
+    dims other than 128, block sizes not a multiple of 16, G not 1/2/4/8)."""
+    return (dtype in (torch.float16, torch.bfloat16) and head_dim == 128
+            and block_size % 16 == 0 and G in (1, 2, 4, 8))
+
+
+def paged_attention_generic(
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    scale: float,
+    block_tables: Optional[torch.Tensor] = None,
+    context_lens: Optional[torch.Tensor] = None,
+    cu_seqlens_q: Optional[torch.Tensor] = None,
+    max_q_len: Optional[int] = None,
+    status: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """The generic CUDA-core kernel called directly (lk_paged_attention_generic).
+
+    cu_seqlens_q None: decode, one query per row at position
+    context_lens[b] - 1 (Attention._decode_fast). Otherwise prefill chunks as in
+    paged_prefill: paged when block_tables is given, else key_cache /
+    value_cache are the chunk's own [T, H_kv, D] keys / values.
+    """
+    dev = _cuda(query, key_cache, value_cache, block_tables, context_lens, cu_seqlens_q, status)
+    T, H, D = query.shape
+    if query.stride(2) != 1 or query.stride(1) != D:
+        raise ValueError("query must have unit d-stride and head stride D")
+    if query.dtype != key_cache.dtype or value_cache.shape != key_cache.shape:
+        raise TypeError("query / cache dtype or shape mismatch")
+    key_cache, value_cache = key_cache.contiguous(), value_cache.contiguous()
+    if block_tables is not None:
+        nb, bs, H_kv, _ = key_cache.shape
+        if block_tables.dtype != torch.int32 or block_tables.stride(1) != 1:
+            raise TypeError("block_tables must be int32 with unit column stride")
+        bt_stride, max_blocks = block_tables.stride(0), block_tables.shape[1]
+    else:
+        nb, H_kv, _ = key_cache.shape
+        bs, bt_stride, max_blocks = 16, 0, 0
+    if context_lens is not None:
+        context_lens = context_lens.contiguous()
+    if cu_seqlens_q is None:
+        S, mq = T, 1
+    else:
+        cu_seqlens_q = cu_seqlens_q.contiguous()
+        S = cu_seqlens_q.numel() - 1
+        mq = int(max_q_len) if max_q_len is not None else int(
+            (cu_seqlens_q[1:] - cu_seqlens_q[:-1]).max().item())
+    code = _dtype_code(query, (torch.float32, torch.float16, torch.bfloat16))
+    out = torch.empty((T, H, D), dtype=query.dtype, device=dev)
+    with _on(dev):
+        check(
+            lib().lk_paged_attention_generic(
+                out.data_ptr(), out.stride(0), query.data_ptr(), query.stride(0),
+                key_cache.data_ptr(), value_cache.data_ptr(), nb, _ptr(block_tables), bt_stride,
+                _ptr(cu_seqlens_q), _ptr(context_lens), S, mq, H, H_kv, D, bs, max_blocks,
+                float(scale), code, _ptr(status), _stream(dev),
             )
         )
     return out

@@ -51,21 +51,43 @@ def test_argument_validation_without_launch():
     # decode: H not a multiple of H_kv
     assert lib.lk_paged_decode(1, 0, 1, 0, 1, 1, 10, 1, 4, 1, 2, 12, 8, 128, 16, 4, 0.1, 1,
                                1, 1 << 20, 2, None) == -1
-    # decode: D != 128 unsupported
-    assert lib.lk_paged_decode(1, 0, 1, 0, 1, 1, 10, 1, 4, 1, 2, 16, 8, 64, 16, 4, 0.1, 1,
-                               1, 1 << 20, 2, None) == -2
-    # decode: G > 8 unsupported
-    assert lib.lk_paged_decode(1, 0, 1, 0, 1, 1, 10, 1, 4, 1, 2, 32, 2, 128, 16, 4, 0.1, 1,
-                               1, 1 << 20, 2, None) == -2
-    # decode: fp32 unsupported on the tensor-core path
-    assert lib.lk_paged_decode(1, 0, 1, 0, 1, 1, 10, 1, 4, 1, 2, 16, 8, 128, 16, 4, 0.1, 1,
-                               1, 1 << 20, 0, None) == -2
+    # decode shapes the split kernel does not take (D = 64, G = 16, fp32, 8-slot
+    # blocks) go to the generic kernel, which still wants the workspace
+    P = 1 << 20  # 256-byte aligned stand-in pointer: these paths launch nothing
+    for H, H_kv, D, bs, dt in ((16, 8, 64, 16, 2), (32, 2, 128, 16, 2), (16, 8, 128, 16, 0),
+                               (16, 8, 128, 8, 2)):
+        assert lib.lk_paged_decode(P, 0, P, 0, P, P, 10, P, 4, P, 2, H, H_kv, D, bs, 4, 0.1, 1,
+                                   None, 0, dt, None) == -4
+        assert lib.lk_paged_decode(P, 0, P, 0, P, P, 10, P, 4, P, 2, H, H_kv, D, bs, 4, 0.1, 1,
+                                   1, 1 << 30, dt, None) == -4  # misaligned
+    # decode: a head dim no kernel takes, and G above 32
+    assert lib.lk_paged_decode(P, 0, P, 0, P, P, 10, P, 4, P, 2, 16, 8, 80, 16, 4, 0.1, 1,
+                               P, 1 << 30, 2, None) == -2
+    assert lib.lk_paged_decode(P, 0, P, 0, P, P, 10, P, 4, P, 2, 64, 1, 128, 16, 4, 0.1, 1,
+                               P, 1 << 30, 2, None) == -2
     # decode: workspace missing
     assert lib.lk_paged_decode(16, 4096, 16, 4096, 256, 256, 10, 16, 4, 16, 2, 32, 8, 128, 16, 4,
                                0.1, 2, None, 0, 2, None) == -4
-    # prefill: G = 3 unsupported
-    assert lib.lk_paged_prefill(16, 16, 0, 16, 16, 10, None, 0, 16, None, 1, 8, 24, 8, 128, 16,
+    # prefill: G = 3 goes to the generic kernel, which takes no D = 80
+    assert lib.lk_paged_prefill(16, 16, 0, 16, 16, 10, None, 0, 16, None, 1, 8, 24, 8, 80, 16,
                                 0.1, 2, None, None) == -2
+    # generic kernel: bad dtype, decode form with several queries, decode form
+    # without block tables, H not a multiple of H_kv, unaligned fp32 pointer
+    g = lib.lk_paged_attention_generic
+    gargs = [P, 2048, P, 2048, P, P, 10, P, 4, None, P, 2, 1, 16, 8, 128, 16, 4, 0.1, 0, None,
+             None]
+    bad = list(gargs); bad[19] = 7
+    assert g(*bad) == -2
+    bad = list(gargs); bad[12] = 3
+    assert g(*bad) == -1
+    bad = list(gargs); bad[7] = None
+    assert g(*bad) == -1
+    bad = list(gargs); bad[13] = 12
+    assert g(*bad) == -1
+    bad = list(gargs); bad[2] = P + 2
+    assert g(*bad) == -3
+    bad = list(gargs); bad[11] = 0                            # no sequences: nothing to do
+    assert g(*bad) == 0
     # sampler: ld < V
     assert lib.lk_sample(1, 1, 2, 100, 50, None, None, 0, 0, 0, None, None, 0, 2, None) == -1
     # sampler: B = 0 no-op
