@@ -16,7 +16,8 @@
 // Layout: CTA = (KV head, tile of query tokens, sequence), 128 threads. The
 // tile's G * QT query rows (QT = 32 / G tokens) sit in shared memory as fp32;
 // 32-token K and V tiles are gathered through the block table into shared
-// memory (coalesced along d) and converted to fp32. Each warp owns up to 8
+// memory (coalesced along d, 16-byte loads when the caches are 16-byte
+// aligned) and converted to fp32. Each warp owns up to 8
 // rows: lane j scores key j of the tile against a row, a warp max / sum gives
 // the online-softmax update, and lane l accumulates output elements
 // l, l + 32, ... of the row (D / 32 per lane) in registers.
@@ -70,7 +71,40 @@ __device__ __forceinline__ void st_f<__nv_bfloat16>(__nv_bfloat16* p, float x) {
   *p = __float2bfloat16_rn(x);
 }
 
-template <typename T, int D>
+// 16 bytes of T at src (16-byte aligned) -> 16 / sizeof(T) floats.
+template <typename T>
+__device__ __forceinline__ void load16_f(const T* src, float* dst);
+template <>
+__device__ __forceinline__ void load16_f<float>(const float* src, float* dst) {
+  const float4 v = *reinterpret_cast<const float4*>(src);
+  dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
+}
+template <>
+__device__ __forceinline__ void load16_f<__nv_bfloat16>(const __nv_bfloat16* src, float* dst) {
+  const uint4 v = *reinterpret_cast<const uint4*>(src);
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    dst[2 * i] = f.x;
+    dst[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void load16_f<__half>(const __half* src, float* dst) {
+  const uint4 v = *reinterpret_cast<const uint4*>(src);
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    dst[2 * i] = f.x;
+    dst[2 * i + 1] = f.y;
+  }
+}
+
+// VEC: the caches are 16-byte aligned, so every (slot, head, d multiple of
+// 16 / sizeof(T)) address is too and the tiles move in 16-byte loads.
+template <typename T, int D, bool VEC>
 __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p) {
   constexpr int DV = D / 32;  // output elements per lane and row
   extern __shared__ float gsm[];
@@ -158,17 +192,40 @@ __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p
       slots[threadIdx.x] = slot;
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < kGKeys * D; e += kGThreads) {
-      const int jj = e / D, d = e - jj * D;
-      const int slot = slots[jj];
-      float kx = 0.f, vx = 0.f;
-      if (slot >= 0) {
-        const int64_t off = slot * slot_stride + static_cast<int64_t>(kvh) * D + d;
-        kx = ld_f(kc + off);
-        vx = ld_f(vc + off);
+    if constexpr (VEC) {
+      constexpr int VE = 16 / sizeof(T);  // elements per 16-byte vector
+      constexpr int NV = D / VE;          // vectors per key row
+      for (int e = threadIdx.x; e < kGKeys * NV; e += kGThreads) {
+        const int jj = e / NV, d = (e - jj * NV) * VE;
+        const int slot = slots[jj];
+        float kx[VE], vx[VE];
+        if (slot >= 0) {
+          const int64_t off = slot * slot_stride + static_cast<int64_t>(kvh) * D + d;
+          load16_f<T>(kc + off, kx);
+          load16_f<T>(vc + off, vx);
+        } else {
+#pragma unroll
+          for (int i = 0; i < VE; ++i) kx[i] = vx[i] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < VE; ++i) {
+          Ks[jj * (D + 1) + d + i] = kx[i];
+          Vs[jj * D + d + i] = vx[i];
+        }
       }
-      Ks[jj * (D + 1) + d] = kx;
-      Vs[jj * D + d] = vx;
+    } else {
+      for (int e = threadIdx.x; e < kGKeys * D; e += kGThreads) {
+        const int jj = e / D, d = e - jj * D;
+        const int slot = slots[jj];
+        float kx = 0.f, vx = 0.f;
+        if (slot >= 0) {
+          const int64_t off = slot * slot_stride + static_cast<int64_t>(kvh) * D + d;
+          kx = ld_f(kc + off);
+          vx = ld_f(vc + off);
+        }
+        Ks[jj * (D + 1) + d] = kx;
+        Vs[jj * D + d] = vx;
+      }
     }
     __syncthreads();
 
@@ -230,11 +287,11 @@ size_t generic_smem_bytes(int D) {
           static_cast<size_t>(kGKeys) * D) * sizeof(float) + kGKeys * sizeof(int);
 }
 
-template <typename T, int D>
+template <typename T, int D, bool VEC>
 int launch_generic_d(const GenericParams& p, int num_seqs, int max_q_len, cudaStream_t s) {
-  auto kern = generic_attn_kernel<T, D>;
+  auto kern = generic_attn_kernel<T, D, VEC>;
   const size_t smem = generic_smem_bytes(D);
-  // Shared memory above 48 KB is opted into once per device.
+  // Shared memory above 48 KB is opted into once per device (and instantiation).
   static std::mutex mu;
   static bool done[64] = {false};
   int dev = 0;
@@ -253,16 +310,24 @@ int launch_generic_d(const GenericParams& p, int num_seqs, int max_q_len, cudaSt
   return lk::check_launch();
 }
 
-template <typename T>
-int launch_generic(const GenericParams& p, int D, int num_seqs, int max_q_len, cudaStream_t s) {
+template <typename T, bool VEC>
+int launch_generic_v(const GenericParams& p, int D, int num_seqs, int max_q_len, cudaStream_t s) {
   switch (D) {
-    case 32: return launch_generic_d<T, 32>(p, num_seqs, max_q_len, s);
-    case 64: return launch_generic_d<T, 64>(p, num_seqs, max_q_len, s);
-    case 96: return launch_generic_d<T, 96>(p, num_seqs, max_q_len, s);
-    case 128: return launch_generic_d<T, 128>(p, num_seqs, max_q_len, s);
-    case 256: return launch_generic_d<T, 256>(p, num_seqs, max_q_len, s);
+    case 32: return launch_generic_d<T, 32, VEC>(p, num_seqs, max_q_len, s);
+    case 64: return launch_generic_d<T, 64, VEC>(p, num_seqs, max_q_len, s);
+    case 96: return launch_generic_d<T, 96, VEC>(p, num_seqs, max_q_len, s);
+    case 128: return launch_generic_d<T, 128, VEC>(p, num_seqs, max_q_len, s);
+    case 256: return launch_generic_d<T, 256, VEC>(p, num_seqs, max_q_len, s);
     default: return LK_ERR_UNSUPPORTED;
   }
+}
+
+template <typename T>
+int launch_generic(const GenericParams& p, int D, int num_seqs, int max_q_len, cudaStream_t s) {
+  const bool vec =
+      ((reinterpret_cast<uintptr_t>(p.k) | reinterpret_cast<uintptr_t>(p.v)) & 15u) == 0;
+  return vec ? launch_generic_v<T, true>(p, D, num_seqs, max_q_len, s)
+             : launch_generic_v<T, false>(p, D, num_seqs, max_q_len, s);
 }
 
 }  // namespace

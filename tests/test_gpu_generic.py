@@ -210,3 +210,25 @@ def test_generic_fp32_engine_loop(cuda):
                                           attn.scale)
         assert_attn_close(out, ref, FP32_MAX_ABS, FP32_MEAN_REL)
     assert ops.decode_status() == 0
+
+
+def test_generic_decode_unaligned_caches(cuda):
+    """Caches that start 2 bytes past a 16-byte boundary take the kernel's
+    element-wise tile loads instead of 16-byte vectors; same results."""
+    b = workloads.make_decode_batch(2, 5, seed=26, ctx=[1, 17, 64, 300, 999], H=32, H_kv=8,
+                                    D=64, device=cuda)
+    n = b.key_cache.numel()
+    kbuf = torch.empty(n + 1, dtype=b.key_cache.dtype, device=cuda)
+    vbuf = torch.empty_like(kbuf)
+    kc = kbuf[1:].view(b.key_cache.shape)
+    vc = vbuf[1:].view(b.value_cache.shape)
+    kc.copy_(b.key_cache)
+    vc.copy_(b.value_cache)
+    assert kc.data_ptr() % 16 != 0
+    out = ops.paged_decode(b.query, kc, vc, b.block_tables, b.context_lens, b.scale)
+    aligned = ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables,
+                               b.context_lens, b.scale)
+    ref = pa.decode(b.query.float(), b.key_cache.float(), b.value_cache.float(), b.block_tables,
+                    b.context_lens, b.scale)
+    assert_attn_close(out, ref)
+    assert torch.equal(out, aligned)
