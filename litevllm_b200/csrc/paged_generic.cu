@@ -104,14 +104,22 @@ __device__ __forceinline__ void load16_f<__half>(const __half* src, float* dst) 
 
 // VEC: the caches are 16-byte aligned, so every (slot, head, d multiple of
 // 16 / sizeof(T)) address is too and the tiles move in 16-byte loads.
-template <typename T, int D, bool VEC>
+// RPW: query rows per warp (the CTA holds 4 * RPW rows).
+template <typename T, int D, bool VEC, int RPW>
 __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p) {
-  constexpr int DV = D / 32;  // output elements per lane and row
+  constexpr int DV = D / 32;                    // output elements per lane and row
+  constexpr int ROWS = kGWarps * RPW;
+  constexpr int VE = VEC ? 16 / sizeof(T) : 1;  // elements per load
+  constexpr int NV = D / VE;                    // loads per key row
+  constexpr int PER = kGKeys * NV / kGThreads;  // loads per thread per tile, K or V
+  // With few loads per thread, the next tile is held in registers while the
+  // current one is computed, so its global latency overlaps the math.
+  constexpr bool PF = VEC && PER <= 4;
   extern __shared__ float gsm[];
-  float* Qs = gsm;                          // [kGRows][D]
-  float* Ks = Qs + kGRows * D;              // [kGKeys][D + 1] (padded: lane j reads row j)
+  float* Qs = gsm;                          // [ROWS][D]
+  float* Ks = Qs + ROWS * D;                // [kGKeys][D + 1] (padded: lane j reads row j)
   float* Vs = Ks + kGKeys * (D + 1);        // [kGKeys][D]
-  int* slots = reinterpret_cast<int*>(Vs + kGKeys * D);  // [kGKeys], -1 = zeros
+  int* slots = reinterpret_cast<int*>(Vs + kGKeys * D);  // [2][kGKeys], -1 = zeros
 
   const int kvh = blockIdx.x, tile = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -128,7 +136,7 @@ __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p
   const int i0 = tile * p.qt;
   if (i0 >= q_len) return;
   const int ntok = min(p.qt, q_len - i0);
-  const int nrows = ntok * G;
+  const int nrows = ntok * G;  // <= ROWS (the host picks RPW so)
 
   int ctx = p.context_lens ? p.context_lens[b] : q_len;
   if (p.max_keys > 0 && ctx > p.max_keys) {
@@ -156,53 +164,98 @@ __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p
     Qs[e] = ld_f(q + tok * p.q_stride + static_cast<int64_t>(h) * D + d);
   }
 
-  float m[kGRowsPerWarp], l[kGRowsPerWarp], o[kGRowsPerWarp][DV];
+  const T* kc = static_cast<const T*>(p.k);
+  const T* vc = static_cast<const T*>(p.v);
+  const int64_t slot_stride = static_cast<int64_t>(p.H_kv) * D;
+  const int32_t* bt = p.block_tables ? p.block_tables + b * p.bt_stride : nullptr;
+
+  // Cache slot of key j (-1: past the keys, or an out-of-range block: zeros).
+  auto slot_of = [&](int j) -> int {
+    if (j >= kv_end) return -1;
+    if (bt) {
+      const int blk = bt[j / p.bs];
+      if (blk < 0 || blk >= p.num_blocks) {
+        if (p.status) atomicOr(p.status, LK_STATUS_BLOCK_OOB);
+        return -1;
+      }
+      return blk * p.bs + j % p.bs;
+    }
+    const int64_t s = static_cast<int64_t>(q_start) + j;
+    if (s < p.num_slots) return static_cast<int>(s);
+    if (p.status) atomicOr(p.status, LK_STATUS_BLOCK_OOB);
+    return -1;
+  };
+
+  // slots of tile 0 in buffer 0; warp 0 keeps tile 1's in a register
+  int pend = -1;
+  if (warp == 0) {
+    slots[lane] = slot_of(lane);
+    pend = slot_of(kGKeys + lane);
+  }
+  __syncthreads();
+
+  uint4 kreg[PF ? PER : 1], vreg[PF ? PER : 1];
+  auto prefetch = [&](const int* sl) {
+    if constexpr (PF) {
 #pragma unroll
-  for (int k = 0; k < kGRowsPerWarp; ++k) {
+      for (int v = 0; v < PER; ++v) {
+        const int e = threadIdx.x + v * kGThreads;
+        const int jj = e / NV, d = (e - jj * NV) * VE;
+        const int slot = sl[jj];
+        if (slot >= 0) {
+          const int64_t off = slot * slot_stride + static_cast<int64_t>(kvh) * D + d;
+          kreg[v] = *reinterpret_cast<const uint4*>(kc + off);
+          vreg[v] = *reinterpret_cast<const uint4*>(vc + off);
+        } else {
+          kreg[v] = make_uint4(0u, 0u, 0u, 0u);
+          vreg[v] = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+    }
+  };
+  prefetch(slots);
+
+  float m[RPW], l[RPW], o[RPW][DV];
+#pragma unroll
+  for (int k = 0; k < RPW; ++k) {
     m[k] = -INFINITY;
     l[k] = 0.f;
 #pragma unroll
     for (int t = 0; t < DV; ++t) o[k][t] = 0.f;
   }
 
-  const T* kc = static_cast<const T*>(p.k);
-  const T* vc = static_cast<const T*>(p.v);
-  const int64_t slot_stride = static_cast<int64_t>(p.H_kv) * D;
-  const int32_t* bt = p.block_tables ? p.block_tables + b * p.bt_stride : nullptr;
-
-  for (int j0 = 0; j0 < kv_end; j0 += kGKeys) {
-    __syncthreads();  // the previous tile's K / V are consumed
-    if (threadIdx.x < kGKeys) {
-      const int j = j0 + threadIdx.x;
-      int slot = -1;
-      if (j < kv_end) {
-        if (bt) {
-          const int blk = bt[j / p.bs];
-          if (blk < 0 || blk >= p.num_blocks) {
-            if (p.status) atomicOr(p.status, LK_STATUS_BLOCK_OOB);
-          } else {
-            slot = blk * p.bs + j % p.bs;
-          }
-        } else {
-          const int64_t s = static_cast<int64_t>(q_start) + j;
-          if (s < p.num_slots) slot = static_cast<int>(s);
-          else if (p.status) atomicOr(p.status, LK_STATUS_BLOCK_OOB);
+  for (int j0 = 0, buf = 0; j0 < kv_end; j0 += kGKeys, buf ^= 1) {
+    int* cur = slots + buf * kGKeys;
+    int* nxt = slots + (buf ^ 1) * kGKeys;
+    // 1. tile j0 into shared memory as fp32
+    if constexpr (PF) {
+#pragma unroll
+      for (int v = 0; v < PER; ++v) {
+        const int e = threadIdx.x + v * kGThreads;
+        const int jj = e / NV, d = (e - jj * NV) * VE;
+        float kx[VE], vx[VE];
+        load16_f<T>(reinterpret_cast<const T*>(&kreg[v]), kx);
+        load16_f<T>(reinterpret_cast<const T*>(&vreg[v]), vx);
+#pragma unroll
+        for (int i = 0; i < VE; ++i) {
+          Ks[jj * (D + 1) + d + i] = kx[i];
+          Vs[jj * D + d + i] = vx[i];
         }
       }
-      slots[threadIdx.x] = slot;
-    }
-    __syncthreads();
-    if constexpr (VEC) {
-      constexpr int VE = 16 / sizeof(T);  // elements per 16-byte vector
-      constexpr int NV = D / VE;          // vectors per key row
+    } else {
       for (int e = threadIdx.x; e < kGKeys * NV; e += kGThreads) {
         const int jj = e / NV, d = (e - jj * NV) * VE;
-        const int slot = slots[jj];
+        const int slot = cur[jj];
         float kx[VE], vx[VE];
         if (slot >= 0) {
           const int64_t off = slot * slot_stride + static_cast<int64_t>(kvh) * D + d;
-          load16_f<T>(kc + off, kx);
-          load16_f<T>(vc + off, vx);
+          if constexpr (VEC) {
+            load16_f<T>(kc + off, kx);
+            load16_f<T>(vc + off, vx);
+          } else {
+            kx[0] = ld_f(kc + off);
+            vx[0] = ld_f(vc + off);
+          }
         } else {
 #pragma unroll
           for (int i = 0; i < VE; ++i) kx[i] = vx[i] = 0.f;
@@ -213,33 +266,36 @@ __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p
           Vs[jj * D + d + i] = vx[i];
         }
       }
-    } else {
-      for (int e = threadIdx.x; e < kGKeys * D; e += kGThreads) {
-        const int jj = e / D, d = e - jj * D;
-        const int slot = slots[jj];
-        float kx = 0.f, vx = 0.f;
-        if (slot >= 0) {
-          const int64_t off = slot * slot_stride + static_cast<int64_t>(kvh) * D + d;
-          kx = ld_f(kc + off);
-          vx = ld_f(vc + off);
-        }
-        Ks[jj * (D + 1) + d] = kx;
-        Vs[jj * D + d] = vx;
-      }
+    }
+    // 2. publish the next tile's slots; fetch the block-table entries of the
+    //    one after it
+    if (warp == 0) {
+      nxt[lane] = pend;
+      pend = slot_of(j0 + 2 * kGKeys + lane);
     }
     __syncthreads();
+    // 3. the next tile's loads fly while this tile is computed
+    if (j0 + kGKeys < kv_end) prefetch(nxt);
 
+    // 4. scores, online softmax and PV for this warp's rows
 #pragma unroll
-    for (int k = 0; k < kGRowsPerWarp; ++k) {
+    for (int k = 0; k < RPW; ++k) {
       const int r = warp + k * kGWarps;
       if (r < nrows) {
         const int pos = prior + i0 + r / G;  // this row's last visible key
         const int j = j0 + lane;
-        const float* qr = Qs + r * D;
+        const float4* qr = reinterpret_cast<const float4*>(Qs + r * D);
         const float* kr = Ks + lane * (D + 1);
-        float s = 0.f;
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll 8
-        for (int d = 0; d < D; ++d) s = fmaf(qr[d], kr[d], s);
+        for (int d4 = 0; d4 < D / 4; ++d4) {
+          const float4 qv = qr[d4];
+          s0 = fmaf(qv.x, kr[4 * d4], s0);
+          s1 = fmaf(qv.y, kr[4 * d4 + 1], s1);
+          s2 = fmaf(qv.z, kr[4 * d4 + 2], s2);
+          s3 = fmaf(qv.w, kr[4 * d4 + 3], s3);
+        }
+        float s = (s0 + s1) + (s2 + s3);
         const bool valid = j <= pos && j < kv_end;
         s = valid ? s * p.scale_log2 : -INFINITY;
         float mt = s;
@@ -266,11 +322,12 @@ __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p
         }
       }
     }
+    __syncthreads();  // Ks / Vs and this tile's slots are free again
   }
 
   T* out = static_cast<T*>(p.out);
 #pragma unroll
-  for (int k = 0; k < kGRowsPerWarp; ++k) {
+  for (int k = 0; k < RPW; ++k) {
     const int r = warp + k * kGWarps;
     if (r < nrows) {
       const int tok = q_start + i0 + r / G, h = kvh * G + r % G;
@@ -282,15 +339,15 @@ __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p
   }
 }
 
-size_t generic_smem_bytes(int D) {
-  return (static_cast<size_t>(kGRows) * D + static_cast<size_t>(kGKeys) * (D + 1) +
-          static_cast<size_t>(kGKeys) * D) * sizeof(float) + kGKeys * sizeof(int);
+size_t generic_smem_bytes(int D, int rpw) {
+  return (static_cast<size_t>(kGWarps) * rpw * D + static_cast<size_t>(kGKeys) * (D + 1) +
+          static_cast<size_t>(kGKeys) * D) * sizeof(float) + 2 * kGKeys * sizeof(int);
 }
 
-template <typename T, int D, bool VEC>
-int launch_generic_d(const GenericParams& p, int num_seqs, int max_q_len, cudaStream_t s) {
-  auto kern = generic_attn_kernel<T, D, VEC>;
-  const size_t smem = generic_smem_bytes(D);
+template <typename T, int D, bool VEC, int RPW>
+int launch_generic_r(const GenericParams& p, int num_seqs, int max_q_len, cudaStream_t s) {
+  auto kern = generic_attn_kernel<T, D, VEC, RPW>;
+  const size_t smem = generic_smem_bytes(D, RPW);
   // Shared memory above 48 KB is opted into once per device (and instantiation).
   static std::mutex mu;
   static bool done[64] = {false};
@@ -308,6 +365,21 @@ int launch_generic_d(const GenericParams& p, int num_seqs, int max_q_len, cudaSt
   dim3 grid(p.H_kv, (max_q_len + p.qt - 1) / p.qt, num_seqs);
   kern<<<grid, kGThreads, smem, s>>>(p);
   return lk::check_launch();
+}
+
+template <typename T, int D, bool VEC>
+int launch_generic_d(GenericParams p, int num_seqs, int max_q_len, cudaStream_t s) {
+  // Rows per warp: the fewest that hold the tile's query rows (decode: the
+  // G heads of one token; prefill: up to 32 rows, 32 / G tokens).
+  const int want = std::min(max_q_len, std::max(1, kGRows / p.G)) * p.G;
+  const int rpw = want <= kGWarps ? 1 : want <= 2 * kGWarps ? 2 : want <= 4 * kGWarps ? 4 : 8;
+  p.qt = std::max(1, kGWarps * rpw / p.G);
+  switch (rpw) {
+    case 1: return launch_generic_r<T, D, VEC, 1>(p, num_seqs, max_q_len, s);
+    case 2: return launch_generic_r<T, D, VEC, 2>(p, num_seqs, max_q_len, s);
+    case 4: return launch_generic_r<T, D, VEC, 4>(p, num_seqs, max_q_len, s);
+    default: return launch_generic_r<T, D, VEC, 8>(p, num_seqs, max_q_len, s);
+  }
 }
 
 template <typename T, bool VEC>
@@ -386,7 +458,7 @@ extern "C" int lk_paged_attention_generic(
   p.G = G;
   p.bs = block_size;
   p.max_keys = static_cast<int>(max_keys);
-  p.qt = kGRows / G;
+  p.qt = kGRows / G;  // refined with the rows per warp at launch
   p.scale_log2 = scale * 1.4426950408889634f;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
