@@ -84,8 +84,11 @@ int lk_store_kv(const void* key, const void* value, void* k_cache, void* v_cache
  * q / out: [B, H, D] (token stride q_token_stride / out_token_stride elements,
  * head stride D). The split kernel takes dtype F16 or BF16, D = 128,
  * block_size a multiple of 16 and G <= 8; other shapes (fp32, other head dims
- * or block sizes, larger G) run lk_paged_attention_generic, which uses only
- * the workspace's status word (at least 4 bytes) and ignores num_splits. A
+ * or block sizes, larger G) run lk_paged_attention_generic's kernel, which
+ * ignores num_splits: it needs the workspace's status word (at least 4
+ * bytes) and splits long contexts across CTAs when the workspace also holds
+ * their partials (lk_paged_attention_generic_workspace_bytes() bytes give
+ * the full split count; a smaller workspace gives fewer splits). A
  * context_len of 0 yields NaN rows, like the reference's softmax over an all
  * -inf row.
  * num_splits: a positive value runs the split-KV kernel with that many
@@ -196,8 +199,18 @@ int lk_paged_prefill(void* out, const void* q, int64_t q_token_stride,
  * flagged LK_STATUS_CTX_OOB); 0 = no bound. Out-of-range block ids read
  * zeros and set LK_STATUS_BLOCK_OOB in *status (may be NULL). Scores, softmax
  * and the PV sum are fp32; a row with no keys (context 0) is NaN. No
- * workspace, no allocation; one launch.
+ * workspace, no allocation; one launch (one CTA per KV head, query tile and
+ * sequence; lk_paged_decode adds split-KV for this kernel).
  */
+/*
+ * Workspace bytes with which lk_paged_decode splits a decode that takes the
+ * generic kernel at its full split count (about 512 keys per split, at most
+ * 64 splits; partials of (max, sum) and D fp32 per row, head and split). No
+ * counterpart in the reference.
+ */
+size_t lk_paged_attention_generic_workspace_bytes(int32_t B, int32_t H, int32_t D,
+                                                  int32_t max_blocks_per_seq,
+                                                  int32_t block_size);
 int lk_paged_attention_generic(void* out, int64_t out_token_stride,
                                const void* q, int64_t q_token_stride,
                                const void* k_cache, const void* v_cache, int64_t num_blocks,

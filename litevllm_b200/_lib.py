@@ -61,6 +61,8 @@ SIGNATURES: dict[str, tuple] = {
          c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_float, c_int32,
          c_void_p, c_size_t, c_void_p, c_void_p],
     ),
+    "lk_paged_attention_generic_workspace_bytes": (
+        c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32]),
     "lk_paged_attention_generic": (
         c_int32,
         [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_int64,

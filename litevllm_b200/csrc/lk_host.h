@@ -60,4 +60,15 @@ int prefix_attention(const void* q, int64_t q_stride, const void* k_cache, const
                      float scale, float* part_ml, float* part_o, int part_splits, int dtype,
                      int32_t* status, int* zeroed_counter, cudaStream_t s);
 
+// Decode on the generic CUDA-core kernel (paged_generic.cu) for the shapes
+// lk_paged_decode's split kernel does not take; split-KV with a merge launch
+// when the workspace has room for the partials. Status bits go to the
+// workspace's first word.
+int generic_decode(void* out, int64_t out_token_stride, const void* q, int64_t q_token_stride,
+                   const void* k_cache, const void* v_cache, int64_t num_blocks,
+                   const int32_t* block_tables, int64_t block_table_stride,
+                   const int32_t* context_lens, int B, int H, int H_kv, int D, int block_size,
+                   int max_blocks_per_seq, float scale, int dtype, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
 }  // namespace lk

@@ -1462,15 +1462,12 @@ extern "C" int lk_paged_decode(void* out, int64_t out_token_stride, const void* 
       H / H_kv > 8) {
     // Shapes the split kernel does not take (fp32 caches, other head dims or
     // block sizes, G > 8) run the generic CUDA-core kernel; its status bits
-    // go to the workspace's status word like the split kernel's (the rest of
-    // the workspace is unused).
-    if (!workspace || workspace_bytes < 4 || (reinterpret_cast<uintptr_t>(workspace) & 255u))
-      return LK_ERR_WORKSPACE;
-    return lk_paged_attention_generic(out, out_token_stride, q, q_token_stride, k_cache, v_cache,
-                                      num_blocks, block_tables, block_table_stride, nullptr,
-                                      context_lens, B, 1, H, H_kv, D, block_size,
-                                      max_blocks_per_seq, scale, dtype,
-                                      static_cast<int32_t*>(workspace), stream);
+    // go to the workspace's status word like the split kernel's, and the rest
+    // of the workspace holds its split-KV partials when there is room.
+    return lk::generic_decode(out, out_token_stride, q, q_token_stride, k_cache, v_cache,
+                              num_blocks, block_tables, block_table_stride, context_lens, B, H,
+                              H_kv, D, block_size, max_blocks_per_seq, scale, dtype, workspace,
+                              workspace_bytes, stream);
   }
   if (static_cast<int64_t>(B) * H_kv > kMaxCounters) return LK_ERR_UNSUPPORTED;
   if (num_blocks * block_size > 0x7fffffffLL) return LK_ERR_UNSUPPORTED;

@@ -53,6 +53,13 @@ struct GenericParams {
   int max_keys;        // > 0: context_lens beyond it are flagged and clamped
   int qt;              // query tokens per CTA
   float scale_log2;
+  // Split-KV (decode only): blockIdx.y is the split; split s covers keys
+  // [s * split_keys, (s + 1) * split_keys) and writes its (max, sum) and
+  // unnormalised output to part_ml / part_o for generic_merge_kernel.
+  int nsplit;          // 1: no split, the kernel writes out itself
+  int split_keys;
+  float* part_ml;      // [B * H][nsplit][2]
+  float* part_o;       // [B * H][nsplit][D]
 };
 
 template <typename T>
@@ -121,7 +128,8 @@ __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p
   float* Vs = Ks + kGKeys * (D + 1);        // [kGKeys][D]
   int* slots = reinterpret_cast<int*>(Vs + kGKeys * D);  // [2][kGKeys], -1 = zeros
 
-  const int kvh = blockIdx.x, tile = blockIdx.y, b = blockIdx.z;
+  const int kvh = blockIdx.x, b = blockIdx.z;
+  const int tile = p.nsplit > 1 ? 0 : blockIdx.y, sp = p.nsplit > 1 ? blockIdx.y : 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.G;
 
@@ -153,8 +161,10 @@ __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p
       atomicOr(p.status, LK_STATUS_CTX_OOB);
     prior = p.cu_seqlens_q ? 0 : -1;
   }
-  // keys [0, kv_end) feed this tile's rows
+  // keys [0, kv_end) feed this tile's rows; this CTA takes [kv_beg, kv_stop)
   const int kv_end = max(0, prior + i0 + ntok);
+  const int kv_beg = sp * p.split_keys;
+  const int kv_stop = p.nsplit > 1 ? min(kv_end, kv_beg + p.split_keys) : kv_end;
 
   // Q rows of the tile: row r = (token i0 + r / G, head kvh * G + r % G).
   const T* q = static_cast<const T*>(p.q);
@@ -171,7 +181,7 @@ __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p
 
   // Cache slot of key j (-1: past the keys, or an out-of-range block: zeros).
   auto slot_of = [&](int j) -> int {
-    if (j >= kv_end) return -1;
+    if (j >= kv_stop) return -1;
     if (bt) {
       const int blk = bt[j / p.bs];
       if (blk < 0 || blk >= p.num_blocks) {
@@ -189,8 +199,8 @@ __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p
   // slots of tile 0 in buffer 0; warp 0 keeps tile 1's in a register
   int pend = -1;
   if (warp == 0) {
-    slots[lane] = slot_of(lane);
-    pend = slot_of(kGKeys + lane);
+    slots[lane] = slot_of(kv_beg + lane);
+    pend = slot_of(kv_beg + kGKeys + lane);
   }
   __syncthreads();
 
@@ -224,7 +234,7 @@ __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p
     for (int t = 0; t < DV; ++t) o[k][t] = 0.f;
   }
 
-  for (int j0 = 0, buf = 0; j0 < kv_end; j0 += kGKeys, buf ^= 1) {
+  for (int j0 = kv_beg, buf = 0; j0 < kv_stop; j0 += kGKeys, buf ^= 1) {
     int* cur = slots + buf * kGKeys;
     int* nxt = slots + (buf ^ 1) * kGKeys;
     // 1. tile j0 into shared memory as fp32
@@ -275,7 +285,7 @@ __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p
     }
     __syncthreads();
     // 3. the next tile's loads fly while this tile is computed
-    if (j0 + kGKeys < kv_end) prefetch(nxt);
+    if (j0 + kGKeys < kv_stop) prefetch(nxt);
 
     // 4. scores, online softmax and PV for this warp's rows
 #pragma unroll
@@ -296,7 +306,7 @@ __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p
           s3 = fmaf(qv.w, kr[4 * d4 + 3], s3);
         }
         float s = (s0 + s1) + (s2 + s3);
-        const bool valid = j <= pos && j < kv_end;
+        const bool valid = j <= pos && j < kv_stop;
         s = valid ? s * p.scale_log2 : -INFINITY;
         float mt = s;
 #pragma unroll
@@ -325,6 +335,23 @@ __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p
     __syncthreads();  // Ks / Vs and this tile's slots are free again
   }
 
+  if (p.nsplit > 1) {  // decode split: one query token, rows = heads
+#pragma unroll
+    for (int k = 0; k < RPW; ++k) {
+      const int r = warp + k * kGWarps;
+      if (r < nrows) {
+        const int64_t idx = (static_cast<int64_t>(b) * p.H + kvh * G + r) * p.nsplit + sp;
+        if (lane == 0) {
+          p.part_ml[2 * idx] = m[k];
+          p.part_ml[2 * idx + 1] = l[k];
+        }
+        float* po = p.part_o + idx * D;
+#pragma unroll
+        for (int t = 0; t < DV; ++t) po[lane + 32 * t] = o[k][t];
+      }
+    }
+    return;
+  }
   T* out = static_cast<T*>(p.out);
 #pragma unroll
   for (int k = 0; k < RPW; ++k) {
@@ -337,6 +364,35 @@ __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p
       for (int t = 0; t < DV; ++t) st_f<T>(orow + lane + 32 * t, o[k][t] * inv);
     }
   }
+}
+
+// Merge of the decode splits: one warp per (sequence, query head). Weights
+// exp2(m_s - M) with M the largest split max; a row with no key is NaN.
+template <typename T, int D>
+__global__ void __launch_bounds__(128) generic_merge_kernel(GenericParams p, int rows) {
+  constexpr int DV = D / 32;
+  const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int b = row / p.H, h = row - b * p.H;
+  const float* ml = p.part_ml + static_cast<int64_t>(row) * p.nsplit * 2;
+  const float* po = p.part_o + static_cast<int64_t>(row) * p.nsplit * D;
+  float M = -INFINITY;
+  for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, ml[2 * s]);
+  float L = 0.f, o[DV];
+#pragma unroll
+  for (int t = 0; t < DV; ++t) o[t] = 0.f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < p.nsplit; ++s) {
+      const float w = exp2f(ml[2 * s] - M);  // 0 for an empty split
+      L = fmaf(ml[2 * s + 1], w, L);
+#pragma unroll
+      for (int t = 0; t < DV; ++t) o[t] = fmaf(po[s * D + lane + 32 * t], w, o[t]);
+    }
+  }
+  const float inv = L > 0.f ? 1.f / L : __int_as_float(0x7fc00000);  // no key: NaN
+  T* orow = static_cast<T*>(p.out) + b * p.out_stride + static_cast<int64_t>(h) * D;
+#pragma unroll
+  for (int t = 0; t < DV; ++t) st_f<T>(orow + lane + 32 * t, o[t] * inv);
 }
 
 size_t generic_smem_bytes(int D, int rpw) {
@@ -362,8 +418,12 @@ int launch_generic_r(const GenericParams& p, int num_seqs, int max_q_len, cudaSt
       done[dev] = true;
     }
   }
-  dim3 grid(p.H_kv, (max_q_len + p.qt - 1) / p.qt, num_seqs);
+  dim3 grid(p.H_kv, p.nsplit > 1 ? p.nsplit : (max_q_len + p.qt - 1) / p.qt, num_seqs);
   kern<<<grid, kGThreads, smem, s>>>(p);
+  if (p.nsplit > 1) {
+    const int rows = num_seqs * p.H;
+    generic_merge_kernel<T, D><<<(rows + 3) / 4, 128, 0, s>>>(p, rows);
+  }
   return lk::check_launch();
 }
 
@@ -404,41 +464,40 @@ int launch_generic(const GenericParams& p, int D, int num_seqs, int max_q_len, c
 
 }  // namespace
 
-extern "C" int lk_paged_attention_generic(
-    void* out, int64_t out_token_stride, const void* q, int64_t q_token_stride,
-    const void* k_cache, const void* v_cache, int64_t num_blocks, const int32_t* block_tables,
-    int64_t block_table_stride, const int32_t* cu_seqlens_q, const int32_t* context_lens,
-    int32_t num_seqs, int32_t max_q_len, int32_t H, int32_t H_kv, int32_t D, int32_t block_size,
-    int32_t max_blocks_per_seq, float scale, int32_t dtype, int32_t* status, void* stream) {
+namespace {
+
+// Splits of a decode whose contexts reach max_keys: about 512 keys (16
+// tiles) per split CTA, at most 64.
+int generic_decode_splits(int64_t max_keys) {
+  return static_cast<int>(std::min<int64_t>(64, std::max<int64_t>(1, (max_keys + 511) / 512)));
+}
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+size_t generic_split_bytes(int64_t rows, int D, int ns) {
+  return 256 + align256(static_cast<size_t>(rows) * ns * 2 * 4) +
+         align256(static_cast<size_t>(rows) * ns * D * 4);
+}
+
+int check_generic_args(int num_seqs, int max_q_len, int H, int H_kv, int D, int64_t num_blocks,
+                       int max_blocks_per_seq, int dtype) {
   if (num_seqs < 0 || max_q_len < 0 || H <= 0 || H_kv <= 0 || H % H_kv != 0 || num_blocks <= 0 ||
       max_blocks_per_seq < 0)
     return LK_ERR_INVALID_ARG;
-  if (num_seqs == 0 || max_q_len == 0) return LK_OK;
-  if (!out || !q || !k_cache || !v_cache) return LK_ERR_INVALID_ARG;
-  if (!cu_seqlens_q && max_q_len != 1) return LK_ERR_INVALID_ARG;
-  if (!block_tables && !cu_seqlens_q) return LK_ERR_INVALID_ARG;
   if (dtype != LK_DTYPE_F32 && dtype != LK_DTYPE_F16 && dtype != LK_DTYPE_BF16)
     return LK_ERR_UNSUPPORTED;
-  const int G = H / H_kv;
-  if (G > kGRows || (D != 32 && D != 64 && D != 96 && D != 128 && D != 256))
+  if (H / H_kv > kGRows || (D != 32 && D != 64 && D != 96 && D != 128 && D != 256))
     return LK_ERR_UNSUPPORTED;
   if (num_seqs > 65535 || H_kv > 65535) return LK_ERR_INVALID_ARG;
-  int64_t num_slots;
-  if (block_tables) {
-    if (block_size <= 0) return LK_ERR_INVALID_ARG;
-    num_slots = num_blocks * block_size;
-  } else {
-    num_slots = num_blocks;
-  }
-  if (num_slots > 0x7fffffffLL) return LK_ERR_UNSUPPORTED;
-  const int64_t max_keys =
-      block_tables && max_blocks_per_seq > 0 ? static_cast<int64_t>(max_blocks_per_seq) * block_size : 0;
-  if (max_keys > 0x7fffffffLL) return LK_ERR_UNSUPPORTED;
-  const int esz = lk::dtype_size(dtype);
-  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out) |
-       reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) &
-      (esz - 1))
-    return LK_ERR_ALIGNMENT;
+  return LK_OK;
+}
+
+GenericParams make_params(void* out, int64_t out_token_stride, const void* q,
+                          int64_t q_token_stride, const void* k_cache, const void* v_cache,
+                          int64_t num_blocks, int64_t num_slots, const int32_t* block_tables,
+                          int64_t block_table_stride, const int32_t* cu_seqlens_q,
+                          const int32_t* context_lens, int H, int H_kv, int block_size,
+                          int64_t max_keys, float scale, int32_t* status) {
   GenericParams p;
   p.out = out;
   p.out_stride = out_token_stride;
@@ -455,15 +514,112 @@ extern "C" int lk_paged_attention_generic(
   p.status = status;
   p.H = H;
   p.H_kv = H_kv;
-  p.G = G;
+  p.G = H / H_kv;
   p.bs = block_size;
   p.max_keys = static_cast<int>(max_keys);
-  p.qt = kGRows / G;  // refined with the rows per warp at launch
+  p.qt = kGRows / p.G;  // refined with the rows per warp at launch
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.nsplit = 1;
+  p.split_keys = 0;
+  p.part_ml = nullptr;
+  p.part_o = nullptr;
+  return p;
+}
+
+int run_generic(const GenericParams& p, int D, int dtype, int num_seqs, int max_q_len,
+                void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case LK_DTYPE_BF16: return launch_generic<__nv_bfloat16>(p, D, num_seqs, max_q_len, s);
     case LK_DTYPE_F16: return launch_generic<__half>(p, D, num_seqs, max_q_len, s);
     default: return launch_generic<float>(p, D, num_seqs, max_q_len, s);
   }
+}
+
+bool aligned_to(const void* a, const void* b, const void* c, const void* d, int esz) {
+  return ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+           reinterpret_cast<uintptr_t>(c) | reinterpret_cast<uintptr_t>(d)) &
+          static_cast<uintptr_t>(esz - 1)) == 0;
+}
+
+}  // namespace
+
+extern "C" size_t lk_paged_attention_generic_workspace_bytes(int32_t B, int32_t H, int32_t D,
+                                                             int32_t max_blocks_per_seq,
+                                                             int32_t block_size) {
+  if (B <= 0 || H <= 0 || D <= 0 || max_blocks_per_seq <= 0 || block_size <= 0) return 256;
+  const int ns = generic_decode_splits(static_cast<int64_t>(max_blocks_per_seq) * block_size);
+  return ns > 1 ? generic_split_bytes(static_cast<int64_t>(B) * H, D, ns) : 256;
+}
+
+namespace lk {
+
+int generic_decode(void* out, int64_t out_token_stride, const void* q, int64_t q_token_stride,
+                   const void* k_cache, const void* v_cache, int64_t num_blocks,
+                   const int32_t* block_tables, int64_t block_table_stride,
+                   const int32_t* context_lens, int B, int H, int H_kv, int D, int block_size,
+                   int max_blocks_per_seq, float scale, int dtype, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  int rc = check_generic_args(B, 1, H, H_kv, D, num_blocks, max_blocks_per_seq, dtype);
+  if (rc != LK_OK) return rc;
+  if (B == 0) return LK_OK;
+  if (!out || !q || !k_cache || !v_cache || !block_tables || !context_lens || block_size <= 0 ||
+      max_blocks_per_seq <= 0)
+    return LK_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < 4 || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return LK_ERR_WORKSPACE;
+  const int64_t num_slots = num_blocks * block_size;
+  const int64_t max_keys = static_cast<int64_t>(max_blocks_per_seq) * block_size;
+  if (num_slots > 0x7fffffffLL || max_keys > 0x7fffffffLL) return LK_ERR_UNSUPPORTED;
+  if (!aligned_to(q, out, k_cache, v_cache, lk::dtype_size(dtype))) return LK_ERR_ALIGNMENT;
+  GenericParams p = make_params(out, out_token_stride, q, q_token_stride, k_cache, v_cache,
+                                num_blocks, num_slots, block_tables, block_table_stride, nullptr,
+                                context_lens, H, H_kv, block_size, max_keys, scale,
+                                static_cast<int32_t*>(workspace));
+  // As many splits as the workspace holds, up to generic_decode_splits.
+  const int64_t rows = static_cast<int64_t>(B) * H;
+  int ns = generic_decode_splits(max_keys);
+  while (ns > 1 && generic_split_bytes(rows, D, ns) > workspace_bytes) --ns;
+  if (ns > 1) {
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    p.nsplit = ns;
+    p.split_keys = static_cast<int>((((max_keys + ns - 1) / ns) + kGKeys - 1) / kGKeys * kGKeys);
+    p.part_ml = reinterpret_cast<float*>(ws + 256);
+    p.part_o = reinterpret_cast<float*>(ws + 256 + align256(static_cast<size_t>(rows) * ns * 8));
+  }
+  return run_generic(p, D, dtype, B, 1, stream);
+}
+
+}  // namespace lk
+
+extern "C" int lk_paged_attention_generic(
+    void* out, int64_t out_token_stride, const void* q, int64_t q_token_stride,
+    const void* k_cache, const void* v_cache, int64_t num_blocks, const int32_t* block_tables,
+    int64_t block_table_stride, const int32_t* cu_seqlens_q, const int32_t* context_lens,
+    int32_t num_seqs, int32_t max_q_len, int32_t H, int32_t H_kv, int32_t D, int32_t block_size,
+    int32_t max_blocks_per_seq, float scale, int32_t dtype, int32_t* status, void* stream) {
+  int rc = check_generic_args(num_seqs, max_q_len, H, H_kv, D, num_blocks, max_blocks_per_seq,
+                              dtype);
+  if (rc != LK_OK) return rc;
+  if (num_seqs == 0 || max_q_len == 0) return LK_OK;
+  if (!out || !q || !k_cache || !v_cache) return LK_ERR_INVALID_ARG;
+  if (!cu_seqlens_q && max_q_len != 1) return LK_ERR_INVALID_ARG;
+  if (!block_tables && !cu_seqlens_q) return LK_ERR_INVALID_ARG;
+  int64_t num_slots;
+  if (block_tables) {
+    if (block_size <= 0) return LK_ERR_INVALID_ARG;
+    num_slots = num_blocks * block_size;
+  } else {
+    num_slots = num_blocks;
+  }
+  if (num_slots > 0x7fffffffLL) return LK_ERR_UNSUPPORTED;
+  const int64_t max_keys =
+      block_tables && max_blocks_per_seq > 0 ? static_cast<int64_t>(max_blocks_per_seq) * block_size : 0;
+  if (max_keys > 0x7fffffffLL) return LK_ERR_UNSUPPORTED;
+  if (!aligned_to(q, out, k_cache, v_cache, lk::dtype_size(dtype))) return LK_ERR_ALIGNMENT;
+  const GenericParams p = make_params(out, out_token_stride, q, q_token_stride, k_cache, v_cache,
+                                      num_blocks, num_slots, block_tables, block_table_stride,
+                                      cu_seqlens_q, context_lens, H, H_kv, block_size, max_keys,
+                                      scale, status);
+  return run_generic(p, D, dtype, num_seqs, max_q_len, stream);
 }

@@ -232,3 +232,26 @@ def test_generic_decode_unaligned_caches(cuda):
                     b.context_lens, b.scale)
     assert_attn_close(out, ref)
     assert torch.equal(out, aligned)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_generic_split_decode_matches_single_pass(cuda, dtype):
+    """lk_paged_decode splits long contexts across CTAs for the generic kernel
+    (partials merged by a second launch); lk_paged_attention_generic runs one
+    CTA per row. Both match the oracle, an empty split included (row 3 is far
+    shorter than the table)."""
+    b = workloads.make_decode_batch(2, 5, seed=27, ctx=[5000, 700, 31, 2048, 0], H=32, H_kv=8,
+                                    D=64, dtype=dtype, device=cuda)
+    assert _lib.lib().lk_paged_attention_generic_workspace_bytes(5, 32, 64, 313, 16) > 256
+    split = ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables,
+                             b.context_lens, b.scale)
+    single = ops.paged_attention_generic(b.query, b.key_cache, b.value_cache, b.scale,
+                                         block_tables=b.block_tables,
+                                         context_lens=b.context_lens)
+    ref = pa.decode(b.query.float(), b.key_cache.float(), b.value_cache.float(), b.block_tables,
+                    b.context_lens, b.scale)
+    tol = (FP32_MAX_ABS, FP32_MEAN_REL) if dtype == torch.float32 else ()
+    assert_attn_close(split, ref, *tol)
+    assert_attn_close(single, ref, *tol)
+    assert torch.isnan(split[4]).all()
+    assert ops.decode_status() == 0
