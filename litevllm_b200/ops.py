@@ -178,12 +178,13 @@ def paged_decode(
     if num_splits == 0:  # auto split count; -1 selects the persistent kernel
         num_splits = decode_num_splits(B, H_kv, max_blocks, bs)
     need = decode_workspace_bytes(B, H, H_kv, D, num_splits)
+    want = need
     if not tuned_attention_shape(query.dtype, D, bs, H // H_kv):
-        # the generic kernel's split-KV partials
-        need = max(need, int(lib().lk_paged_attention_generic_workspace_bytes(
+        # room for the generic kernel's split-KV partials (less only means fewer splits)
+        want = max(need, int(lib().lk_paged_attention_generic_workspace_bytes(
             B, H, D, max_blocks, bs)))
     if workspace is None:
-        workspace = WORKSPACES.get(dev, f"decode:{_stream(dev)}", need)
+        workspace = WORKSPACES.get(dev, f"decode:{_stream(dev)}", want)
     elif workspace.numel() * workspace.element_size() < need:
         raise ValueError(f"workspace too small: need {need} bytes")
     with _on(dev):
