@@ -60,10 +60,17 @@ int prefix_attention(const void* q, int64_t q_stride, const void* k_cache, const
                      float scale, float* part_ml, float* part_o, int part_splits, int dtype,
                      int32_t* status, int* zeroed_counter, cudaStream_t s);
 
+// Head of every decode workspace: the status word (padded to 256 B), then the
+// split kernel's per-(sequence, head group) counters, which every completed
+// call leaves zero and which no other use of the workspace may touch.
+constexpr int64_t kDecodeMaxCounters = 65536;
+constexpr size_t kDecodeHeadBytes = 256 + kDecodeMaxCounters * 4;
+
 // Decode on the generic CUDA-core kernel (paged_generic.cu) for the shapes
 // lk_paged_decode's split kernel does not take; split-KV with a merge launch
-// when the workspace has room for the partials. Status bits go to the
-// workspace's first word.
+// when the workspace has room for the partials (placed after
+// kDecodeHeadBytes, so a later split-kernel call on the same workspace finds
+// its counters zero). Status bits go to the workspace's first word.
 int generic_decode(void* out, int64_t out_token_stride, const void* q, int64_t q_token_stride,
                    const void* k_cache, const void* v_cache, int64_t num_blocks,
                    const int32_t* block_tables, int64_t block_table_stride,

@@ -916,8 +916,8 @@ paged_decode_persistent_kernel(const __grid_constant__ CUtensorMap kmap,
 // Workspace layout: [status: int32, padded to 256 B][counters: kMaxCounters
 // int32, a fixed region so that calls with different B find it where the
 // previous call left it zeroed][part_ml: B*splits*H*2 f32][part_o: B*splits*H*D f32]
-constexpr int64_t kMaxCounters = 65536;
-constexpr size_t kHeadBytes = 256 + kMaxCounters * 4;
+constexpr int64_t kMaxCounters = lk::kDecodeMaxCounters;
+constexpr size_t kHeadBytes = lk::kDecodeHeadBytes;
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 // ------------------------------------------------------------------------

@@ -474,8 +474,11 @@ int generic_decode_splits(int64_t max_keys) {
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
+// Decode workspace with split partials: the decode head (status word and the
+// split kernel's counters, left untouched here), then (max, sum) and output
+// partials.
 size_t generic_split_bytes(int64_t rows, int D, int ns) {
-  return 256 + align256(static_cast<size_t>(rows) * ns * 2 * 4) +
+  return lk::kDecodeHeadBytes + align256(static_cast<size_t>(rows) * ns * 2 * 4) +
          align256(static_cast<size_t>(rows) * ns * D * 4);
 }
 
@@ -584,8 +587,9 @@ int generic_decode(void* out, int64_t out_token_stride, const void* q, int64_t q
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     p.nsplit = ns;
     p.split_keys = static_cast<int>((((max_keys + ns - 1) / ns) + kGKeys - 1) / kGKeys * kGKeys);
-    p.part_ml = reinterpret_cast<float*>(ws + 256);
-    p.part_o = reinterpret_cast<float*>(ws + 256 + align256(static_cast<size_t>(rows) * ns * 8));
+    p.part_ml = reinterpret_cast<float*>(ws + lk::kDecodeHeadBytes);
+    p.part_o = reinterpret_cast<float*>(ws + lk::kDecodeHeadBytes +
+                                        align256(static_cast<size_t>(rows) * ns * 8));
   }
   return run_generic(p, D, dtype, B, 1, stream);
 }

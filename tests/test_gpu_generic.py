@@ -255,3 +255,43 @@ def test_generic_split_decode_matches_single_pass(cuda, dtype):
     assert_attn_close(single, ref, *tol)
     assert torch.isnan(split[4]).all()
     assert ops.decode_status() == 0
+
+
+def test_generic_decode_with_small_caller_workspace(cuda):
+    """A caller workspace sized for the split kernel only (below the generic
+    kernel's full split size) gives fewer splits, not an error; same results."""
+    b = workloads.make_decode_batch(2, 4, seed=28, ctx=[6000, 1, 513, 4096], H=32, H_kv=8,
+                                    D=64, device=cuda)
+    mb = b.block_tables.shape[1]
+    ns = ops.decode_num_splits(4, 8, mb, 16)
+    small = ops.decode_workspace_bytes(4, 32, 8, 64, ns)
+    full = _lib.lib().lk_paged_attention_generic_workspace_bytes(4, 32, 64, mb, 16)
+    assert small < full
+    ws = torch.zeros(small, dtype=torch.uint8, device=cuda)
+    out = ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables, b.context_lens,
+                           b.scale, workspace=ws)
+    ref = pa.decode(b.query.float(), b.key_cache.float(), b.value_cache.float(), b.block_tables,
+                    b.context_lens, b.scale)
+    assert_attn_close(out, ref)
+    assert ops.decode_status(ws) == 0
+
+
+def test_generic_split_then_tuned_decode_share_a_workspace(cuda):
+    """The generic split partials sit after the split kernel's counter region:
+    a tuned decode that reuses the same workspace after a generic split decode
+    still finds its counters zero and matches the oracle."""
+    g = workloads.make_decode_batch(2, 8, seed=29, ctx=[4096] * 8, H=32, H_kv=8, D=64,
+                                    device=cuda)
+    t = workloads.make_decode_batch(2, 32, seed=30, device=cuda)
+    need = max(_lib.lib().lk_paged_attention_generic_workspace_bytes(8, 32, 64, 256, 16),
+               ops.decode_workspace_bytes(32, 32, 8, 128, 8))
+    ws = torch.zeros(need, dtype=torch.uint8, device=cuda)
+    for _ in range(2):
+        ops.paged_decode(g.query, g.key_cache, g.value_cache, g.block_tables, g.context_lens,
+                         g.scale, workspace=ws)
+        out = ops.paged_decode(t.query, t.key_cache, t.value_cache, t.block_tables,
+                               t.context_lens, t.scale, num_splits=8, workspace=ws)
+        ref = pa.decode(t.query.float(), t.key_cache.float(), t.value_cache.float(),
+                        t.block_tables, t.context_lens, t.scale)
+        assert_attn_close(out, ref)
+    assert ops.decode_status(ws) == 0
