@@ -123,6 +123,33 @@ def test_ops_refuse_cpu_tensors():
         ops.store_kvcache(torch.zeros(1, 8, 128, dtype=torch.bfloat16),
                           torch.zeros(1, 8, 128, dtype=torch.bfloat16), kc, kc,
                           torch.zeros(1, dtype=torch.int64))
+    # shapes for the generic kernel (fp32, head_dim 64) are refused the same way
+    q32 = torch.zeros(2, 32, 64)
+    kc32 = torch.zeros(4, 16, 8, 64)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.paged_decode(q32, kc32, kc32, torch.zeros(2, 1, dtype=torch.int32),
+                         torch.ones(2, dtype=torch.int32), 0.1)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.paged_attention_generic(q32, kc32, kc32, 0.1,
+                                    block_tables=torch.zeros(2, 1, dtype=torch.int32),
+                                    context_lens=torch.ones(2, dtype=torch.int32))
+
+
+def test_generic_shape_routing_and_workspace_sizes():
+    from litevllm_b200 import ops
+
+    assert ops.tuned_attention_shape(torch.bfloat16, 128, 16, 4)
+    assert not ops.tuned_attention_shape(torch.float32, 128, 16, 4)
+    assert not ops.tuned_attention_shape(torch.bfloat16, 64, 16, 4)
+    assert not ops.tuned_attention_shape(torch.bfloat16, 128, 8, 4)
+    assert not ops.tuned_attention_shape(torch.bfloat16, 128, 16, 3)
+    f = _lib.lib().lk_paged_attention_generic_workspace_bytes
+    head = 256 + 65536 * 4
+    assert f(256, 32, 64, 32, 16) == 256          # 512 keys: one split, status word only
+    # 4096 keys -> 8 splits of 512: head, then (max, sum) and output partials
+    assert f(256, 32, 64, 256, 16) == head + 256 * 32 * 8 * 2 * 4 + 256 * 32 * 8 * 64 * 4
+    assert f(1, 1, 64, 100000, 16) == head + 64 * 2 * 4 + 64 * 64 * 4   # capped at 64 splits
+    assert f(0, 32, 64, 256, 16) == 256
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
