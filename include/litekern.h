@@ -254,7 +254,8 @@ int lk_paged_prefill_ws(void* out, const void* q, int64_t q_token_stride,
  * with IEEE fp32 division and addition; ties go to the lowest index; a NaN key
  * beats every number (torch.argmax semantics). g is read from `noise`
  * ([B, noise_ld] fp32) when non-NULL, else generated in-kernel as
- * g = -log(-log(u)), u from Philox4x32-10 keyed by (seed, offset, b, v);
+ * g = -ln(-ln(u)), u from Philox4x32-10 keyed by (seed, offset, b, v), the
+ * logarithms from hardware base-2 logarithms (within 5e-7 relative of exact);
  * noise_dump ([B, V] fp32, optional) receives the generated g.
  * logits: [B, V] with row stride ld elements, dtype F32, F16 or BF16.
  * out_ids: int64 [B]. workspace: lk_sample_workspace_bytes(B, V) bytes,
@@ -346,6 +347,18 @@ int lk_sample_filtered(int64_t* out_ids, const void* logits, int32_t B, int32_t 
 int lk_selftest_wait_timeout(int32_t* status, uint64_t timeout_ns, void* stream);
 
 /*
+ * Self-tests of two pieces of the in-kernel-noise sampler (no counterpart in
+ * the reference). lk_selftest_sampler_div writes out[j * n + i] = x[i] /
+ * temps[j] as the sampler computes it (Markstein's correction of x * RN(1/T),
+ * IEEE division for out-of-range inputs); a caller compares it with IEEE
+ * fp32 division. lk_selftest_gumbel writes the Gumbel noise the sampler
+ * derives from each 32-bit Philox word bits[i].
+ */
+int lk_selftest_sampler_div(float* out, const float* x, int32_t n, const float* temps, int32_t nt,
+                            void* stream);
+int lk_selftest_gumbel(float* out, const uint32_t* bits, int32_t n, void* stream);
+
+/*
  * Allocation-free variant of lk_sample. It has no counterpart in the
  * reference. It is for callers that cannot call cudaMalloc at the point where
  * they sample: code running while another component owns the allocator
@@ -355,11 +368,15 @@ int lk_selftest_wait_timeout(int32_t* status, uint64_t timeout_ns, void* stream)
  * file-scope 160 KiB __device__ scratch array that every GPU which loads this
  * library holds until the process exits; the call itself allocates and frees
  * nothing. Limits: B <= 8192 rows and B * chunks <= 16384, where chunks is
- * the vocabulary split lk_sample would use (at most ceil(4 * SMs / B), and 1
- * for V <= 4096); larger problems return LK_ERR_TOO_LARGE before any launch.
+ * the vocabulary split of the call (greedy and noise-tensor rows: at most
+ * 6 * SMs / B, and 1 for V <= 2048; in-kernel-noise rows lengthen their
+ * chunks to stay within the limit), so every B <= 8192 fits on a 148-SM
+ * B200; larger problems return LK_ERR_TOO_LARGE before any launch.
  * The first call on each device looks up the array's device address with
- * that device current (cudaGetSymbolAddress); make that first call before
- * any stream capture. Every call shares the one array: calls that overlap on
+ * that device current (cudaGetSymbolAddress) and keeps it for the life of the
+ * process; make that first call before any stream capture. The kept address
+ * does not survive cudaDeviceReset on that device (a new context places the
+ * array elsewhere): do not call this entry point after resetting a device. Every call shares the one array: calls that overlap on
  * the GPU (other streams, other threads) race and must be serialised by the
  * caller. Each call clears the counters it uses, so an earlier aborted call
  * leaves nothing behind. Arguments and results are those of lk_sample.

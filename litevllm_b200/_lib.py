@@ -87,6 +87,8 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "lk_host_device_pointer": (c_int32, [c_void_p, c_void_p]),
     "lk_selftest_wait_timeout": (c_int32, [c_void_p, c_uint64, c_void_p]),
+    "lk_selftest_sampler_div": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_void_p]),
+    "lk_selftest_gumbel": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p]),
     "lk_sample_filtered": (
         c_int32,
         [c_void_p, c_void_p, c_int32, c_int32, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,

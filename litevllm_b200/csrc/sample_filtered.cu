@@ -20,6 +20,7 @@
 // breaks such ties in an unspecified order).
 #include "lk_common.cuh"
 #include "lk_host.h"
+#include "lk_philox.cuh"
 
 namespace {
 
@@ -38,33 +39,20 @@ struct FilterParams {
   const float* top_p;     // [B] or NULL (>= 1: off)
   const float* noise;
   int64_t noise_ld;
-  uint32_t seed_lo, seed_hi, off_lo, off_hi;
+  uint32_t off_lo, off_hi;
+  lk::PhiloxKey key;  // round keys of the seed
   int64_t* out;
 };
 
-// Philox4x32-10 (Salmon et al., SC'11) and the u -> Gumbel map of the main
-// sampler, so that the filtered and unfiltered draws share one noise stream.
-struct U4f { uint32_t x, y, z, w; };
-LK_DEVINL U4f philox(U4f c, uint32_t k0, uint32_t k1) {
-  constexpr uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u, W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
-#pragma unroll
-  for (int r = 0; r < 10; ++r) {
-    const uint32_t hi0 = __umulhi(M0, c.x), lo0 = M0 * c.x;
-    const uint32_t hi1 = __umulhi(M1, c.z), lo1 = M1 * c.z;
-    c = U4f{hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0};
-    k0 += W0;
-    k1 += W1;
-  }
-  return c;
-}
+// In-kernel noise: the main sampler's Philox stream and u -> Gumbel map
+// (lk_philox.cuh), so that the filtered and unfiltered draws share one noise
+// stream.
 LK_DEVINL float gumbel_at(const FilterParams& p, int b, int v) {
   if (p.noise) return p.noise[static_cast<int64_t>(b) * p.noise_ld + v];
-  const U4f r = philox(U4f{static_cast<uint32_t>(v >> 2), static_cast<uint32_t>(b), p.off_lo,
-                           p.off_hi},
-                       p.seed_lo, p.seed_hi);
+  const lk::U4 r = lk::philox4x32_10(
+      lk::U4{static_cast<uint32_t>(v >> 2), static_cast<uint32_t>(b), p.off_lo, p.off_hi}, p.key);
   const uint32_t w = (v & 3) == 0 ? r.x : (v & 3) == 1 ? r.y : (v & 3) == 2 ? r.z : r.w;
-  const float u = (static_cast<float>(w >> 9) + 0.5f) * 1.1920928955078125e-07f;
-  return -logf(-logf(u));
+  return lk::gumbel_from_bits(w);
 }
 
 template <typename T> LK_DEVINL uint32_t bits16(T x);
@@ -276,8 +264,7 @@ extern "C" int lk_sample_filtered(int64_t* out_ids, const void* logits, int32_t 
   p.top_p = top_p;
   p.noise = noise;
   p.noise_ld = noise_ld;
-  p.seed_lo = static_cast<uint32_t>(seed);
-  p.seed_hi = static_cast<uint32_t>(seed >> 32);
+  p.key = lk::philox_key(seed);
   p.off_lo = static_cast<uint32_t>(offset);
   p.off_hi = static_cast<uint32_t>(offset >> 32);
   p.out = out_ids;

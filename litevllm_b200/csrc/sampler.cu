@@ -15,12 +15,13 @@
 // shared memory. The last CTA of a row to finish (atomic counter, no
 // waiting) reduces the per-chunk winners and writes the int64 token id.
 //
-// In-kernel noise: u = ((r >> 9) + 0.5) * 2^-23 with r from Philox4x32-10
-// (Salmon, Moraes, Dror, Shaw, "Parallel Random Numbers: As Easy as 1, 2, 3",
-// SC'11) keyed by the 64-bit seed, counter (v / 4, b, offset_lo, offset_hi);
-// word v % 4 of the block feeds element v. g = -log(-log(u)) with CUDA logf.
+// In-kernel noise (lk_philox.cuh): u = ((r >> 9) + 0.5) * 2^-23 with r from
+// Philox4x32-10 keyed by the 64-bit seed, counter (v / 4, b, offset_lo,
+// offset_hi); word v % 4 of the block feeds element v; g = -ln(-ln u) from
+// hardware base-2 logarithms (within 5e-7 relative of the exact value).
 #include "lk_common.cuh"
 #include "lk_host.h"
+#include "lk_philox.cuh"
 
 #include <cooperative_groups.h>
 #include <stdlib.h>
@@ -35,6 +36,7 @@ namespace {
 constexpr int kSampThreads = 256;
 constexpr int kVec = 8;  // elements per 16-byte vector of 16-bit logits
 constexpr int kSampCtasPerSm = 6;
+constexpr int kGumbelCtasPerSm = 4;
 
 struct SampleParams {
   const void* logits;
@@ -45,43 +47,30 @@ struct SampleParams {
   const float* temps;
   const float* noise;
   int64_t noise_ld;
-  uint32_t seed_lo, seed_hi, off_lo, off_hi;
+  uint32_t off_lo, off_hi;
+  lk::PhiloxKey key;  // round keys of the seed
   float* noise_dump;
   int64_t* out;
   float* part_key;   // [B][nchunks]
   int32_t* part_idx; // [B][nchunks]
   int32_t* counters; // [B]
+  int nv;             // whole 16-byte vectors per row
+  int gumbel;         // 1: gumbel_kernel takes the call
 };
 
-// ------------------------------------------------------------- Philox ---
-struct U4 { uint32_t x, y, z, w; };
-
-LK_DEVINL U4 philox4x32_10(U4 c, uint32_t k0, uint32_t k1) {
-  constexpr uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u;
-  constexpr uint32_t W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
-#pragma unroll
-  for (int r = 0; r < 10; ++r) {
-    // one 32 x 32 -> 64-bit product gives both halves
-    const uint64_t p0 = static_cast<uint64_t>(M0) * c.x, p1 = static_cast<uint64_t>(M1) * c.z;
-    const uint32_t hi0 = static_cast<uint32_t>(p0 >> 32), lo0 = static_cast<uint32_t>(p0);
-    const uint32_t hi1 = static_cast<uint32_t>(p1 >> 32), lo1 = static_cast<uint32_t>(p1);
-    c = U4{hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0};
-    k0 += W0;
-    k1 += W1;
-  }
-  return c;
-}
-
-LK_DEVINL float gumbel_from_bits(uint32_t r) {
-  const float u = (static_cast<float>(r >> 9) + 0.5f) * 1.1920928955078125e-07f;  // 2^-23
-  return -logf(-logf(u));
-}
+using lk::U4;
 
 // ---------------------------------------------------------- comparisons ---
 // a beats the current best (b) if it is larger, or NaN where b is not; the
 // caller visits indices in increasing order so equal keys keep the earlier.
 LK_DEVINL bool beats_later(float a, float b) {
   return a > b || (a != a && b == b);
+}
+// NaN-propagating fp32 max.
+LK_DEVINL float fmax_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
 }
 // Full comparison for merging two candidates with explicit indices.
 LK_DEVINL bool beats(float ka, int ia, float kb, int ib) {
@@ -150,13 +139,13 @@ LK_DEVINL void scan_chunk(const SampleParams& p, int b, int v0, int v1, float te
       } else if constexpr (MODE == 2) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const U4 r = philox4x32_10(U4{static_cast<uint32_t>((vv >> 2) + h),
-                                        static_cast<uint32_t>(b), p.off_lo, p.off_hi},
-                                     p.seed_lo, p.seed_hi);
-          g[4 * h + 0] = gumbel_from_bits(r.x);
-          g[4 * h + 1] = gumbel_from_bits(r.y);
-          g[4 * h + 2] = gumbel_from_bits(r.z);
-          g[4 * h + 3] = gumbel_from_bits(r.w);
+          const U4 r = lk::philox4x32_10(U4{static_cast<uint32_t>((vv >> 2) + h),
+                                            static_cast<uint32_t>(b), p.off_lo, p.off_hi},
+                                         p.key);
+          g[4 * h + 0] = lk::gumbel_from_bits(r.x);
+          g[4 * h + 1] = lk::gumbel_from_bits(r.y);
+          g[4 * h + 2] = lk::gumbel_from_bits(r.z);
+          g[4 * h + 3] = lk::gumbel_from_bits(r.w);
         }
         if (drow) {
           reinterpret_cast<float4*>(drow + vv)[0] = make_float4(g[0], g[1], g[2], g[3]);
@@ -207,11 +196,11 @@ LK_DEVINL void scan_chunk(const SampleParams& p, int b, int v0, int v1, float te
     if constexpr (MODE == 1) {
       g = nrow[v];
     } else if constexpr (MODE == 2) {
-      const U4 r = philox4x32_10(U4{static_cast<uint32_t>(v >> 2), static_cast<uint32_t>(b),
-                                    p.off_lo, p.off_hi},
-                                 p.seed_lo, p.seed_hi);
+      const U4 r = lk::philox4x32_10(U4{static_cast<uint32_t>(v >> 2), static_cast<uint32_t>(b),
+                                        p.off_lo, p.off_hi},
+                                     p.key);
       const uint32_t w = (v & 3) == 0 ? r.x : (v & 3) == 1 ? r.y : (v & 3) == 2 ? r.z : r.w;
-      g = gumbel_from_bits(w);
+      g = lk::gumbel_from_bits(w);
       if (drow) drow[v] = g;
     }
     visit(x, v, g);
@@ -248,17 +237,10 @@ LK_DEVINL void block_reduce(float& k, int& i) {
   }
 }
 
-template <typename T, bool VEC>
-__global__ void __launch_bounds__(kSampThreads, kSampCtasPerSm) sample_kernel(const SampleParams p) {
-  lk::pdl_wait();  // launched to overlap the kernel ahead of it: wait for it before reading
-  const int ch = blockIdx.x, b = blockIdx.y;
-  const float temp = p.temps ? p.temps[b] : 0.f;
-  const int v0 = ch * p.chunk, v1 = min(p.V, v0 + p.chunk);
-  float best = -INFINITY;
-  int besti = 0x7fffffff;
-  if (!(temp > 0.f)) scan_chunk<T, VEC, 0>(p, b, v0, v1, temp, best, besti);
-  else if (p.noise) scan_chunk<T, VEC, 1>(p, b, v0, v1, temp, best, besti);
-  else scan_chunk<T, VEC, 2>(p, b, v0, v1, temp, best, besti);
+// Block winner -> row result: a one-chunk row writes its id; otherwise the
+// chunk's winner goes to the workspace and the row's last CTA to finish
+// (atomic counter, no waiting) reduces the winners and resets the counter.
+LK_DEVINL void finish_row(const SampleParams& p, int b, int ch, float best, int besti) {
   block_reduce(best, besti);
   if (p.nchunks == 1) {
     if (threadIdx.x == 0) p.out[b] = besti == 0x7fffffff ? 0 : besti;
@@ -291,6 +273,92 @@ __global__ void __launch_bounds__(kSampThreads, kSampCtasPerSm) sample_kernel(co
     p.counters[b] = 0;
   }
 }
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(kSampThreads, kSampCtasPerSm) sample_kernel(const SampleParams p) {
+  lk::pdl_wait();  // launched to overlap the kernel ahead of it: wait for it before reading
+  const int ch = blockIdx.x, b = blockIdx.y;
+  const float temp = p.temps ? p.temps[b] : 0.f;
+  const int v0 = ch * p.chunk, v1 = min(p.V, v0 + p.chunk);
+  float best = -INFINITY;
+  int besti = 0x7fffffff;
+  if (!(temp > 0.f)) scan_chunk<T, VEC, 0>(p, b, v0, v1, temp, best, besti);
+  else if (p.noise) scan_chunk<T, VEC, 1>(p, b, v0, v1, temp, best, besti);
+  else scan_chunk<T, VEC, 2>(p, b, v0, v1, temp, best, besti);
+  finish_row(p, b, ch, best, besti);
+}
+
+// In-kernel-noise rows of 16-bit logits (16-byte aligned rows, gumbel_kernel
+// below): the sampled path of config 4 / 5. It is bound by instruction issue, not HBM: per
+// element a quarter Philox block, two hardware logarithms and the division,
+// so every step here is trimmed to few instructions:
+//  * Philox round keys arrive as kernel parameters (constant operands);
+//  * x / T is the IEEE quotient computed as in Markstein's theorem (P.
+//    Markstein, "Computation of elementary functions on the IBM RISC
+//    System/6000 processor", IBM J. Res. Dev. 34(1), 1990): with y = RN(1/T)
+//    and q0 = RN(x y), r = x - q0 T is exact and RN(q0 + r y) is the
+//    correctly rounded x / T when nothing underflows or overflows. Vectors
+//    with an element outside [xlo, xhi] (zeros, infinities, NaN, tiny or
+//    huge values for this T) take __fdiv_rn instead; tested against IEEE
+//    division over every 16-bit value;
+//  * the running best is compared once per 8-element vector (NaN-propagating
+//    max of its keys); only a vector that improves it is searched for the
+//    element, which after the first few vectors is rare.
+struct FastDiv {
+  float t, y, xlo, xhi;
+  LK_DEVINL static FastDiv make(float temp) {
+    FastDiv d;
+    d.t = temp;
+    d.y = __frcp_rn(temp);
+    // |x| in [xlo, xhi] keeps q0, r and the result normal and finite
+    const bool ok = temp >= 0x1p-60f && temp <= 0x1p60f;
+    d.xlo = ok ? 0x1p-98f * fmaxf(1.f, temp) : INFINITY;
+    d.xhi = ok ? 0x1p98f * fminf(1.f, temp) : 0.f;
+    return d;
+  }
+  LK_DEVINL bool in_range(float x) const { return fabsf(x) >= xlo && fabsf(x) <= xhi; }
+  LK_DEVINL float fast(float x) const {
+    const float q0 = __fmul_rn(x, y);
+    const float r = fmaf(-q0, t, x);
+    return fmaf(r, y, q0);
+  }
+};
+
+template <typename T>
+LK_DEVINL void gumbel_keys(const SampleParams& p, const FastDiv& dv, int b, int vv,
+                           const uint4& raw, float (&key)[8], float* drow) {
+  float f[8];
+  Load16<T>::cvt(raw, f);
+  float g[8];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const U4 r = lk::philox4x32_10(
+        U4{static_cast<uint32_t>((vv >> 2) + h), static_cast<uint32_t>(b), p.off_lo, p.off_hi},
+        p.key);
+    g[4 * h + 0] = lk::gumbel_from_bits(r.x);
+    g[4 * h + 1] = lk::gumbel_from_bits(r.y);
+    g[4 * h + 2] = lk::gumbel_from_bits(r.z);
+    g[4 * h + 3] = lk::gumbel_from_bits(r.w);
+  }
+  if (drow) {
+    reinterpret_cast<float4*>(drow + vv)[0] = make_float4(g[0], g[1], g[2], g[3]);
+    reinterpret_cast<float4*>(drow + vv)[1] = make_float4(g[4], g[5], g[6], g[7]);
+  }
+  bool fast = true;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) fast = fast && dv.in_range(f[e]);
+  float q[8];
+  if (fast) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) q[e] = dv.fast(f[e]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) q[e] = __fdiv_rn(f[e], dv.t);
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) key[e] = __fadd_rn(q[e], g[e]);
+}
+
 
 // ---------------------------------------------------- softmax(x / T) ---
 template <typename T>
@@ -358,11 +426,6 @@ template <> LK_DEVINL uint32_t pmax_nan<__nv_bfloat16>(uint32_t a, uint32_t b) {
 template <> LK_DEVINL uint32_t pmax_nan<__half>(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-LK_DEVINL float fmax_nan(float a, float b) {
-  float d;
-  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
   return d;
 }
 template <typename T> LK_DEVINL float half_lo(uint32_t w);
@@ -625,6 +688,83 @@ __global__ void __launch_bounds__(kSampThreads) argmax_bulk_kernel(const SampleP
   }
 }
 
+// One row segment [j0, j1) of 16-byte vectors (plus, with tail, the row's
+// V % 8 ragged elements) of an in-kernel-noise row.
+template <typename T>
+LK_DEVINL void gumbel_segment(const SampleParams& p, int b, int j0, int j1, bool tail, float temp,
+                              float& best, int& besti) {
+  const T* row = static_cast<const T*>(p.logits) + static_cast<int64_t>(b) * p.ld;
+  const int nv = p.nv;
+      float* drow = p.noise_dump ? p.noise_dump + static_cast<int64_t>(b) * p.V : nullptr;
+      const FastDiv dv = FastDiv::make(temp);
+      // Each thread takes vectors j, j + 256, ... of the segment, loading two
+      // before computing them; a vector's keys are compared once through
+      // their NaN-propagating max, and only a vector that improves the
+      // running best is searched for the element (rare after the first few).
+      // Measured against computing two vectors before comparing either and
+      // loading the next two ahead: that form ran 10 % slower here.
+      const uint4* rowv = reinterpret_cast<const uint4*>(row);
+      auto consider = [&](const uint4& raw, int j) {
+        float k[8];
+        gumbel_keys<T>(p, dv, b, j * kVec, raw, k, drow);
+        const float m = fmax_nan(fmax_nan(fmax_nan(k[0], k[1]), fmax_nan(k[2], k[3])),
+                                 fmax_nan(fmax_nan(k[4], k[5]), fmax_nan(k[6], k[7])));
+        if (beats_later(m, best)) {
+          const bool want_nan = m != m;
+          int e = 7;
+#pragma unroll
+          for (int q = 7; q >= 0; --q) e = (want_nan ? k[q] != k[q] : k[q] == m) ? q : e;
+          best = m;
+          besti = j * kVec + e;
+        }
+      };
+      int j = j0 + threadIdx.x;
+      for (; j + kSampThreads < j1; j += 2 * kSampThreads) {
+        const uint4 r0 = __ldcs(rowv + j), r1 = __ldcs(rowv + j + kSampThreads);
+        consider(r0, j);
+        consider(r1, j + kSampThreads);
+      }
+      if (j < j1) consider(__ldcs(rowv + j), j);
+      if (tail) {  // the row's ragged tail
+        for (int t = nv * kVec + threadIdx.x; t < p.V; t += kSampThreads) {
+          const U4 r = lk::philox4x32_10(
+              U4{static_cast<uint32_t>(t >> 2), static_cast<uint32_t>(b), p.off_lo, p.off_hi},
+              p.key);
+          const uint32_t w = (t & 3) == 0 ? r.x : (t & 3) == 1 ? r.y : (t & 3) == 2 ? r.z : r.w;
+          const float g = lk::gumbel_from_bits(w);
+          if (drow) drow[t] = g;
+          const float key = __fadd_rn(__fdiv_rn(lk::Elem<T>::to_f(row[t]), temp), g);
+          if (beats_later(key, best)) {
+            best = key;
+            besti = t;
+          }
+        }
+      }
+}
+
+// Grid (chunk, row): each CTA takes one chunk of a row's vectors (the last
+// chunk also the ragged tail). The compute-bound loop makes the SMs' speeds
+// differ by ~15 %, so many chunks of a few vectors per thread (several waves)
+// let the hardware's CTA dispatch balance them; a static cut of the batch
+// into one CTA per resident slot ran 20 % slower for that reason.
+template <typename T>
+__global__ void __launch_bounds__(kSampThreads, kGumbelCtasPerSm) gumbel_kernel(const SampleParams p) {
+  lk::pdl_wait();  // launched to overlap the kernel ahead of it: wait for it before reading
+  const int ch = blockIdx.x, b = blockIdx.y;
+  const float temp = p.temps[b];
+  const int cv = p.chunk / kVec;  // vectors per chunk
+  const int j0 = ch * cv, j1 = min(p.nv, j0 + cv);
+  const bool tail = ch == p.nchunks - 1;
+  float best = -INFINITY;
+  int besti = 0x7fffffff;
+  if (temp > 0.f) {
+    gumbel_segment<T>(p, b, j0, j1, tail, temp, best, besti);
+  } else {  // a greedy row inside a sampled batch
+    scan_chunk<T, true, 0>(p, b, j0 * kVec, tail ? p.V : j1 * kVec, temp, best, besti);
+  }
+  finish_row(p, b, ch, best, besti);
+}
+
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 // Workspace layout: [counters: 65536 int32 — a fixed region, so that calls
@@ -673,6 +813,17 @@ int choose_chunks(int B, int V) {
   if (n > 1024) n = 1024;
   return static_cast<int>(n);
 }
+
+// LITEKERN_GUMBEL_GENERIC=1 (read once) sends in-kernel-noise rows to the
+// general sample_kernel instead of gumbel_kernel (the earlier path).
+bool gumbel_generic() {
+  static bool g = [] {
+    const char* e = getenv("LITEKERN_GUMBEL_GENERIC");
+    return e && atoi(e) != 0;
+  }();
+  return g;
+}
+
 
 constexpr int kMaxCluster = 8;  // portable cluster size
 
@@ -743,80 +894,171 @@ int launch_sample(const SampleParams& p, int B, bool vec, cudaStream_t s) {
       return lk::check_launch();
     }
   }
+  if constexpr (!std::is_same<T, float>::value) {
+    if (p.gumbel) {
+      const cudaError_t e =
+          lk::launch_after_previous(gumbel_kernel<T>, grid, dim3(kSampThreads), 0, s, p);
+      return e == cudaSuccess ? LK_OK : LK_ERR_CUDA;
+    }
+  }
   const cudaError_t e =
       vec ? lk::launch_after_previous(sample_kernel<T, true>, grid, dim3(kSampThreads), 0, s, p)
           : lk::launch_after_previous(sample_kernel<T, false>, grid, dim3(kSampThreads), 0, s, p);
   return e == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 
-}  // namespace
-
-extern "C" size_t lk_sample_workspace_bytes(int32_t B, int32_t V) {
-  if (B <= 0 || V <= 0) return 0;
-  const int n = choose_chunks(B, V);
-  return kCounterBytes + 2 * align256(static_cast<size_t>(B) * n * 4);
+// gumbel_kernel's chunk: vectors per thread per CTA (LITEKERN_GUMBEL_VPT,
+// read once; default 4), so chunks of 8 * 256 * vpt elements.
+int gumbel_vpt() {
+  static int v = [] {
+    const char* e = getenv("LITEKERN_GUMBEL_VPT");
+    const int x = e ? atoi(e) : 4;
+    return x >= 1 && x <= 64 ? x : 4;
+  }();
+  return v;
+}
+bool use_gumbel(int V, bool vec, bool rng) { return rng && vec && V >= kVec && !gumbel_generic(); }
+int gumbel_chunks(int V) {
+  const int cv = gumbel_vpt() * kSampThreads;
+  return std::max(1, (V / kVec + cv - 1) / cv);
 }
 
-extern "C" int lk_sample(int64_t* out_ids, const void* logits, int32_t B, int32_t V, int64_t ld,
-                         const float* temperatures, const float* noise, int64_t noise_ld,
-                         uint64_t seed, uint64_t offset, float* noise_dump, void* workspace,
-                         size_t workspace_bytes, int32_t dtype, void* stream) {
+// Chunks (CTAs) per row for one call: all-greedy 16-bit rows reduce their
+// chunks inside one cluster (at most kMaxCluster); in-kernel-noise 16-bit
+// rows take gumbel_kernel's chunks; everything else one wave.
+int chunks_for(int B, int V, bool vec, bool greedy_only, bool rng) {
+  if (greedy_only && vec && sample_unroll() != 0) {
+    const int n = choose_chunks(B, V);
+    return chunk_override() == 0 && n > kMaxCluster ? kMaxCluster : n;
+  }
+  if (use_gumbel(V, vec, rng)) return gumbel_chunks(V);
+  return choose_chunks(B, V);
+}
+
+// Validates the arguments and fills everything but the scratch pointers;
+// returns LK_OK or an error code. Shared by lk_sample and lk_sample_noalloc.
+int prepare(SampleParams& p, bool& vec, int64_t* out_ids, const void* logits, int32_t B,
+            int32_t V, int64_t ld, const float* temperatures, const float* noise,
+            int64_t noise_ld, uint64_t seed, uint64_t offset, float* noise_dump, int32_t dtype,
+            int64_t max_partials = INT64_MAX) {
   if (B < 0 || V <= 0 || ld < V) return LK_ERR_INVALID_ARG;
   if (B == 0) return LK_OK;
   if (!out_ids || !logits || B > 65535) return LK_ERR_INVALID_ARG;
   if (noise && noise_ld < V) return LK_ERR_INVALID_ARG;
   if (dtype != LK_DTYPE_F32 && dtype != LK_DTYPE_F16 && dtype != LK_DTYPE_BF16)
     return LK_ERR_UNSUPPORTED;
-  SampleParams p;
+  const int esz = lk::dtype_size(dtype);
+  vec = dtype != LK_DTYPE_F32 &&
+        (reinterpret_cast<uintptr_t>(logits) & 15u) == 0 && ((ld * esz) & 15) == 0 &&
+        (!noise || (((reinterpret_cast<uintptr_t>(noise) & 15u) == 0) &&
+                    ((noise_ld * 4) & 15) == 0)) &&
+        (!noise_dump || ((reinterpret_cast<uintptr_t>(noise_dump) & 15u) == 0 &&
+                         ((static_cast<int64_t>(V) * 4) & 15) == 0));
   p.logits = logits;
   p.ld = ld;
   p.V = V;
-  p.nchunks = choose_chunks(B, V);
-  // All-greedy 16-bit rows reduce their chunks inside one cluster: at most
-  // kMaxCluster chunks per row.
-  if (temperatures == nullptr && dtype != LK_DTYPE_F32 && sample_unroll() != 0 &&
-      chunk_override() == 0 && p.nchunks > kMaxCluster)
-    p.nchunks = kMaxCluster;
-  const int64_t per = (static_cast<int64_t>(V) + p.nchunks - 1) / p.nchunks;
-  p.chunk = static_cast<int>(((per + kVec - 1) / kVec) * kVec);
-  p.nchunks = static_cast<int>((V + static_cast<int64_t>(p.chunk) - 1) / p.chunk);
+  p.nchunks = chunks_for(B, V, vec, temperatures == nullptr,
+                         temperatures != nullptr && noise == nullptr);
+  if (use_gumbel(V, vec, temperatures != nullptr && noise == nullptr)) {
+    // whole vectors per chunk; the ragged tail joins the last chunk
+    int64_t cv = static_cast<int64_t>(gumbel_vpt()) * kSampThreads;
+    const int64_t nvr = V / kVec;
+    const int64_t nmax = std::max<int64_t>(1, max_partials / B);
+    if ((nvr + cv - 1) / cv > nmax) cv = (nvr + nmax - 1) / nmax;  // fewer, longer chunks
+    p.chunk = static_cast<int>(cv * kVec);
+    p.nchunks = static_cast<int>((nvr + cv - 1) / cv);
+    p.gumbel = 1;
+  } else {
+    const int64_t per = (static_cast<int64_t>(V) + p.nchunks - 1) / p.nchunks;
+    p.chunk = static_cast<int>(((per + kVec - 1) / kVec) * kVec);
+    p.nchunks = static_cast<int>((V + static_cast<int64_t>(p.chunk) - 1) / p.chunk);
+    p.gumbel = 0;
+  }
+  p.nv = V / kVec;
   p.temps = temperatures;
   p.noise = noise;
   p.noise_ld = noise_ld;
-  p.seed_lo = static_cast<uint32_t>(seed);
-  p.seed_hi = static_cast<uint32_t>(seed >> 32);
+  p.key = lk::philox_key(seed);
   p.off_lo = static_cast<uint32_t>(offset);
   p.off_hi = static_cast<uint32_t>(offset >> 32);
   p.noise_dump = noise_dump;
   p.out = out_ids;
-  if (p.nchunks > 1) {
-    const size_t need = lk_sample_workspace_bytes(B, V);
-    if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
-      return LK_ERR_WORKSPACE;
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
-    p.counters = reinterpret_cast<int32_t*>(ws);
-    const size_t cb = kCounterBytes;
-    const size_t kb = align256(static_cast<size_t>(B) * choose_chunks(B, V) * 4);
-    p.part_key = reinterpret_cast<float*>(ws + cb);
-    p.part_idx = reinterpret_cast<int32_t*>(ws + cb + kb);
-  } else {
-    p.counters = nullptr;
-    p.part_key = nullptr;
-    p.part_idx = nullptr;
-  }
-  const int esz = lk::dtype_size(dtype);
-  const bool vec = dtype != LK_DTYPE_F32 &&
-                   (reinterpret_cast<uintptr_t>(logits) & 15u) == 0 && ((ld * esz) & 15) == 0 &&
-                   (!noise || (((reinterpret_cast<uintptr_t>(noise) & 15u) == 0) &&
-                               ((noise_ld * 4) & 15) == 0)) &&
-                   (!noise_dump || ((reinterpret_cast<uintptr_t>(noise_dump) & 15u) == 0 &&
-                                    ((static_cast<int64_t>(V) * 4) & 15) == 0));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  p.counters = nullptr;
+  p.part_key = nullptr;
+  p.part_idx = nullptr;
+  return LK_OK;
+}
+
+int launch(const SampleParams& p, int B, bool vec, int32_t dtype, cudaStream_t s) {
   switch (dtype) {
     case LK_DTYPE_BF16: return launch_sample<__nv_bfloat16>(p, B, vec, s);
     case LK_DTYPE_F16: return launch_sample<__half>(p, B, vec, s);
     default: return launch_sample<float>(p, B, false, s);
   }
+}
+
+// Largest chunk count any call shape (B, V) can take: the workspace covers it.
+int max_chunks(int B, int V) { return std::max(choose_chunks(B, V), gumbel_chunks(V)); }
+
+}  // namespace
+
+extern "C" size_t lk_sample_workspace_bytes(int32_t B, int32_t V) {
+  if (B <= 0 || V <= 0) return 0;
+  return kCounterBytes + 2 * align256(static_cast<size_t>(B) * max_chunks(B, V) * 4);
+}
+
+extern "C" int lk_sample(int64_t* out_ids, const void* logits, int32_t B, int32_t V, int64_t ld,
+                         const float* temperatures, const float* noise, int64_t noise_ld,
+                         uint64_t seed, uint64_t offset, float* noise_dump, void* workspace,
+                         size_t workspace_bytes, int32_t dtype, void* stream) {
+  SampleParams p;
+  bool vec = false;
+  const int rc = prepare(p, vec, out_ids, logits, B, V, ld, temperatures, noise, noise_ld, seed,
+                         offset, noise_dump, dtype);
+  if (rc != LK_OK || B == 0) return rc;
+  if (p.nchunks > 1) {
+    const size_t need = lk_sample_workspace_bytes(B, V);
+    if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+      return LK_ERR_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const size_t kb = align256(static_cast<size_t>(B) * max_chunks(B, V) * 4);
+    p.counters = reinterpret_cast<int32_t*>(ws);
+    p.part_key = reinterpret_cast<float*>(ws + kCounterBytes);
+    p.part_idx = reinterpret_cast<int32_t*>(ws + kCounterBytes + kb);
+  }
+  return launch(p, B, vec, dtype, static_cast<cudaStream_t>(stream));
+}
+
+// ------------------------------------------------------------ self-tests ---
+namespace {
+
+__global__ void selftest_div_kernel(float* out, const float* x, int n, const float* temps, int nt) {
+  const int j = blockIdx.y;
+  const FastDiv dv = FastDiv::make(temps[j]);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    out[static_cast<int64_t>(j) * n + i] = dv.in_range(x[i]) ? dv.fast(x[i]) : __fdiv_rn(x[i], dv.t);
+}
+
+__global__ void selftest_gumbel_kernel(float* out, const uint32_t* bits, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    out[i] = lk::gumbel_from_bits(bits[i]);
+}
+
+}  // namespace
+
+extern "C" int lk_selftest_sampler_div(float* out, const float* x, int32_t n, const float* temps,
+                                       int32_t nt, void* stream) {
+  if (!out || !x || !temps || n <= 0 || nt <= 0 || nt > 65535) return LK_ERR_INVALID_ARG;
+  selftest_div_kernel<<<dim3(64, nt), 256, 0, static_cast<cudaStream_t>(stream)>>>(out, x, n,
+                                                                                  temps, nt);
+  return lk::check_launch();
+}
+
+extern "C" int lk_selftest_gumbel(float* out, const uint32_t* bits, int32_t n, void* stream) {
+  if (!out || !bits || n <= 0) return LK_ERR_INVALID_ARG;
+  selftest_gumbel_kernel<<<4 * lk::num_sms(), 256, 0, static_cast<cudaStream_t>(stream)>>>(out, bits,
+                                                                                          n);
+  return lk::check_launch();
 }
 
 extern "C" int lk_softmax_temp(float* probs, int64_t probs_ld, const void* logits, int32_t B,
@@ -882,36 +1124,13 @@ extern "C" int lk_sample_noalloc(int64_t* out_ids, const void* logits, int32_t B
                                  int64_t ld, const float* temperatures, const float* noise,
                                  int64_t noise_ld, uint64_t seed, uint64_t offset,
                                  float* noise_dump, int32_t dtype, void* stream) {
-  if (B < 0 || V <= 0 || ld < V) return LK_ERR_INVALID_ARG;
-  if (B == 0) return LK_OK;
-  if (!out_ids || !logits || B > 65535) return LK_ERR_INVALID_ARG;
-  if (noise && noise_ld < V) return LK_ERR_INVALID_ARG;
-  if (dtype != LK_DTYPE_F32 && dtype != LK_DTYPE_F16 && dtype != LK_DTYPE_BF16)
-    return LK_ERR_UNSUPPORTED;
   SampleParams p;
-  p.logits = logits;
-  p.ld = ld;
-  p.V = V;
-  p.nchunks = choose_chunks(B, V);
-  // All-greedy 16-bit rows reduce their chunks inside one cluster: at most
-  // kMaxCluster chunks per row.
-  if (temperatures == nullptr && dtype != LK_DTYPE_F32 && sample_unroll() != 0 &&
-      chunk_override() == 0 && p.nchunks > kMaxCluster)
-    p.nchunks = kMaxCluster;
-  const int64_t per = (static_cast<int64_t>(V) + p.nchunks - 1) / p.nchunks;
-  p.chunk = static_cast<int>(((per + kVec - 1) / kVec) * kVec);
-  p.nchunks = static_cast<int>((V + static_cast<int64_t>(p.chunk) - 1) / p.chunk);
+  bool vec = false;
+  const int rc0 = prepare(p, vec, out_ids, logits, B, V, ld, temperatures, noise, noise_ld, seed,
+                          offset, noise_dump, dtype, kNoAllocMaxPartials);
+  if (rc0 != LK_OK || B == 0) return rc0;
   if (B > kNoAllocMaxRows || static_cast<int64_t>(B) * p.nchunks > kNoAllocMaxPartials)
     return LK_ERR_TOO_LARGE;
-  p.temps = temperatures;
-  p.noise = noise;
-  p.noise_ld = noise_ld;
-  p.seed_lo = static_cast<uint32_t>(seed);
-  p.seed_hi = static_cast<uint32_t>(seed >> 32);
-  p.off_lo = static_cast<uint32_t>(offset);
-  p.off_hi = static_cast<uint32_t>(offset >> 32);
-  p.noise_dump = noise_dump;
-  p.out = out_ids;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (p.nchunks > 1) {
     void* base = nullptr;
@@ -924,21 +1143,6 @@ extern "C" int lk_sample_noalloc(int64_t* out_ids, const void* logits, int32_t B
     // The counters must start at zero; clear the rows this call uses.
     if (cudaMemsetAsync(p.counters, 0, static_cast<size_t>(B) * 4, s) != cudaSuccess)
       return LK_ERR_CUDA;
-  } else {
-    p.counters = nullptr;
-    p.part_key = nullptr;
-    p.part_idx = nullptr;
   }
-  const int esz = lk::dtype_size(dtype);
-  const bool vec = dtype != LK_DTYPE_F32 &&
-                   (reinterpret_cast<uintptr_t>(logits) & 15u) == 0 && ((ld * esz) & 15) == 0 &&
-                   (!noise || (((reinterpret_cast<uintptr_t>(noise) & 15u) == 0) &&
-                               ((noise_ld * 4) & 15) == 0)) &&
-                   (!noise_dump || ((reinterpret_cast<uintptr_t>(noise_dump) & 15u) == 0 &&
-                                    ((static_cast<int64_t>(V) * 4) & 15) == 0));
-  switch (dtype) {
-    case LK_DTYPE_BF16: return launch_sample<__nv_bfloat16>(p, B, vec, s);
-    case LK_DTYPE_F16: return launch_sample<__half>(p, B, vec, s);
-    default: return launch_sample<float>(p, B, false, s);
-  }
+  return launch(p, B, vec, dtype, s);
 }

@@ -213,3 +213,91 @@ def test_sampler_kernel_options(variant):
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     assert "ok" in r.stdout
+
+
+def _all_16bit_values():
+    """Every finite and non-finite bf16 and fp16 value, as fp32 (NaNs dropped)."""
+    bits = torch.arange(65536, dtype=torch.int32).to(torch.int16)
+    v = torch.cat([bits.view(torch.bfloat16).float(), bits.view(torch.float16).float()])
+    return v[~torch.isnan(v)]
+
+
+def test_sampler_division_is_ieee_for_every_16bit_value(cuda):
+    """The in-kernel-noise kernel's x / T (Markstein's correction, IEEE division
+    outside its range) equals IEEE fp32 division for every 16-bit logit and a
+    spread of temperatures, including ones that force the fallback."""
+    x = _all_16bit_values()
+    gen = torch.Generator().manual_seed(3)
+    temps = torch.cat([
+        torch.tensor([0.7, 1.0, 1.3, 0.1, 2.0, 1e-3, 37.5, 3e-5, 1e5, 1e-30, 1e30, 0.5, 0.999999,
+                      1.0000001, 2.0 ** -60, 2.0 ** 60, 2.0 ** -61, 2.0 ** 61]),
+        torch.rand(96, generator=gen) * 2 + 0.01,
+        torch.exp(torch.randn(32, generator=gen) * 6),
+    ]).float()
+    out = torch.empty((temps.numel(), x.numel()), device=cuda)
+    from litevllm_b200 import _lib
+    xd, td = x.to(cuda), temps.to(cuda)
+    _lib.check(_lib.lib().lk_selftest_sampler_div(out.data_ptr(), xd.data_ptr(), x.numel(),
+                                                   td.data_ptr(), temps.numel(), None))
+    want = (x.numpy()[None, :] / temps.numpy()[:, None]).astype(np.float32)
+    got = out.cpu().numpy()
+    both_nan = np.isnan(got) & np.isnan(want)
+    bad = (got.view(np.int32) != want.view(np.int32)) & ~both_nan
+    assert not bad.any(), (np.argwhere(bad)[:5], got[bad][:5], want[bad][:5])
+
+
+def test_gumbel_map_every_uniform(cuda):
+    """The noise map over all 2^23 uniforms the kernel can draw (random low
+    bits below them) is -ln(-ln u) to 1e-6 relative (2e-6 absolute)."""
+    k = np.arange(2 ** 23, dtype=np.uint64)
+    low = np.random.default_rng(1).integers(0, 512, size=k.size, dtype=np.uint64)
+    bits = ((k << np.uint64(9)) | low).astype(np.uint32)
+    out = torch.empty(bits.size, device=cuda)
+    from litevllm_b200 import _lib
+    bd = torch.from_numpy(bits.view(np.int32)).to(cuda)
+    _lib.check(_lib.lib().lk_selftest_gumbel(out.data_ptr(), bd.data_ptr(), bits.size, None))
+    u = (k.astype(np.float64) + 0.5) * 2.0 ** -23
+    want = -np.log(-np.log(u))
+    got = out.cpu().numpy().astype(np.float64)
+    err = np.abs(got - want)
+    assert (err <= 2e-6 + 1e-6 * np.abs(want)).all(), (err.max(), int(err.argmax()))
+    # the oracle's fp32 map agrees within the noise-dump tolerance
+    g32 = osamp.gumbel_from_u(osamp.uniform_bits_to_u(bits[:: 97]))
+    np.testing.assert_allclose(out.cpu().numpy()[:: 97], g32, rtol=2e-6, atol=2e-6)
+
+
+@pytest.mark.parametrize("B,V,dtype", [(128, 151936, torch.bfloat16), (64, 151936, torch.bfloat16),
+                                       (5, 32003, torch.float16), (300, 4096, torch.bfloat16)])
+def test_in_kernel_noise_configs_bit_exact_given_dump(cuda, B, V, dtype):
+    """Config 4 / 5 shapes (and a ragged V, fp16, many rows) through the
+    in-kernel-noise kernel: ids equal the oracle's given the dumped noise."""
+    x = workloads.make_logits(4, B, V, seed=B, dtype=dtype, device=cuda)
+    t = (torch.rand(B, generator=torch.Generator().manual_seed(B)) * 1.5 + 0.2).to(cuda)
+    t[::7] = 0.0  # greedy rows inside a sampled batch
+    dump = torch.zeros((B, V), device=cuda)
+    ids = ops.sample(x, t, seed=99, offset=B, noise_dump=dump).cpu().numpy()
+    want = osamp.gumbel(x.float().cpu().numpy(), t.cpu().numpy(), dump.cpu().numpy())
+    assert np.array_equal(ids, want)
+
+
+def test_in_kernel_noise_edge_values(cuda):
+    """-inf masks, +inf, NaN, zeros, subnormals and extreme temperatures in the
+    in-kernel-noise kernel: the same ids as the oracle given the dumped noise."""
+    B, V = 12, 20000
+    gen = torch.Generator().manual_seed(12)
+    x = torch.randn((B, V), generator=gen)
+    x[0, ::2] = float("-inf")                     # masked vocabulary
+    x[1, :] = float("-inf")                       # fully masked row -> index 0
+    x[2, 777] = float("inf")
+    x[3, 1234] = float("nan")
+    x[4, :] = 0.0
+    x[5, ::3] = -0.0
+    x[6, :100] = 1e-39                            # bf16 subnormals
+    x[7, 5] = 3.0e38
+    x = x.bfloat16()
+    t = torch.tensor([0.7, 1.0, 0.9, 1.2, 1.0, 0.5, 1e-30, 0.25, 1e30, 3e-5, 1e5, 0.0])
+    dump = torch.zeros((B, V), device=cuda)
+    ids = ops.sample(x.to(cuda), t.to(cuda), seed=5, offset=6, noise_dump=dump).cpu().numpy()
+    want = osamp.gumbel(x.float().numpy(), t.numpy(), dump.cpu().numpy())
+    assert np.array_equal(ids, want), (ids, want)
+    assert ids[1] == 0 and ids[2] == 777 and ids[3] == 1234
