@@ -10,6 +10,13 @@ r*B .. r*B+B-1, its own KV pool and inputs; no collective touches the data
 path (weak scaling). torch.distributed is used only for the start/stop
 barrier and the max-over-ranks time. Rank 0 prints one JSON line.
 
+The same line carries sub-records ("sub") for every target the configurations
+name, each device-timed with CUDA events over --steps after --warmup, max over
+ranks: the sampler alone (greedy [256, 128256]; in-kernel-noise Gumbel-max
+[128, 151936] at T = 0.7), config 5 (64 long-context sequences split over the
+ranks: strong scaling), config 3 (chunked prefill on prior context + 252
+decodes) and config 4 (prefix-shared decode). --no-sub skips them.
+
 --impl reference times the reference algorithm on the host CPU (the CPU
 restatement of litevllm's Attention.forward store + _decode_fast and the greedy
 Sampler, run with every host thread) on a bounded sample of the same workload.
@@ -49,6 +56,8 @@ def parse():
     ap.add_argument("--num-splits", type=int, default=0, help="decode split-KV override (0=auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="skip the sub-records (sampler, cfg5, cfg3, cfg4) of the default line")
     ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4", "cfg5"],
                     help="cfg2 (default) is the contract's workload; cfg3 / cfg5 print a "
                          "secondary line for the mixed prefill step / long-context decode")
@@ -239,8 +248,10 @@ def run_ours(args, ws, rank, local):
     torch.cuda.synchronize(dev)
     with ClockSampler(local) as clk:
         t0.record(stream)
+        h0 = time.perf_counter()
         for i in range(K):
             step(i, dec_ev[i])
+        host_us = (time.perf_counter() - h0) / K * 1e6  # host time to enqueue one step
         t1.record(stream)
         torch.cuda.synchronize(dev)
     if ws > 1:
@@ -326,17 +337,47 @@ def run_ours(args, ws, rank, local):
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             e2e_ms = float(t.item())
         h2d = sum(x.numel() * x.element_size() for x in (h_q, h_k, h_v, h_slot, h_bt, h_ctx, h_logits[0]))
-        e2e = dict(ms=e2e_ms, h2d=h2d, d2h=B * 8,
+        # the host link on its own: the same pinned copies, every rank at once
+        if ws > 1:
+            torch.distributed.barrier()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(cstream):
+            torch.cuda.synchronize(dev)
+            c0.record(cstream)
+            for _ in range(5):
+                for n, t_ in host_in[0].items():
+                    bufs[0][n].copy_(t_, non_blocking=True)
+            c1.record(cstream)
+        torch.cuda.synchronize(dev)
+        h2d_ms = c0.elapsed_time(c1) / 5
+        if ws > 1:
+            t = torch.tensor([h2d_ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            h2d_ms = float(t.item())
+        h2d_gbs = h2d / (h2d_ms * 1e-3) / 1e9
+        e2e = dict(ms=e2e_ms, h2d=h2d, d2h=B * 8, h2d_gbs=h2d_gbs,
                    host=("pinned buffers on the GPU's NUMA node (NVML CPU affinity, "
                          f"{len(near)} CPUs)") if near else "pinned buffers (process CPU affinity unchanged)")
         os.sched_setaffinity(0, prev_cpus)
 
+    mine_t = torch.tensor([ms, dec_ms, host_us], device=dev, dtype=torch.float64)
     if ws > 1:
-        t = torch.tensor([ms, dec_ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, dec_ms = float(t[0]), float(t[1])
+        allt = [torch.empty_like(mine_t) for _ in range(ws)]
+        torch.distributed.all_gather(allt, mine_t)
+        allt = torch.stack(allt).cpu()
+    else:
+        allt = mine_t.cpu()[None]
+    ms, dec_ms = float(allt[:, 0].max()), float(allt[:, 1].max())
+
+    def spread(col):
+        v = sorted(float(x) for x in allt[:, col])
+        return {"min": round(v[0], 4), "median": round(statistics.median(v), 4),
+                "max": round(v[-1], 4)}
+
+    per_rank = {"ms_per_step": spread(0), "decode_ms": spread(1),
+                "host_enqueue_us_per_step": spread(2)}
     return dict(ms=ms, dec_ms=dec_ms, ctx=batch.ctx, B=B, e2e=e2e, clocks=clk.summary(),
-                nsplit=nsplit, K=K)
+                nsplit=nsplit, K=K, per_rank=per_rank)
 
 
 # -------------------------------------------------------- CPU (reference) arm ---
@@ -450,15 +491,18 @@ def _time_events(stream, fn, K, warmup):
     return t0.elapsed_time(t1) / K, evs
 
 
-def run_secondary(args, ws, rank, local):
-    """Config 3 (mixed chunked-prefill + decode step) or config 5 (long-context
-    decode + T=1.0 sampler), device-timed per kernel. One JSON line on rank 0."""
+def measure_sub(workload, steps, warmup, ws, rank, local):
+    """Secondary workloads, device-timed per kernel with CUDA events, max over
+    ranks: "cfg3" (mixed chunked-prefill + decode step), "cfg4" (prefix-shared
+    decode + T=0.7 sampler), "cfg5" (long-context decode + T=1.0 sampler,
+    64 sequences split over the ranks: strong scaling). Returns the record."""
     from litevllm_b200 import ops, workloads
     from litevllm_b200.sharding import shard
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     stream = torch.cuda.current_stream(dev)
+    args = argparse.Namespace(workload=workload, steps=steps, warmup=warmup)
     peak_hbm, _ = measured_peak()
     peak_tf, tf_kind = measured_tflops()
     Ev = lambda: torch.cuda.Event(enable_timing=True)
@@ -536,35 +580,50 @@ def run_secondary(args, ws, rank, local):
 
         def step(st, i=[0]):
             i[0] += 1
-            e = (Ev(), Ev()) if st is not None else None
+            e = (Ev(), Ev(), Ev()) if st is not None else None
             ops.store_kvcache(b.key, b.value, b.key_cache, b.value_cache, b.slot_mapping)
             if e: e[0].record(st)
             ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables, b.context_lens,
                              b.scale, num_splits=nsplit, out=out)
             if e: e[1].record(st)
             ops.sample(logits, temps, seed=7, offset=i[0], out=ids)
+            if e: e[2].record(st)
             return e
 
         ms, evs = _time_events(stream, step, args.steps, max(3, args.warmup))
-        dec_ms = sum(a.elapsed_time(c) for a, c in evs) / len(evs)
-        t = torch.tensor([ms, dec_ms], device=dev)
+        dec_ms = sum(a.elapsed_time(c) for a, c, _ in evs) / len(evs)
+        smp_ms = sum(c.elapsed_time(d) for _, c, d in evs) / len(evs)
+        dec_b = decode_bytes(b.ctx, B)
+        smp_b = B * V5 * 2 + B * 8
+        step_b = dec_b + store_bytes(B) + smp_b
+        # per rank: time maxima; bytes summed (ranks hold different contexts)
+        t = torch.tensor([ms, dec_ms, smp_ms], device=dev, dtype=torch.float64)
+        nb = torch.tensor([step_b, dec_b], device=dev, dtype=torch.float64)
         if ws > 1:
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, dec_ms = float(t[0]), float(t[1])
-        dec_b = decode_bytes(b.ctx, B)
-        step_b = dec_b + store_bytes(B) + B * V5 * 2
+            torch.distributed.all_reduce(nb, op=torch.distributed.ReduceOp.SUM)
+        ms, dec_ms, smp_ms = (float(x) for x in t)
+        job_b, job_dec_b = (float(x) for x in nb)
+        dec_gbs = dec_b / (dec_ms * 1e-3) / 1e9  # this rank's bytes over the slowest rank's time
         line = {"workload": "cfg5", "metric": METRIC, "n_gpus": ws, "steps": args.steps,
                 "config": {"workload": "config 5: bf16 long-context decode, 64 sequences in total "
                            f"({B} per GPU), context U[32768,131072], 32 Q / 8 KV heads, D=128, "
                            "block 16, split-KV, + T=1.0 Gumbel-max sampler (in-kernel Philox) "
-                           "over 151936", "parallelism": f"request-sharded x{ws}"},
-                "value": round(step_b * ws / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-                "ms_per_step": round(ms, 4), "sampled_tok_s": round(B * ws / (ms * 1e-3), 1),
+                           "over 151936", "parallelism": f"request-sharded x{ws}",
+                           "l2": f"inputs larger than L2: {job_dec_b / ws / 1e9:.1f} GB of KV per GPU"},
+                "scaling": "strong",
+                "value": round(job_b / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "ms_per_step": round(ms, 4), "sampled_tok_s": round(64 / (ms * 1e-3), 1),
                 "decode_split_kv": nsplit,
+                "decode": {"ms": round(dec_ms, 4),
+                           "job_gbs": round(job_dec_b / (dec_ms * 1e-3) / 1e9, 1)},
+                "sampler": {"kernel": "gumbel_kernel (in-kernel Philox, T=1.0)",
+                            "ms": round(smp_ms, 4), "rows": B, "vocab": V5,
+                            "gbs": round(smp_b / (smp_ms * 1e-3) / 1e9, 1)},
                 "roofline": {"kernel": "paged_decode_kernel", "bound": "hbm",
-                             "achieved": round(dec_b / (dec_ms * 1e-3) / 1e9, 1), "peak": peak_hbm,
-                             "unit": "GB/s",
-                             "frac": round(dec_b / (dec_ms * 1e-3) / 1e9 / peak_hbm, 4)}}
+                             "achieved": round(dec_gbs, 1), "peak": peak_hbm, "unit": "GB/s",
+                             "frac": round(dec_gbs / peak_hbm, 4),
+                             "algorithmic_bytes_per_launch": dec_b}}
     else:
         # config 3: 4 chunks of 512 on prior U[0,3584] + 252 decode sequences,
         # 2300 new tokens stored through slot_mapping, pool of 65536 blocks.
@@ -637,8 +696,48 @@ def run_secondary(args, ws, rank, local):
                                     "note": "store, then prefill and decode on two streams "
                                             "(Attention.forward_mixed); ms_per_step runs them "
                                             "one after the other to time each"}}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    return line
+
+
+def measure_sampler(steps, warmup, ws, local):
+    """The vocab-wide sampler on its own, both modes the configurations use:
+    greedy over [256, 128256] (config 2) and in-kernel-noise Gumbel-max at
+    T = 0.7 over [128, 151936] (config 4's shape). Each is timed as `steps`
+    back-to-back calls (CUDA events on the launching stream) rotating over four
+    logits buffers (263 / 156 MB, larger than L2), the way a serving step issues
+    it after the LM head; max over ranks."""
+    from litevllm_b200 import ops, workloads
+
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    peak, _ = measured_peak()
+    rec = {}
+    for name, B, V, T in (("greedy", 256, 128256, None), ("gumbel_rng", 128, 151936, 0.7)):
+        bufs = [workloads.make_logits(2 if T is None else 4, B, V, seed=s_, device=dev)
+                for s_ in range(4)]
+        temps = None if T is None else torch.full((B,), T, device=dev)
+        ids = torch.empty(B, dtype=torch.int64, device=dev)
+        k = [0]
+
+        def call(_st, k=k, bufs=bufs, temps=temps, ids=ids):
+            k[0] += 1
+            ops.sample(bufs[k[0] & 3], temps, seed=11, offset=k[0], out=ids)
+
+        ms, _ = _time_events(stream, call, steps, max(3, warmup))
+        t = torch.tensor([ms], device=dev)
+        if ws > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        us = float(t[0]) * 1e3
+        nbytes = B * V * 2 + B * 8
+        gbs = nbytes / (us * 1e-6) / 1e9
+        rec[name] = {"rows": B, "vocab": V, "temperature": T or 0.0, "us": round(us, 2),
+                     "algorithmic_bytes": nbytes, "gbs": round(gbs, 1),
+                     "frac_of_hbm_peak": round(gbs / peak, 4)}
+        del bufs
+    rec["gumbel_rng"]["bound"] = ("instruction issue: per element a quarter Philox4x32-10 "
+                                  "block, two hardware logarithms and the division")
+    rec["timing"] = "back-to-back calls over 4 rotating buffers > L2, CUDA events"
+    return rec
 
 
 def _decode_launches(num_splits: int) -> int:
@@ -660,7 +759,9 @@ def main():
         torch.cuda.set_device(local)
         torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local))
     if args.workload != "cfg2":
-        run_secondary(args, ws, rank, local)
+        rec = measure_sub(args.workload, args.steps, args.warmup, ws, rank, local)
+        if rank == 0:
+            print(json.dumps(rec), flush=True)
         if ws > 1:
             torch.distributed.barrier()
             torch.distributed.destroy_process_group()
@@ -701,12 +802,15 @@ def main():
             "unit": "GB/s",
             "frac": round(dec_gbs / peak, 4),
             "traffic": profiled_traffic(),
+            "traffic_source": "ncu dram bytes of one config-2 launch (profiles/paged_decode_cfg2.md), "
+                              "not measured in this run",
             "algorithmic_bytes_per_launch": dec_b,
         },
         # per layer: store, decode ordering + decode (one launch when the
         # ordering kernel is switched off or the persistent kernel runs); sampler
         "gpu_launches": r["K"] * ((1 + _decode_launches(r["nsplit"])) * args.layers + 1),
         "clocks": r["clocks"],
+        "per_rank": r["per_rank"],
     }
     if r["e2e"]:
         e = r["e2e"]
@@ -718,7 +822,22 @@ def main():
             "ms_per_step": round(e["ms"], 4),
             "sampled_tok_s": round(B * N / (e["ms"] * 1e-3), 1),
             "host": e["host"],
+            # the e2e step moves h2d_bytes_per_step over the host link: its own
+            # roofline is that copy alone, measured with every rank copying
+            "h2d_link_gbs_measured": round(e["h2d_gbs"], 1),
+            "frac_of_h2d_link": round(e["h2d"] / (e["ms"] * 1e-3) / 1e9 / e["h2d_gbs"], 4),
         }
+    if not args.no_sub:
+        # every north-star target measured in the same run, after the headline
+        torch.cuda.empty_cache()
+        sub = {"sampler": measure_sampler(args.steps, args.warmup, ws, local)}
+        for w in ("cfg5", "cfg3", "cfg4"):
+            torch.cuda.empty_cache()
+            rec = measure_sub(w, args.steps, args.warmup, ws, rank, local)
+            for k_ in ("metric", "n_gpus", "steps", "workload"):
+                rec.pop(k_, None)
+            sub[w] = rec
+        line["sub"] = sub
     if rank == 0 and N == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline()
         line["cpu_baseline"] = {"value": round(cb["gbs"], 3), "unit": "GB/s", "cores": cb["cores"],
