@@ -30,6 +30,7 @@ the fixtures do not depend on any random generator.
 
 from __future__ import annotations
 
+import os
 import sys
 from pathlib import Path
 
@@ -180,4 +181,7 @@ def penalty_fixture(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    # the reference checkout: argument, LITEVLLM_REFERENCE, else a "reference"
+    # directory beside this repository
+    main(sys.argv[1] if len(sys.argv) > 1 else
+         os.environ.get("LITEVLLM_REFERENCE") or str(HERE.parent.parent.parent / "reference"))

@@ -173,18 +173,20 @@ def test_repetition_penalty_rejects_bad_arguments():
     assert lib.lk_repetition_penalty(1, 2, 10, 10, 1, 4, 4, 1, None, 7, None) == -2
 
 
-def test_integration_stub_binds_against_the_library():
-    """The ctypes stub printed in INTEGRATION.md runs as written (prototypes
-    only; its functions need a GPU and are not called here)."""
-    doc = (Path(__file__).resolve().parent.parent / "INTEGRATION.md").read_text()
-    start = doc.index("```python\nimport ctypes, torch")
-    code = doc[start + len("```python\n"):doc.index("```", start + 10)]
-    code = code.replace('ctypes.CDLL("liblitekern.so")', f'ctypes.CDLL("{_lib.LIB_PATH}")')
-    ns: dict = {}
-    exec(compile(code, "INTEGRATION.md", "exec"), ns)
-    assert callable(ns["store_kvcache"]) and callable(ns["decode"])
-    assert ns["_lk"].lk_status_string(0) == b"ok"
-    assert ns["_lk"].lk_paged_decode_workspace_bytes(256, 32, 8, 128, 2) > 256 + 65536 * 4
+def test_integration_stub_binds_against_the_library(monkeypatch):
+    """The ctypes stub include/litekern_ctypes.py (quoted in the integration
+    notes) loads against the library as written (prototypes only; its
+    functions need a GPU and are not called here)."""
+    import importlib.util
+
+    monkeypatch.setenv("LITEKERN_LIB", str(_lib.LIB_PATH))
+    path = Path(__file__).resolve().parent.parent / "include" / "litekern_ctypes.py"
+    spec = importlib.util.spec_from_file_location("litekern_ctypes", path)
+    ns = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ns)
+    assert callable(ns.store_kvcache) and callable(ns.decode)
+    assert ns._lk.lk_status_string(0) == b"ok"
+    assert ns._lk.lk_paged_decode_workspace_bytes(256, 32, 8, 128, 2) > 256 + 65536 * 4
 
 
 def test_shared_prefix_decode_rejects_bad_arguments():

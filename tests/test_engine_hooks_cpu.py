@@ -3,6 +3,7 @@ prepare_inputs must build exactly the reference's tensors, and the batched
 process_outputs must leave sequences exactly as the reference's per-sequence
 loop does (greedy rows; the GPU sampler is replaced by argmax here)."""
 
+import os
 import sys
 import types
 from pathlib import Path
@@ -10,7 +11,10 @@ from pathlib import Path
 import pytest
 import torch
 
-REF = Path("/root/reference")
+# the reference checkout: LITEVLLM_REFERENCE, else a "reference" directory
+# beside this repository
+REF = Path(os.environ.get("LITEVLLM_REFERENCE")
+           or Path(__file__).resolve().parent.parent.parent / "reference")
 pytestmark = pytest.mark.skipif(not (REF / "litevllm").exists(),
                                 reason="reference checkout not present")
 

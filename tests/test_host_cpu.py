@@ -11,7 +11,10 @@ import torch.multiprocessing as mp
 
 from litevllm_b200 import sharding, workloads
 
-REF = Path("/root/reference")
+# the reference checkout: LITEVLLM_REFERENCE, else a "reference" directory
+# beside this repository
+REF = Path(os.environ.get("LITEVLLM_REFERENCE")
+           or Path(__file__).resolve().parent.parent.parent / "reference")
 
 
 def test_shards_partition_the_batch():
