@@ -704,8 +704,8 @@ def measure_sampler(steps, warmup, ws, local):
     greedy over [256, 128256] (config 2) and in-kernel-noise Gumbel-max at
     T = 0.7 over [128, 151936] (config 4's shape). Each is timed as `steps`
     back-to-back calls (CUDA events on the launching stream) rotating over four
-    logits buffers (263 / 156 MB, larger than L2), the way a serving step issues
-    it after the LM head; max over ranks."""
+    logits buffers (263 / 156 MB, larger than L2), replayed from a CUDA graph
+    the way a captured serving step issues them; max over ranks."""
     from litevllm_b200 import ops, workloads
 
     dev = torch.device("cuda", local)
@@ -717,13 +717,27 @@ def measure_sampler(steps, warmup, ws, local):
                 for s_ in range(4)]
         temps = None if T is None else torch.full((B,), T, device=dev)
         ids = torch.empty(B, dtype=torch.int64, device=dev)
-        k = [0]
-
-        def call(_st, k=k, bufs=bufs, temps=temps, ids=ids):
-            k[0] += 1
-            ops.sample(bufs[k[0] & 3], temps, seed=11, offset=k[0], out=ids)
-
-        ms, _ = _time_events(stream, call, steps, max(3, warmup))
+        # One call costs ~15 us of host time (argument checks, ctypes), longer
+        # than the kernel: timed call by call, the GPU would wait on the host.
+        # The calls are captured in a CUDA graph and the graph is replayed, so
+        # the events time the kernels back to back, as in a captured decode step.
+        for i in range(max(3, warmup)):
+            ops.sample(bufs[i & 3], temps, seed=11, offset=i, out=ids)
+        torch.cuda.synchronize(dev)
+        n = max(8, steps)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(n):
+                ops.sample(bufs[i & 3], temps, seed=11, offset=i, out=ids)
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / n
         t = torch.tensor([ms], device=dev)
         if ws > 1:
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -736,7 +750,8 @@ def measure_sampler(steps, warmup, ws, local):
         del bufs
     rec["gumbel_rng"]["bound"] = ("instruction issue: per element a quarter Philox4x32-10 "
                                   "block, two hardware logarithms and the division")
-    rec["timing"] = "back-to-back calls over 4 rotating buffers > L2, CUDA events"
+    rec["timing"] = ("`steps` calls captured in one CUDA graph over 4 rotating buffers > L2, "
+                     "replayed and timed with CUDA events")
     return rec
 
 

@@ -792,6 +792,16 @@ int ctas_per_sm() {
   }
 }
 
+// LITEKERN_SAMPLE_CLUSTER=0 (read once): all-greedy rows merge their chunks
+// through the workspace (last CTA of the row) instead of a cluster.
+bool sample_cluster() {
+  static bool c = [] {
+    const char* e = getenv("LITEKERN_SAMPLE_CLUSTER");
+    return !(e && atoi(e) == 0);
+  }();
+  return c;
+}
+
 int chunk_override() {
   static int c = [] {
     const char* e = getenv("LITEKERN_SAMPLE_CHUNKS");
@@ -837,7 +847,7 @@ int launch_sample(const SampleParams& p, int B, bool vec, cudaStream_t s) {
   dim3 grid(p.nchunks, B);
   if constexpr (!std::is_same<T, float>::value) {
     if (vec && p.temps == nullptr && sample_unroll() != 0) {
-      if (p.nchunks > 1 && p.nchunks <= kMaxCluster) {
+      if (p.nchunks > 1 && p.nchunks <= kMaxCluster && sample_cluster()) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = grid;
         cfg.blockDim = dim3(kSampThreads);
@@ -928,8 +938,18 @@ int gumbel_chunks(int V) {
 // rows take gumbel_kernel's chunks; everything else one wave.
 int chunks_for(int B, int V, bool vec, bool greedy_only, bool rng) {
   if (greedy_only && vec && sample_unroll() != 0) {
-    const int n = choose_chunks(B, V);
-    return chunk_override() == 0 && n > kMaxCluster ? kMaxCluster : n;
+    if (chunk_override() > 0) return chunk_override();
+    // Few, long chunks: just enough CTAs to give every SM one (ceil(SMs / B)
+    // per row). Each thread then keeps several batches of loads in flight
+    // over its chunk; measured from a CUDA graph at 256 x 128256, 1 chunk per
+    // row ran 12.7 us, 2 (a cluster pair) 13.7 us, 8 chunks 22.6 us (the
+    // per-CTA ramp and merge dominate short chunks); at 64 rows 3 chunks 7.4
+    // us, 1 chunk 9.3 us.
+    const int64_t maxn = std::max<int64_t>(1, (V + 2047) / 2048);
+    int64_t n = (lk::num_sms() + B - 1) / B;
+    n = std::min<int64_t>(n, maxn);
+    if (sample_cluster()) n = std::min<int64_t>(n, kMaxCluster);
+    return static_cast<int>(std::max<int64_t>(1, n));
   }
   if (use_gumbel(V, vec, rng)) return gumbel_chunks(V);
   return choose_chunks(B, V);
