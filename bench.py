@@ -5,8 +5,9 @@ shapes, 256 sequences per GPU, log-normal contexts, V = 128256).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...   (one process per GPU)
 
-Sequences are sharded by request: GPU r owns global sequences
-r*B .. r*B+B-1, its own KV pool and inputs; no collective touches the data
+Sequences are sharded by request: the N*B global sequences are dealt to the
+GPUs by context length (sharding.balanced_shard: B each, nearly equal total
+context); each GPU owns its KV pool and inputs; no collective touches the data
 path (weak scaling). torch.distributed is used only for the start/stop
 barrier and the max-over-ranks time. Rank 0 prints one JSON line.
 
@@ -125,6 +126,8 @@ class ClockSampler:
 
     def __init__(self, index: int):
         self.index = index
+        # poll period (BENCH_CLOCK_POLL_MS, default 0.5 ms; 0 disables polling)
+        self.period_s = float(os.environ.get("BENCH_CLOCK_POLL_MS", "0.5")) * 1e-3
         self.samples = []
         self.reasons = set()
         self.max_mhz = None
@@ -153,14 +156,14 @@ class ClockSampler:
                         self.reasons.add(name)
             except Exception:
                 pass
-            time.sleep(0.0005)
+            time.sleep(self.period_s)
 
     def __enter__(self):
         # The launching thread holds the GIL while it enqueues steps; with the
         # default 5 ms switch interval a region of a few ms yields one sample.
         # A short interval lets the poller run between launches.
         self._switch = sys.getswitchinterval()
-        if self.ok:
+        if self.ok and self.period_s > 0:
             sys.setswitchinterval(1e-4)
             self._t = threading.Thread(target=self._run, daemon=True)
             self._t.start()
@@ -205,12 +208,16 @@ def run_ours(args, ws, rank, local):
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    from litevllm_b200.sharding import shard
+    from litevllm_b200.sharding import balanced_shard
 
-    mine = shard(B_PER_GPU * ws, ws, rank)
+    # the global batch's sequences are dealt to the ranks by length (equal
+    # counts, nearly equal total context): the step is the slowest rank's
+    lens = [workloads.context_len(CFG, 0, i) for i in range(B_PER_GPU * ws)]
+    mine = balanced_shard(lens, ws, rank)
     B = len(mine)
-    first = mine.start
-    batch = workloads.make_decode_batch(CFG, B, seed=0, first_seq=first, device=dev)
+    first = rank * B_PER_GPU
+    batch = workloads.make_decode_batch(CFG, B, seed=0, first_seq=first,
+                                        ctx=[lens[i] for i in mine], device=dev)
     # L layers: separate KV pools per layer would multiply memory; the layers
     # share the block tables and read distinct pools (layer 0 reuses batch's).
     pools = [(batch.key_cache, batch.value_cache)]
@@ -376,8 +383,14 @@ def run_ours(args, ws, rank, local):
 
     per_rank = {"ms_per_step": spread(0), "decode_ms": spread(1),
                 "host_enqueue_us_per_step": spread(2)}
+    # the whole job's bytes: ranks hold different context mixes
+    step_b = args.layers * (decode_bytes(batch.ctx, B) + store_bytes(B)) + sampler_bytes(B)
+    jb = torch.tensor([float(step_b), float(B)], device=dev, dtype=torch.float64)
+    if ws > 1:
+        torch.distributed.all_reduce(jb, op=torch.distributed.ReduceOp.SUM)
     return dict(ms=ms, dec_ms=dec_ms, ctx=batch.ctx, B=B, e2e=e2e, clocks=clk.summary(),
-                nsplit=nsplit, K=K, per_rank=per_rank)
+                nsplit=nsplit, K=K, per_rank=per_rank, job_bytes=float(jb[0]),
+                job_seqs=int(jb[1]))
 
 
 # -------------------------------------------------------- CPU (reference) arm ---
@@ -425,7 +438,8 @@ def workload_config(N):
                     "tokens + decode (1 layer) + greedy sampler over [256, 128256] bf16",
         "global_batch": B_PER_GPU * N,
         "l2": "inputs larger than L2: KV pool ~1.2 GB per GPU, two rotating 66 MB logits buffers",
-        "parallelism": f"request-sharded x{N} (no collective on the data path)",
+        "parallelism": f"request-sharded x{N}: the {B_PER_GPU * N} sequences dealt to the GPUs "
+                       "by context length, equal counts (no collective on the data path)",
     }
 
 
@@ -497,7 +511,7 @@ def measure_sub(workload, steps, warmup, ws, rank, local):
     decode + T=0.7 sampler), "cfg5" (long-context decode + T=1.0 sampler,
     64 sequences split over the ranks: strong scaling). Returns the record."""
     from litevllm_b200 import ops, workloads
-    from litevllm_b200.sharding import shard
+    from litevllm_b200.sharding import balanced_shard
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -568,11 +582,14 @@ def measure_sub(workload, steps, warmup, ws, rank, local):
                                    "step_ms": round(ms_r, 4),
                                    "logical_gbs": round(logical / (dec_r * 1e-3) / 1e9, 1)}}
     elif args.workload == "cfg5":
-        mine = shard(64, ws, rank)
+        # 64 sequences dealt to the ranks by context length (equal counts)
+        lens = [workloads.context_len(5, 0, i) for i in range(64)]
+        mine = balanced_shard(lens, ws, rank)
         B = len(mine)
-        b = workloads.make_decode_batch(5, B, seed=0, first_seq=mine.start, device=dev)
+        b = workloads.make_decode_batch(5, B, seed=0, first_seq=rank * 64,
+                                        ctx=[lens[i] for i in mine], device=dev)
         V5 = 151936
-        logits = workloads.make_logits(5, B, V5, seed=0, first_seq=mine.start, device=dev)
+        logits = workloads.make_logits(5, B, V5, seed=0, first_seq=rank * 64, device=dev)
         temps = workloads.temperatures_for(5, B, device=dev)
         ids = torch.empty(B, dtype=torch.int64, device=dev)
         out = torch.empty_like(b.query)
@@ -597,14 +614,23 @@ def measure_sub(workload, steps, warmup, ws, rank, local):
         smp_b = B * V5 * 2 + B * 8
         step_b = dec_b + store_bytes(B) + smp_b
         # per rank: time maxima; bytes summed (ranks hold different contexts)
+        own_dec_ms = dec_ms
         t = torch.tensor([ms, dec_ms, smp_ms], device=dev, dtype=torch.float64)
         nb = torch.tensor([step_b, dec_b], device=dev, dtype=torch.float64)
         if ws > 1:
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             torch.distributed.all_reduce(nb, op=torch.distributed.ReduceOp.SUM)
+        own = torch.tensor([dec_b / (own_dec_ms * 1e-3) / 1e9], device=dev, dtype=torch.float64)
         ms, dec_ms, smp_ms = (float(x) for x in t)
         job_b, job_dec_b = (float(x) for x in nb)
-        dec_gbs = dec_b / (dec_ms * 1e-3) / 1e9  # this rank's bytes over the slowest rank's time
+        # per rank: its own decode bytes over its own decode time
+        if ws > 1:
+            allr = [torch.empty_like(own) for _ in range(ws)]
+            torch.distributed.all_gather(allr, own)
+            rates = sorted(float(x) for x in allr)
+        else:
+            rates = [float(own)]
+        dec_gbs = statistics.median(rates)
         line = {"workload": "cfg5", "metric": METRIC, "n_gpus": ws, "steps": args.steps,
                 "config": {"workload": "config 5: bf16 long-context decode, 64 sequences in total "
                            f"({B} per GPU), context U[32768,131072], 32 Q / 8 KV heads, D=128, "
@@ -623,6 +649,10 @@ def measure_sub(workload, steps, warmup, ws, rank, local):
                 "roofline": {"kernel": "paged_decode_kernel", "bound": "hbm",
                              "achieved": round(dec_gbs, 1), "peak": peak_hbm, "unit": "GB/s",
                              "frac": round(dec_gbs / peak_hbm, 4),
+                             "achieved_per_rank": {"min": round(rates[0], 1),
+                                                   "max": round(rates[-1], 1)},
+                             "note": "median over ranks of each rank's decode bytes / its "
+                                     "decode time",
                              "algorithmic_bytes_per_launch": dec_b}}
     else:
         # config 3: 4 chunks of 512 on prior U[0,3584] + 252 decode sequences,
@@ -785,10 +815,9 @@ def main():
     N = ws
     ms = r["ms"]
     B = r["B"]
-    step_bytes = args.layers * (decode_bytes(r["ctx"], B) + store_bytes(B)) + sampler_bytes(B)
-    # value: whole-job hot-path bytes per second; every rank moves its own step_bytes
-    # (per-rank context mixes differ slightly; rank 0's count stands for all)
-    value = step_bytes * N / (ms * 1e-3) / 1e9
+    # value: whole-job hot-path bytes (summed over ranks) per second of the slowest rank
+    job_bytes = r["job_bytes"]
+    value = job_bytes / (ms * 1e-3) / 1e9
     dec_b = decode_bytes(r["ctx"], B)
     dec_gbs = dec_b / (r["dec_ms"] * 1e-3) / 1e9
     peak, peak_kind = measured_peak()
@@ -806,7 +835,7 @@ def main():
         "dtype": "bf16",
         "data": "synthetic",
         "config": workload_config(N),
-        "sampled_tok_s": round(B * N / (ms * 1e-3), 1),
+        "sampled_tok_s": round(r["job_seqs"] / (ms * 1e-3), 1),
         "decode_split_kv": r["nsplit"],
         "roofline": {
             "kernel": "paged_decode_kernel",
@@ -830,12 +859,12 @@ def main():
     if r["e2e"]:
         e = r["e2e"]
         line["e2e"] = {
-            "value": round(step_bytes * N / (e["ms"] * 1e-3) / 1e9, 2),
+            "value": round(job_bytes / (e["ms"] * 1e-3) / 1e9, 2),
             "unit": "GB/s",
             "h2d_bytes_per_step": e["h2d"],
             "d2h_bytes_per_step": e["d2h"],
             "ms_per_step": round(e["ms"], 4),
-            "sampled_tok_s": round(B * N / (e["ms"] * 1e-3), 1),
+            "sampled_tok_s": round(r["job_seqs"] / (e["ms"] * 1e-3), 1),
             "host": e["host"],
             # the e2e step moves h2d_bytes_per_step over the host link: its own
             # roofline is that copy alone, measured with every rank copying

@@ -174,17 +174,23 @@ def paged_decode(
     if B == 0:
         return out
     max_blocks = block_tables.shape[1]
-    num_splits = int(num_splits)
-    if num_splits == 0:  # auto split count; -1 selects the persistent kernel
-        num_splits = decode_num_splits(B, H_kv, max_blocks, bs)
-    need = decode_workspace_bytes(B, H, H_kv, D, num_splits)
-    want = need
-    if not tuned_attention_shape(query.dtype, D, bs, H // H_kv):
-        # room for the generic kernel's split-KV partials (less only means fewer splits)
-        want = max(need, int(lib().lk_paged_attention_generic_workspace_bytes(
-            B, H, D, max_blocks, bs)))
+    plan_key = (B, H, H_kv, D, bs, max_blocks, query.dtype, int(num_splits))
+    plan = _DECODE_PLANS.get(plan_key)
+    if plan is None:
+        num_splits = int(num_splits)
+        if num_splits == 0:  # auto split count; -1 selects the persistent kernel
+            num_splits = decode_num_splits(B, H_kv, max_blocks, bs)
+        need = decode_workspace_bytes(B, H, H_kv, D, num_splits)
+        want = need
+        if not tuned_attention_shape(query.dtype, D, bs, H // H_kv):
+            # room for the generic kernel's split-KV partials (less only means fewer splits)
+            want = max(need, int(lib().lk_paged_attention_generic_workspace_bytes(
+                B, H, D, max_blocks, bs)))
+        plan = _DECODE_PLANS[plan_key] = (num_splits, need, want)
+    num_splits, need, want = plan
+    stream = _stream(dev)
     if workspace is None:
-        workspace = WORKSPACES.get(dev, f"decode:{_stream(dev)}", want)
+        workspace = WORKSPACES.get(dev, f"decode:{stream}", want)
     elif workspace.numel() * workspace.element_size() < need:
         raise ValueError(f"workspace too small: need {need} bytes")
     with _on(dev):
@@ -194,10 +200,16 @@ def paged_decode(
                 key_cache.data_ptr(), value_cache.data_ptr(), nb, block_tables.data_ptr(),
                 block_tables.stride(0), context_lens.data_ptr(), B, H, H_kv, D, bs, max_blocks,
                 float(scale), num_splits, workspace.data_ptr(),
-                workspace.numel() * workspace.element_size(), code, _stream(dev),
+                workspace.numel() * workspace.element_size(), code, stream,
             )
         )
     return out
+
+
+# (B, H, H_kv, D, block_size, max_blocks, dtype, num_splits argument) ->
+# (split count, workspace bytes the kernel needs, bytes to allocate): the
+# library's answers for a shape, asked once per shape instead of per call.
+_DECODE_PLANS: dict = {}
 
 
 def paged_decode_shared_prefix(
@@ -458,19 +470,24 @@ def sample(
         out = torch.empty(B, dtype=torch.int64, device=dev)
     if B == 0:
         return out
-    need = int(lib().lk_sample_workspace_bytes(B, V))
+    need = _SAMPLE_WS.get((B, V))
+    if need is None:
+        need = _SAMPLE_WS[(B, V)] = int(lib().lk_sample_workspace_bytes(B, V))
+    stream = _stream(dev)
     if workspace is None:
-        workspace = WORKSPACES.get(dev, f"sample:{_stream(dev)}", need)
+        workspace = WORKSPACES.get(dev, f"sample:{stream}", need)
     with _on(dev):
         check(
             lib().lk_sample(
                 out.data_ptr(), logits.data_ptr(), B, V, logits.stride(0), _ptr(temperatures),
                 _ptr(noise), noise_ld, seed & (2**64 - 1), offset & (2**64 - 1), _ptr(noise_dump),
-                workspace.data_ptr(), workspace.numel() * workspace.element_size(), code,
-                _stream(dev),
+                workspace.data_ptr(), workspace.numel() * workspace.element_size(), code, stream,
             )
         )
     return out
+
+
+_SAMPLE_WS: dict = {}  # (B, V) -> lk_sample_workspace_bytes, asked once per shape
 
 
 def sample_filtered(

@@ -24,6 +24,21 @@ def test_shards_partition_the_batch():
             assert got == list(range(G))
 
 
+def test_balanced_shards_partition_and_balance():
+    for G, W in ((64, 8), (2048, 8), (64, 3), (10, 4), (5, 8)):
+        lens = [workloads.context_len(5, 0, i) for i in range(G)]
+        parts = [sharding.balanced_shard(lens, W, r) for r in range(W)]
+        assert sorted(i for p in parts for i in p) == list(range(G))
+        counts = [len(p) for p in parts]
+        assert max(counts) - min(counts) <= 1
+        if G % W == 0 and G >= 2 * W:
+            sums = [sum(lens[i] for i in p) for p in parts]
+            contiguous = [sum(lens[i] for i in sharding.shard(G, W, r)) for r in range(W)]
+            # the slowest rank carries less than with contiguous blocks
+            assert max(sums) <= max(contiguous)
+            assert max(sums) - min(sums) <= max(lens) - min(lens)
+
+
 def test_context_lengths_keyed_by_global_index():
     full = [workloads.context_len(2, 0, i) for i in range(64)]
     assert all(16 <= c <= 4096 for c in full)
