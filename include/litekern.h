@@ -301,12 +301,16 @@ int lk_copy_blocks(const uint64_t* src_cache_ptrs, const uint64_t* dst_cache_ptr
  * the caller's fp32 cos / sin tables ([max_pos, D/2], the RotaryEmbedding
  * cos_cached / sin_cached buffers) at positions[t]; q is rotated in place
  * ([T, H, D]); k is rotated and stored with v into slot slot_mapping[t] of the
- * caches (slot_mapping NULL: q / k only, no store; -1: skip). D = 128, dtype
+ * caches (slot_mapping NULL: q / k only, no store; -1: skip), and written to
+ * k_out ([T, H_kv, D], token stride k_out_token_stride; may be k itself) when
+ * k_out is not NULL, for attention over the new tokens only (the reference's
+ * _prefill reads the rotated k directly). D = 128, dtype
  * F16 or BF16, rounding points as in the reference (16-bit after the norm
  * and after the weight, fp32 rotation, 16-bit store).
  */
 int lk_rope_store_kv(void* q, int64_t q_token_stride, const void* k, int64_t k_token_stride,
-                     const void* v, int64_t v_token_stride, void* k_cache, void* v_cache,
+                     const void* v, int64_t v_token_stride, void* k_out,
+                     int64_t k_out_token_stride, void* k_cache, void* v_cache,
                      int64_t num_slots, const int64_t* slot_mapping, const int64_t* positions,
                      const float* cos_cache, const float* sin_cache, int64_t max_pos,
                      const void* q_norm_weight, const void* k_norm_weight, float eps,

@@ -22,7 +22,8 @@ _ATTENTION_SITES = ("litevllm.layers.attention", "litevllm.layers", "litevllm.mo
 _SAMPLER_SITES = ("litevllm.layers.sampler", "litevllm.layers", "litevllm.engine.llm_engine")
 
 
-def install(engine_hooks: bool = False) -> list[str]:
+def install(engine_hooks: bool = False, merged_steps: bool = False,
+            fused_rope: bool = False) -> list[str]:
     """Point litevllm's Attention, PagedAttention and Sampler at this package.
 
     Returns the patched "module.name" sites. Modules of litevllm that are not
@@ -30,7 +31,12 @@ def install(engine_hooks: bool = False) -> list[str]:
     With engine_hooks=True, ModelRunner.prepare_inputs and
     LLMEngine._process_outputs are also replaced by the vectorised / batched
     versions in litevllm_b200.engine_hooks (one sampler launch and one host
-    sync per step instead of one per sequence).
+    sync per step instead of one per sequence); merged_steps=True (with
+    engine_hooks) also replaces LLMEngine.step by one forward per step for
+    the prefill chunks and the decodes together. fused_rope=True replaces
+    Qwen3Attention.forward / LlamaAttention.forward by versions whose q/k
+    RMSNorm, rotary embedding and KV store are one kernel
+    (litevllm_b200.model_hooks).
     """
     from .attention import Attention, PagedAttention
     from .sampler import Sampler
@@ -61,7 +67,13 @@ def install(engine_hooks: bool = False) -> list[str]:
             return patched
         from . import engine_hooks as hooks
 
-        hooks.install(runner_mod.ModelRunner, engine_mod.LLMEngine)
+        hooks.install(runner_mod.ModelRunner, engine_mod.LLMEngine, merged_steps=merged_steps)
         patched += ["litevllm.engine.model_runner.ModelRunner.prepare_inputs",
                     "litevllm.engine.llm_engine.LLMEngine._process_outputs"]
+        if merged_steps:
+            patched.append("litevllm.engine.llm_engine.LLMEngine.step")
+    if fused_rope:
+        from . import model_hooks
+
+        patched += model_hooks.install()
     return patched

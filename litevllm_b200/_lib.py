@@ -96,7 +96,8 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "lk_rope_store_kv": (
         c_int32,
-        [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64,
+        [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p,
+         c_void_p, c_int64,
          c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float, c_int32,
          c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p],
     ),

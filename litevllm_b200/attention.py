@@ -51,6 +51,26 @@ SHARED_PREFIX_MIN_TOKENS = 256
 SHARED_PREFIX_MIN_ROWS = 4
 
 
+# Mixed-step hint, set by engine_hooks.prepare_inputs_mixed for a step whose
+# batch holds prefill chunks (rows [0, num_prefill_tokens) of every layer's
+# q / k / v, packed by cu_seqlens_q) followed by one decode token per
+# sequence. The model's layers pass the step's block_tables tensor to
+# Attention.forward unchanged; a call with that exact tensor runs
+# forward_mixed with the hint's layout (the reference's call signature has
+# no room for it).
+_MIXED_STEP = {"table": None}
+
+
+def set_mixed_step_hint(block_tables: Optional[torch.Tensor], cu_seqlens_q=None,
+                        num_prefill_seqs: int = 0, num_prefill_tokens: int = 0,
+                        max_q_len: int = 0) -> None:
+    """Declare the mixed layout of the step whose table is `block_tables`
+    (None clears the hint)."""
+    _MIXED_STEP.clear()
+    _MIXED_STEP.update(table=block_tables, cu_seqlens_q=cu_seqlens_q, P=int(num_prefill_seqs),
+                       TP=int(num_prefill_tokens), max_q_len=int(max_q_len))
+
+
 def set_shared_prefix_hint(block_tables: Optional[torch.Tensor], prefix_tokens: int) -> None:
     """Declare that every row of `block_tables` starts with the same
     `prefix_tokens` tokens (whole, filled blocks); None clears the hint."""
@@ -115,6 +135,13 @@ class Attention(nn.Module):
         context_lens and cu_seqlens_q attends prior paged context plus the
         chunk, for several sequences at once.
         """
+        mixed = _MIXED_STEP
+        if block_table is not None and block_table is mixed["table"]:
+            # a merged prefill + decode step (engine_hooks.prepare_inputs_mixed)
+            return self.forward_mixed(
+                query, key, value, key_cache, value_cache, block_table, slot_mapping,
+                context_lens, mixed["cu_seqlens_q"], mixed["P"], mixed["TP"], mixed["max_q_len"])
+
         if slot_mapping is not None and key_cache is not None:
             ops.store_kvcache(key, value, key_cache, value_cache, slot_mapping)
 

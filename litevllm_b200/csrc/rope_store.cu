@@ -8,7 +8,8 @@
 // the 16-bit weight dtype, multiplied by the weight in that dtype, the
 // rotation is computed in fp32 from the caller's fp32 cos / sin tables (the
 // RotaryEmbedding cos_cached / sin_cached buffers) and rounded once when
-// stored. One CTA per token, one warp per head (D = 128): lane l owns the
+// stored (and, when the caller asks, written back as the rotated k that an
+// attention over the new tokens alone reads). One CTA per token, one warp per head (D = 128): lane l owns the
 // rotation pairs (l, l + 64) and (l + 32, l + 96).
 #include "lk_common.cuh"
 #include "lk_host.h"
@@ -28,6 +29,8 @@ struct RopeParams {
   int64_t k_stride;
   const void* v;
   int64_t v_stride;
+  void* k_out;             // [T, H_kv, D] rotated k, or NULL
+  int64_t k_out_stride;
   void* k_cache;           // [num_slots, H_kv, D]
   void* v_cache;
   const int64_t* slot_mapping;
@@ -103,6 +106,11 @@ __global__ void __launch_bounds__(256) rope_store_kernel(const RopeParams p) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) x[i] = lk::Elem<T>::to_f(krow[lane + 32 * i]);
     norm_rope<T>(x, static_cast<const T*>(p.k_w), p.eps, cs, sn, lane);
+    if (p.k_out) {
+      T* ko = static_cast<T*>(p.k_out) + t * p.k_out_stride + h * kRopeD;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ko[lane + 32 * i] = from_f<T>(x[i]);
+    }
     if (store) {
       T* kd = static_cast<T*>(p.k_cache) + (slot * p.H_kv + h) * kRopeD;
       T* vd = static_cast<T*>(p.v_cache) + (slot * p.H_kv + h) * kRopeD;
@@ -120,7 +128,7 @@ __global__ void __launch_bounds__(256) rope_store_kernel(const RopeParams p) {
 
 extern "C" int lk_rope_store_kv(void* q, int64_t q_token_stride, const void* k,
                                 int64_t k_token_stride, const void* v, int64_t v_token_stride,
-                                void* k_cache, void* v_cache, int64_t num_slots,
+                                void* k_out, int64_t k_out_token_stride, void* k_cache, void* v_cache, int64_t num_slots,
                                 const int64_t* slot_mapping, const int64_t* positions,
                                 const float* cos_cache, const float* sin_cache, int64_t max_pos,
                                 const void* q_norm_weight, const void* k_norm_weight, float eps,
@@ -139,6 +147,8 @@ extern "C" int lk_rope_store_kv(void* q, int64_t q_token_stride, const void* k,
   p.k_stride = k_token_stride;
   p.v = v;
   p.v_stride = v_token_stride;
+  p.k_out = k_out;
+  p.k_out_stride = k_out_token_stride;
   p.k_cache = k_cache;
   p.v_cache = v_cache;
   p.slot_mapping = slot_mapping;

@@ -15,7 +15,19 @@
   temperature, top-k and top-p (top-k / top-p rows need 16-bit logits) and read
   back with one ``.tolist()``; the other rows go through ``Sampler.sample``.
 
-``install(runner_cls, engine_cls)`` binds both onto the reference classes.
+* ``prepare_inputs_mixed`` / ``merged_step`` — one forward per engine step
+  instead of one for the decode groups plus one per prefill group
+  (litevllm/engine/llm_engine.py:127-138): the step's prefill chunks come
+  first in the batch (packed by ``cu_seqlens_q``), then one token per decode
+  sequence; every sequence has its block table and context length, and the
+  attention layers run the chunked-prefill kernel (over the prior paged
+  context plus the chunk, causal inside it) next to the decode kernel.
+  Prefill rows see their prior context, which the reference's ``_prefill``
+  (block tables None) does not: the two agree for chunks that start at
+  position 0, the reference's own case.
+
+``install(runner_cls, engine_cls, merged_steps=False)`` binds them onto the
+reference classes.
 """
 
 from __future__ import annotations
@@ -25,7 +37,7 @@ import sys
 import numpy as np
 import torch
 
-from .attention import set_shared_prefix_hint
+from .attention import set_mixed_step_hint, set_shared_prefix_hint
 from .sampler import Sampler
 
 
@@ -117,6 +129,101 @@ def prepare_inputs(self, seq_groups, block_manager):
                          is_prefill=is_prefill, seq_ids=seq_ids)
 
 
+def _to_device(arr: np.ndarray, device: torch.device) -> torch.Tensor:
+    host = torch.from_numpy(arr)
+    if device.type == "cuda":
+        host = host.pin_memory()
+    return host.to(device, non_blocking=True)
+
+
+def prepare_inputs_mixed(self, prefill_groups, decode_groups, block_manager):
+    """InputMetadata of one merged step: the prefill chunks of prefill_groups
+    (in order), then one token per sequence of decode_groups. Token data are
+    what ModelRunner.prepare_inputs builds for each group
+    (model_runner.py:180-260); block_tables / context_lens cover every
+    sequence (a prefill row's context is its prior tokens plus its chunk).
+    The step's layout is handed to the attention layers through
+    set_mixed_step_hint; is_prefill is True when the step has a chunk."""
+    if not prefill_groups:
+        set_mixed_step_hint(None)
+        return prepare_inputs(self, decode_groups, block_manager)
+    InputMetadata = sys.modules[type(self).__module__].InputMetadata
+    bs = self.config.cache_config.block_size
+    ids_parts, pos_parts, slot_parts = [], [], []
+    tables, ctx_lens, seq_ids, q_lens = [], [], [], []
+    for phase, groups in ((True, prefill_groups), (False, decode_groups)):
+        for sg in groups:
+            for seq in sg.get_unfinished_seqs():
+                blocks = np.asarray(block_manager.get_block_table(seq.seq_id).physical_block_ids,
+                                    dtype=np.int64)
+                if seq.is_prefill != phase:
+                    raise ValueError("prefill_groups / decode_groups hold the other kind")
+                if phase:
+                    start, end = seq.num_computed_tokens, seq.data.prompt_len
+                    toks = np.asarray(seq.data.prompt_token_ids[start:end], dtype=np.int64)
+                    pos = np.arange(start, end, dtype=np.int64)
+                    ctx_lens.append(end)
+                    q_lens.append(end - start)
+                else:
+                    toks = np.asarray(seq.data.all_token_ids[-1:], dtype=np.int64)
+                    pos = np.asarray([seq.data.total_len - 1], dtype=np.int64)
+                    ctx_lens.append(seq.data.total_len)
+                seq_ids.append(seq.seq_id)
+                tables.append(blocks)
+                bidx = pos // bs
+                have = bidx < blocks.shape[0]
+                slot = np.zeros_like(pos)
+                if have.any():
+                    slot[have] = blocks[bidx[have]] * bs + pos[have] % bs
+                ids_parts.append(toks)
+                pos_parts.append(pos)
+                slot_parts.append(slot)
+    n = sum(p.shape[0] for p in pos_parts)
+    device = torch.device(self.device)
+    dev64 = _to_device(np.concatenate([np.concatenate(ids_parts), np.concatenate(pos_parts),
+                                       np.concatenate(slot_parts)]), device)
+    input_ids, positions, slot_mapping = dev64[:n], dev64[n:2 * n], dev64[2 * n:]
+    P = len(q_lens)
+    cu = np.zeros(P + 1, dtype=np.int32)
+    cu[1:] = np.cumsum(q_lens)
+    max_blocks = max(t.shape[0] for t in tables)
+    tab = np.zeros((len(tables), max_blocks), dtype=np.int32)
+    for i, t in enumerate(tables):
+        tab[i, :t.shape[0]] = t
+    d32 = _to_device(np.concatenate([tab.reshape(-1), np.asarray(ctx_lens, dtype=np.int32), cu]),
+                     device)
+    nb = len(tables) * max_blocks
+    block_tables = d32[:nb].view(len(tables), max_blocks)
+    context_lens = d32[nb:nb + len(tables)]
+    cu_seqlens_q = d32[nb + len(tables):]
+    set_shared_prefix_hint(None, 0)
+    set_mixed_step_hint(block_tables, cu_seqlens_q, P, int(cu[-1]), max(q_lens))
+    return InputMetadata(input_ids=input_ids, positions=positions, slot_mapping=slot_mapping,
+                         block_tables=block_tables, context_lens=context_lens,
+                         is_prefill=True, seq_ids=seq_ids)
+
+
+def merged_step(self):
+    """LLMEngine.step with one forward for all scheduled groups (prefill
+    chunks, then decodes) instead of llm_engine.py:127-138's one forward for
+    the decode groups plus one per prefill group; scheduling, outputs and
+    bookkeeping as in the reference step (:111-151)."""
+    sched_output = self.scheduler.schedule()
+    if sched_output.is_empty:
+        return []
+    groups = sched_output.scheduled_seq_groups
+    prefill = [sg for sg in groups if any(s.is_prefill for s in sg.get_unfinished_seqs())]
+    decode = [sg for sg in groups if not any(s.is_prefill for s in sg.get_unfinished_seqs())]
+    metadata = prepare_inputs_mixed(self.model_runner, prefill, decode, self.block_manager)
+    logits = self.model_runner.execute_model(metadata)
+    set_mixed_step_hint(None)
+    self._process_outputs(logits, prefill + decode)
+    results = [self._build_step_output(sg) for sg in groups]
+    self.scheduler.update_running(groups)
+    self.scheduler.free_finished()
+    return results
+
+
 def process_outputs(self, logits, seq_groups) -> None:
     """Batched LLMEngine._process_outputs (one sampler launch for plain rows)."""
     entries = []
@@ -148,8 +255,12 @@ def process_outputs(self, logits, seq_groups) -> None:
             top_k = torch.tensor([int(sp.top_k) for sp in params], dtype=torch.int32, device=dev)
             top_p = torch.tensor([float(sp.top_p) for sp in params], dtype=torch.float32,
                                  device=dev)
-        picked = Sampler.sample_batch(logits.index_select(0, rows), temps, top_k=top_k,
-                                      top_p=top_p).tolist()
+        row_ids = [entries[i][2] for i in fast]
+        if row_ids == list(range(logits.shape[0])):
+            sel = logits  # every row sampled, in order: no gather
+        else:
+            sel = logits.index_select(0, rows)
+        picked = Sampler.sample_batch(sel, temps, top_k=top_k, top_p=top_p).tolist()
         for i, t in zip(fast, picked):
             tokens[i] = int(t)
     for i, (sg, seq, row) in enumerate(entries):
@@ -160,7 +271,10 @@ def process_outputs(self, logits, seq_groups) -> None:
         self._should_stop(seq, sg.sampling_params, tok)
 
 
-def install(runner_cls, engine_cls) -> None:
-    """Bind the batched methods onto the reference ModelRunner / LLMEngine."""
+def install(runner_cls, engine_cls, merged_steps: bool = False) -> None:
+    """Bind the batched methods onto the reference ModelRunner / LLMEngine;
+    with merged_steps also LLMEngine.step (one forward per step)."""
     runner_cls.prepare_inputs = prepare_inputs
     engine_cls._process_outputs = process_outputs
+    if merged_steps:
+        engine_cls.step = merged_step

@@ -610,12 +610,17 @@ def rope_store_kvcache(
     k_norm_weight: Optional[torch.Tensor] = None,
     eps: float = 1e-6,
     status: Optional[torch.Tensor] = None,
+    key_out: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """In one launch: optional q/k RMSNorm, RoPE on q (in place) and k, and the
     store of k / v into the paged cache. Mirrors Qwen3Attention.forward
-    (litevllm/models/qwen3.py:76-92) up to the attention call; returns query."""
+    (litevllm/models/qwen3.py:76-92) up to the attention call; returns query.
+    key_out ([T, H_kv, D], may be key itself) receives the rotated k."""
     dev = _cuda(query, key, value, key_cache, value_cache, slot_mapping, positions, cos_cached,
-                sin_cached, q_norm_weight, k_norm_weight, status)
+                sin_cached, q_norm_weight, k_norm_weight, status, key_out)
+    if key_out is not None and (key_out.shape != key.shape or key_out.dtype != key.dtype
+                                or key_out.stride(2) != 1 or key_out.stride(1) != key.shape[2]):
+        raise ValueError("key_out must match key's shape and dtype, unit d-stride, head stride D")
     T, H, D = query.shape
     H_kv = key.shape[1]
     for t in (query, key, value):
@@ -641,7 +646,8 @@ def rope_store_kvcache(
         check(
             lib().lk_rope_store_kv(
                 query.data_ptr(), query.stride(0), key.data_ptr(), key.stride(0), value.data_ptr(),
-                value.stride(0), _ptr(key_cache), _ptr(value_cache), num_slots, _ptr(slot_mapping),
+                value.stride(0), _ptr(key_out), 0 if key_out is None else key_out.stride(0),
+                _ptr(key_cache), _ptr(value_cache), num_slots, _ptr(slot_mapping),
                 positions.data_ptr(), cos_cached.data_ptr(), sin_cached.data_ptr(),
                 cos_cached.shape[0], _ptr(q_norm_weight), _ptr(k_norm_weight), float(eps), T, H,
                 H_kv, D, code, _ptr(status), _stream(dev),

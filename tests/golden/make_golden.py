@@ -151,7 +151,57 @@ def main(ref_root: str) -> None:
         q_out_dtype=str(q_ref.dtype),
     )
     penalty_fixture(ref_root)
+    attention_block_fixture(ref_root)
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
+
+
+def attention_block_fixture(ref_root: str) -> None:
+    """The reference's own Qwen3Attention (q/k RMSNorm) and LlamaAttention
+    blocks in bf16 (Attention from the reference too): a 20-token prefill that
+    stores its K/V into a paged cache, then one decode step over that cache.
+    Weights, inputs, the bf16 cos / sin tables and both outputs are saved."""
+    sys.path.insert(0, ref_root)
+    from litevllm.models.llama import LlamaAttention
+    from litevllm.models.qwen3 import Qwen3Attention
+
+    g = torch.Generator().manual_seed(777)
+    hidden, H, H_kv, D, bs, S = 256, 8, 2, 128, 16, 20
+    out = {}
+    for tag, cls, kw in (("qwen3", Qwen3Attention, dict(rope_theta=1000000.0, use_qk_norm=True)),
+                         ("llama", LlamaAttention, dict(rope_theta=500000.0))):
+        torch.manual_seed(5)
+        m = cls(hidden, H, H_kv, D, max_position_embeddings=4096, **kw)
+        with torch.no_grad():
+            for name, prm in m.named_parameters():
+                if name.endswith("norm.weight"):
+                    prm.copy_(1 + 0.1 * torch.randn(prm.shape, generator=g))
+                else:
+                    prm.copy_(torch.randn(prm.shape, generator=g) * prm.shape[-1] ** -0.5)
+        m = m.to(torch.bfloat16)
+        kc = torch.zeros((8, bs, H_kv, D), dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+        blocks = [3, 5]
+        x = torch.randn((S, hidden), generator=g).bfloat16()
+        pos = torch.arange(S)
+        slots = torch.tensor([blocks[p // bs] * bs + p % bs for p in range(S)])
+        x2 = torch.randn((1, hidden), generator=g).bfloat16()
+        with torch.no_grad():
+            y = m(x, pos, (kc, vc), slots, None, None, True)
+            y2 = m(x2, torch.tensor([S]), (kc, vc), torch.tensor([blocks[S // bs] * bs + S % bs]),
+                   torch.tensor([blocks], dtype=torch.int32),
+                   torch.tensor([S + 1], dtype=torch.int32), False)
+        sd = {k: bf16_bits(v) for k, v in m.state_dict().items() if v.dtype == torch.bfloat16}
+        out.update({f"{tag}.{k}": v for k, v in sd.items()})
+        out.update({f"{tag}.x": bf16_bits(x), f"{tag}.x2": bf16_bits(x2),
+                    f"{tag}.y": y.float().numpy(), f"{tag}.y2": y2.float().numpy(),
+                    # the rows of the positions used (the test's tables stop there)
+                    f"{tag}.cos": bf16_bits(m.rotary_emb.cos_cached[:64]),
+                    f"{tag}.sin": bf16_bits(m.rotary_emb.sin_cached[:64]),
+                    f"{tag}.k_cache": bf16_bits(kc), f"{tag}.v_cache": bf16_bits(vc),
+                    f"{tag}.eps": np.float32(getattr(getattr(m, "q_norm", None), "eps", 1e-6))})
+    out["shape"] = np.array([hidden, H, H_kv, D, bs, S])
+    out["blocks"] = np.array([3, 5])
+    np.savez_compressed(HERE / "attn_block.npz", **out)
 
 
 def penalty_fixture(ref_root: str) -> None:
@@ -182,6 +232,12 @@ def penalty_fixture(ref_root: str) -> None:
 
 if __name__ == "__main__":
     # the reference checkout: argument, LITEVLLM_REFERENCE, else a "reference"
-    # directory beside this repository
-    main(sys.argv[1] if len(sys.argv) > 1 else
-         os.environ.get("LITEVLLM_REFERENCE") or str(HERE.parent.parent.parent / "reference"))
+    # directory beside this repository; "--only NAME" writes one fixture
+    args = [a for a in sys.argv[1:] if not a.startswith("--only")]
+    root = args[0] if args else (os.environ.get("LITEVLLM_REFERENCE")
+                                 or str(HERE.parent.parent.parent / "reference"))
+    only = [a.split("=", 1)[1] for a in sys.argv[1:] if a.startswith("--only=")]
+    if only == ["attn_block"]:
+        attention_block_fixture(root)
+    else:
+        main(root)

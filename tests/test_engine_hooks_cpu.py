@@ -133,3 +133,63 @@ def test_shared_prefix_tokens_counts_whole_shared_filled_blocks():
     assert shared_prefix_tokens([a, c], [80, 90], 16) == 64             # 4 shared, all filled
     assert shared_prefix_tokens([a], [80], 16) == 0                     # one row: nothing shared
     assert shared_prefix_tokens([a, np.array([6, 9])], [80, 32], 16) == 0
+
+
+def test_prepare_inputs_mixed_matches_reference_per_group(ref, monkeypatch):
+    """One merged step (prefill chunks, then decodes) carries exactly the
+    token data of the reference's per-group prepare_inputs calls
+    (llm_engine.py:127-138), plus a table and context length for every row
+    and cu_seqlens_q for the chunks."""
+    import numpy as np
+
+    from litevllm_b200 import attention, engine_hooks
+    import litevllm.engine.model_runner as mr
+
+    sched = _schedule(ref, [list(range(3, 40)), list(range(7, 30))])
+    first = sched.schedule().scheduled_seq_groups
+    for sg in first:  # both become decodes that have crossed a block boundary
+        for seq in sg.get_unfinished_seqs():
+            seq.num_computed_tokens = seq.data.prompt_len
+            for t in range(5):
+                seq.data.append_token(200 + t)
+                if seq.get_num_blocks(16) > len(sched.block_manager.get_block_table(seq.seq_id)):
+                    sched.block_manager.append_slot(seq.seq_id)
+    sched.update_running(first)
+    for i, p in enumerate([list(range(50, 83)), list(range(9, 14))]):
+        sched.add_request(ref.SequenceGroup.create(f"n{i}", p, ref.SamplingParams(temperature=0.0)))
+    groups = sched.schedule().scheduled_seq_groups
+    prefill = [g for g in groups if any(s.is_prefill for s in g.get_unfinished_seqs())]
+    decode = [g for g in groups if not any(s.is_prefill for s in g.get_unfinished_seqs())]
+    assert len(prefill) == 2 and len(decode) == 2
+    runner = _runner(ref)
+    monkeypatch.setattr(sys.modules[type(runner).__module__], "InputMetadata", mr.InputMetadata,
+                        raising=False)
+    bm = sched.block_manager
+    got = engine_hooks.prepare_inputs_mixed(runner, prefill, decode, bm)
+    want_p = [ref.ModelRunner.prepare_inputs(runner, [g], bm) for g in prefill]
+    want_d = ref.ModelRunner.prepare_inputs(runner, decode, bm)
+    for name in ("input_ids", "positions", "slot_mapping"):
+        want = torch.cat([getattr(w, name) for w in want_p] + [getattr(want_d, name)])
+        assert torch.equal(getattr(got, name), want), name
+    assert got.seq_ids == sum((w.seq_ids for w in want_p), []) + want_d.seq_ids
+    P = len(prefill)
+    # decode rows: the reference's tables (zero padded further) and lengths
+    mb = want_d.block_tables.shape[1]
+    assert torch.equal(got.block_tables[P:, :mb], want_d.block_tables)
+    assert not got.block_tables[P:, mb:].any()
+    assert torch.equal(got.context_lens[P:], want_d.context_lens)
+    # prefill rows: their whole tables, context = prior + chunk = prompt length
+    for i, g in enumerate(prefill):
+        seq = g.get_unfinished_seqs()[0]
+        ids = bm.get_block_table(seq.seq_id).physical_block_ids
+        assert got.block_tables[i, :len(ids)].tolist() == ids
+        assert int(got.context_lens[i]) == seq.data.prompt_len
+    hint = attention._MIXED_STEP
+    q_lens = [w.input_ids.numel() for w in want_p]
+    assert hint["table"] is got.block_tables and hint["P"] == P
+    assert hint["TP"] == sum(q_lens) and hint["max_q_len"] == max(q_lens)
+    assert hint["cu_seqlens_q"].tolist() == [0] + np.cumsum(q_lens).tolist()
+    # a step without chunks is the plain decode metadata, hint cleared
+    plain = engine_hooks.prepare_inputs_mixed(runner, [], decode, bm)
+    _same(plain, want_d)
+    assert attention._MIXED_STEP["table"] is None

@@ -118,6 +118,26 @@ def test_decode_config5_long_context_subset(cuda):
     _check(b)
 
 
+def test_decode_config5_full_batch_eight_rows(cuda):
+    """Config 5 at full size: 64 sequences of 32K-128K tokens (22 GB of bf16
+    KV) in one split-KV launch; the oracle checks 8 rows, the longest among
+    them, each on its own gathered blocks."""
+    b = workloads.make_decode_batch(5, 64, seed=0, device=cuda)
+    out = ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables, b.context_lens,
+                           b.scale)
+    longest = max(range(64), key=lambda i: b.ctx[i])
+    rows = sorted(set(list(range(3, 64, 9)) + [longest]))
+    assert len(rows) >= 8
+    for i in rows:
+        n = -(-b.ctx[i] // 16)
+        blk = b.block_tables[i, :n].long()
+        kc, vc = b.key_cache[blk].float(), b.value_cache[blk].float()
+        bt = torch.arange(n, dtype=torch.int32, device=cuda)[None]
+        ref = pa.decode(b.query[i:i + 1].float(), kc, vc, bt, b.context_lens[i:i + 1], b.scale)
+        assert_attn_close(out[i:i + 1], ref)
+        del kc, vc
+
+
 def test_decode_two_streams_concurrently(cuda):
     """Split decodes on two streams at once: each stream has its own default
     workspace (counters, partials, ordering), so neither corrupts the other."""

@@ -115,6 +115,28 @@ def test_install_patches_reference_namespace():
         import litevllm.models.qwen3 as Q
 
         assert Q.Attention is Attention
+        # the optional hooks: engine methods, merged steps, fused norm + RoPE + store
+        import litevllm.engine.llm_engine as E
+        import litevllm.engine.model_runner as MR
+        import litevllm.models.llama as LL
+
+        from litevllm_b200 import engine_hooks, model_hooks
+
+        saved = (MR.ModelRunner.prepare_inputs, E.LLMEngine._process_outputs, E.LLMEngine.step,
+                 Q.Qwen3Attention.forward, LL.LlamaAttention.forward)
+        try:
+            sites = install(engine_hooks=True, merged_steps=True, fused_rope=True)
+            assert MR.ModelRunner.prepare_inputs is engine_hooks.prepare_inputs
+            assert E.LLMEngine._process_outputs is engine_hooks.process_outputs
+            assert E.LLMEngine.step is engine_hooks.merged_step
+            assert Q.Qwen3Attention.forward is model_hooks.fused_forward
+            assert LL.LlamaAttention.forward is model_hooks.fused_forward
+            assert "litevllm.models.qwen3.Qwen3Attention.forward" in sites
+            # the unfused forward stays reachable for shapes the kernel does not take
+            assert model_hooks._ORIGINAL[Q.Qwen3Attention] is saved[3]
+        finally:
+            (MR.ModelRunner.prepare_inputs, E.LLMEngine._process_outputs, E.LLMEngine.step,
+             Q.Qwen3Attention.forward, LL.LlamaAttention.forward) = saved
     finally:
         sys.path.remove(str(REF))
 
