@@ -333,9 +333,11 @@ int lk_host_device_pointer(const void* host_ptr, uint64_t* device_ptr);
  * draw over the kept tokens (same distribution; bit-exact given the noise).
  * Per row: temperatures[b] (0 = greedy, filters ignored), top_k[b] (<= 0 or
  * NULL: off), top_p[b] (>= 1 or NULL: off). Noise as for lk_sample (given
- * tensor, or Philox keyed by seed / offset / row / index). 16-bit logits
- * ([B, V], row stride ld); tokens with equal logits are kept or dropped
- * together. No workspace.
+ * tensor, or Philox keyed by seed / offset / row / index). Logits F32, F16
+ * or BF16 ([B, V], row stride ld); tokens with equal logits are kept or
+ * dropped together; with F32 logits the top-k survivors also include every
+ * token whose probability equals the k-th largest (distinct fp32 logits can
+ * round to one probability, and the reference keeps them all). No workspace.
  */
 int lk_sample_filtered(int64_t* out_ids, const void* logits, int32_t B, int32_t V, int64_t ld,
                        const float* temperatures, const int32_t* top_k, const float* top_p,

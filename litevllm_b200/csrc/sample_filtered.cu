@@ -8,16 +8,21 @@
 // Drawing argmax over the kept tokens of x / T + g, g Gumbel noise, samples the
 // renormalised kept distribution exactly, so no probabilities are written.
 //
-// One CTA (1024 threads) per row; 16-bit logits, so each value has a 16-bit
-// order-preserving key and both cut points are found with two 8-bit passes:
+// One CTA (1024 threads) per row. Each logit has an order-preserving integer
+// key of its own width (16 bits for bf16 / f16, 32 for fp32), and both cut
+// points are found with one 8-bit radix pass per key byte:
 //   1. max of y = x / T and Z = sum exp(y - max)
-//   2-3. top-k: radix select of the k-th largest key (high byte, then low byte)
-//   4-5. top-p: probability mass per key byte among the top-k survivors, scanned
-//        from the top, gives the smallest key whose strictly-greater mass is
-//        <= top_p (high byte, then low byte)
-//   6. Gumbel-max over keys >= max(both cuts).
+//   2. top-k: radix select of the k-th largest key, high byte first
+//   3. top-p: probability mass per key byte among the top-k survivors, scanned
+//      from the top, gives the smallest key whose strictly-greater mass is
+//      <= top_p, high byte first
+//   4. Gumbel-max over keys >= max(both cuts).
 // Tokens with equal keys are kept or dropped together (the reference's sort
-// breaks such ties in an unspecified order).
+// breaks such ties in an unspecified order). fp32 logits: distinct logits can
+// round to the same probability, and the reference keeps every probability
+// equal to the k-th largest; so for fp32 the top-k survivors are the tokens
+// whose probability is >= that of the k-th largest key, not only its key and
+// above.
 #include "lk_common.cuh"
 #include "lk_host.h"
 #include "lk_philox.cuh"
@@ -59,6 +64,19 @@ template <typename T> LK_DEVINL uint32_t bits16(T x);
 template <> LK_DEVINL uint32_t bits16<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat16_as_ushort(x); }
 template <> LK_DEVINL uint32_t bits16<__half>(__half x) { return __half_as_ushort(x); }
 
+// Order-preserving key of a logit and its width in bytes.
+template <typename T> struct Key {
+  static constexpr int kBytes = 2;
+  LK_DEVINL static uint32_t of(T x) { return order_key16(bits16<T>(x)); }
+};
+template <> struct Key<float> {
+  static constexpr int kBytes = 4;
+  LK_DEVINL static uint32_t of(float x) {
+    const uint32_t u = __float_as_uint(x);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  }
+};
+
 // Block-wide sums / maxima over kFT threads.
 LK_DEVINL float block_sum(float v, float* red) {
 #pragma unroll
@@ -97,29 +115,39 @@ __global__ void __launch_bounds__(kFT) sample_filtered_kernel(const FilterParams
   const float top_p = p.top_p ? p.top_p[b] : 1.f;
   const bool sampled = temp > 0.f;
 
-  uint32_t cut = 0;  // keep keys >= cut
+  constexpr int kP = Key<T>::kBytes;
+  uint32_t cut = 0;        // top-k: keep keys >= cut
+  uint32_t pcut = 0;       // top-p: of the top-k survivors, keep keys >= pcut
+  bool tie_rule = false;   // fp32 top-k: also keep probabilities >= p_kth
+  float p_kth = 0.f, m = -INFINITY, inv_z = 0.f;
+  // survivors of the top-k cut
+  auto kept_k = [&](uint32_t key, float x) {
+    if (key >= cut) return true;
+    return tie_rule && expf(__fdiv_rn(x, temp) - m) * inv_z >= p_kth;
+  };
   if (sampled) {
     // ---- 1. max and normaliser of y = x / T
-    float m = -INFINITY;
     for (int v = threadIdx.x; v < V; v += kFT) m = fmaxf(m, __fdiv_rn(lk::Elem<T>::to_f(row[v]), temp));
     m = block_max(m, red);
     float z = 0.f;
     for (int v = threadIdx.x; v < V; v += kFT)
       z += expf(__fdiv_rn(lk::Elem<T>::to_f(row[v]), temp) - m);
     z = block_sum(z, red);
-    const float inv_z = 1.f / z;
+    inv_z = 1.f / z;
 
-    // ---- 2-3. top-k cut: the k-th largest key (radix select, two bytes)
+    // ---- 2. top-k cut: the k-th largest key (radix select, one byte a pass)
     if (k > 0 && k < V) {
       uint32_t prefix = 0;
       int need = k;
-      for (int pass = 0; pass < 2; ++pass) {
+      for (int pass = 0; pass < kP; ++pass) {
+        const int shift = 8 * (kP - 1 - pass);
         for (int i = threadIdx.x; i < 256; i += kFT) hcount[i] = 0u;
         __syncthreads();
         for (int v = threadIdx.x; v < V; v += kFT) {
-          const uint32_t key = order_key16(bits16<T>(row[v]));
-          if (pass == 0) atomicAdd(&hcount[key >> 8], 1u);
-          else if ((key >> 8) == prefix) atomicAdd(&hcount[key & 0xFFu], 1u);
+          const uint32_t key = Key<T>::of(row[v]);
+          // keys whose higher bytes equal the prefix found so far
+          const bool in = pass == 0 || (key >> (shift + 8)) == prefix;
+          if (in) atomicAdd(&hcount[(key >> shift) & 0xFFu], 1u);
         }
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -135,31 +163,38 @@ __global__ void __launch_bounds__(kFT) sample_filtered_kernel(const FilterParams
           s_sel[1] = need - acc;
         }
         __syncthreads();
-        if (pass == 0) prefix = static_cast<uint32_t>(s_sel[0]);
-        else prefix = (prefix << 8) | static_cast<uint32_t>(s_sel[0]);
+        prefix = (prefix << 8) | static_cast<uint32_t>(s_sel[0]);
         need = s_sel[1];
         __syncthreads();
       }
       cut = prefix;
+      if constexpr (kP == 4) {
+        // the k-th largest logit itself (keys map back one to one)
+        const uint32_t u = (cut & 0x80000000u) ? (cut & 0x7FFFFFFFu) : ~cut;
+        p_kth = expf(__fdiv_rn(__uint_as_float(u), temp) - m) * inv_z;
+        tie_rule = true;
+      }
     }
-
-    // ---- 4-5. top-p cut over the survivors of top-k. A key v is kept iff the
-    // mass of survivors with keys strictly above v is <= top_p. Pass 0 finds
-    // the high byte where the running mass (from the top) crosses top_p: keys
-    // in higher bytes are kept, lower ones dropped; pass 1 repeats inside that
-    // byte on the low byte.
+    // ---- 3. top-p cut over the survivors of top-k. A key v is kept iff the
+    // mass of survivors with keys strictly above v is <= top_p. Each pass
+    // finds, inside the bytes fixed so far, the byte where the running mass
+    // (from the top) crosses top_p: keys in higher bytes are kept, lower ones
+    // dropped.
     if (top_p < 1.f) {
       float above = 0.f;
       uint32_t prefix = 0;
-      for (int pass = 0; pass < 2; ++pass) {
+      for (int pass = 0; pass < kP; ++pass) {
+        const int shift = 8 * (kP - 1 - pass);
         for (int i = threadIdx.x; i < 256; i += kFT) hmass[i] = 0.f;
         __syncthreads();
         for (int v = threadIdx.x; v < V; v += kFT) {
-          const uint32_t key = order_key16(bits16<T>(row[v]));
-          if (key < cut) continue;
-          if (pass == 1 && (key >> 8) != prefix) continue;
-          const float pv = expf(__fdiv_rn(lk::Elem<T>::to_f(row[v]), temp) - m) * inv_z;
-          atomicAdd(&hmass[pass == 0 ? (key >> 8) : (key & 0xFFu)], pv);
+          const T raw = row[v];
+          const uint32_t key = Key<T>::of(raw);
+          const float x = lk::Elem<T>::to_f(raw);
+          if (!kept_k(key, x)) continue;
+          if (pass > 0 && (key >> (shift + 8)) != prefix) continue;
+          const float pv = expf(__fdiv_rn(x, temp) - m) * inv_z;
+          atomicAdd(&hmass[(key >> shift) & 0xFFu], pv);
         }
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -179,21 +214,21 @@ __global__ void __launch_bounds__(kFT) sample_filtered_kernel(const FilterParams
         const int bin = s_sel[0];
         const float acc = red[0];
         __syncthreads();
-        if (pass == 0) {
-          if (bin < 0) break;  // all survivors fit within top_p
-          prefix = static_cast<uint32_t>(bin);
-          above = acc;
-        } else {
-          // bin < 0 here only if the low-byte sums rounded differently from
-          // the high-byte sum: keep the whole crossing byte.
-          const uint32_t pcut = (prefix << 8) | static_cast<uint32_t>(bin < 0 ? 0 : bin);
-          if (pcut > cut) cut = pcut;
+        if (bin < 0) {
+          // pass 0: all survivors fit within top_p, no cut. A later pass
+          // only if the lower-byte sums rounded differently from the
+          // enclosing byte's sum: keep that whole byte.
+          if (pass > 0) pcut = prefix << (shift + 8);
+          break;
         }
+        prefix = (prefix << 8) | static_cast<uint32_t>(bin);
+        above = acc;
+        if (pass == kP - 1) pcut = prefix;
       }
     }
   }
 
-  // ---- 6. argmax of y + g over keys >= cut (greedy rows: argmax x)
+  // ---- 4. argmax of y + g over the kept keys (greedy rows: argmax x)
   float best = -INFINITY;
   int besti = 0x7fffffff;
   for (int v = threadIdx.x; v < V; v += kFT) {
@@ -203,7 +238,8 @@ __global__ void __launch_bounds__(kFT) sample_filtered_kernel(const FilterParams
     if (!sampled) {
       key = x;
     } else {
-      if (order_key16(bits16<T>(raw)) < cut) continue;
+      const uint32_t kx = Key<T>::of(raw);
+      if (kx < pcut || !kept_k(kx, x)) continue;
       key = __fadd_rn(__fdiv_rn(x, temp), gumbel_at(p, b, v));
     }
     if (key > best || (key != key && best == best)) {
@@ -254,7 +290,8 @@ extern "C" int lk_sample_filtered(int64_t* out_ids, const void* logits, int32_t 
   if (B == 0) return LK_OK;
   if (!out_ids || !logits || B > 0x7fffffff) return LK_ERR_INVALID_ARG;
   if (noise && noise_ld < V) return LK_ERR_INVALID_ARG;
-  if (dtype != LK_DTYPE_BF16 && dtype != LK_DTYPE_F16) return LK_ERR_UNSUPPORTED;
+  if (dtype != LK_DTYPE_BF16 && dtype != LK_DTYPE_F16 && dtype != LK_DTYPE_F32)
+    return LK_ERR_UNSUPPORTED;
   FilterParams p;
   p.logits = logits;
   p.ld = ld;
@@ -270,6 +307,7 @@ extern "C" int lk_sample_filtered(int64_t* out_ids, const void* logits, int32_t 
   p.out = out_ids;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == LK_DTYPE_BF16) sample_filtered_kernel<__nv_bfloat16><<<B, kFT, 0, s>>>(p);
-  else sample_filtered_kernel<__half><<<B, kFT, 0, s>>>(p);
+  else if (dtype == LK_DTYPE_F16) sample_filtered_kernel<__half><<<B, kFT, 0, s>>>(p);
+  else sample_filtered_kernel<float><<<B, kFT, 0, s>>>(p);
   return lk::check_launch();
 }

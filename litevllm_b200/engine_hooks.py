@@ -12,7 +12,7 @@
   sampled from its row (the last prompt row for a prefill), prompts are marked
   computed, stop rules run in sequence order. Rows without a repetition
   penalty are sampled in one ``Sampler.sample_batch`` launch with per-row
-  temperature, top-k and top-p (top-k / top-p rows need 16-bit logits) and read
+  temperature, top-k and top-p and read
   back with one ``.tolist()``; the other rows go through ``Sampler.sample``.
 
 * ``prepare_inputs_mixed`` / ``merged_step`` — one forward per engine step
@@ -42,10 +42,7 @@ from .sampler import Sampler
 
 
 def _fast_params(params, logits_dtype) -> bool:
-    if getattr(params, "repetition_penalty", 1.0) != 1.0:
-        return False
-    filtered = getattr(params, "top_k", -1) > 0 or getattr(params, "top_p", 1.0) < 1.0
-    return not filtered or logits_dtype in (torch.bfloat16, torch.float16)
+    return getattr(params, "repetition_penalty", 1.0) == 1.0
 
 
 def shared_prefix_tokens(tables, ctx_lens, bs: int) -> int:

@@ -500,7 +500,7 @@ def sample_filtered(
     offset: int = 0,
     out: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
-    """Top-k / top-p filtered Gumbel-max sampling (16-bit logits), int64 [B].
+    """Top-k / top-p filtered Gumbel-max sampling (fp32 / f16 / bf16 logits), int64 [B].
     Mirrors Sampler.sample's filtered branch (litevllm/layers/sampler.py:178-225)."""
     if logits.dim() == 1:
         logits = logits.unsqueeze(0)
@@ -508,7 +508,7 @@ def sample_filtered(
     B, V = logits.shape
     if logits.stride(1) != 1:
         logits = logits.contiguous()
-    code = _dtype_code(logits)
+    code = _dtype_code(logits, (torch.float32, torch.float16, torch.bfloat16))
     temperatures = temperatures.to(torch.float32).contiguous()
     if top_k is not None:
         top_k = top_k.to(torch.int32).contiguous()

@@ -6,9 +6,9 @@ reference signature (litevllm/layers/sampler.py:147-187):
 * repetition penalty -> liblitekern fused kernel on a clone of the logits, the
   reference's arithmetic and dedupe (:190-201);
 * temperature 0 -> liblitekern greedy argmax (replaces _argmax_kernel);
-* top-k / top-p -> fused liblitekern filter + Gumbel-max draw for 16-bit
-  logits (same kept set and distribution as :204-225); fp32 logits use
-  liblitekern softmax(x / T), the reference's masking and torch.multinomial;
+* top-k / top-p -> fused liblitekern filter + Gumbel-max draw (same kept set
+  and distribution as :204-225; fp32, f16 and bf16 logits), no probability
+  tensor, no sort;
 * otherwise -> liblitekern Gumbel-max with in-kernel Philox noise: one pass,
   no probability tensor. The seed is drawn from torch's CPU generator, so
   torch.manual_seed makes it reproducible; sampling_params.seed, when set,
@@ -26,19 +26,6 @@ from typing import Optional
 import torch
 
 from . import ops
-
-
-def _apply_top_k_top_p(probs, top_k, top_p):
-    if top_k > 0:
-        k = min(top_k, probs.size(-1))
-        kth = torch.topk(probs, k, dim=-1).values[..., -1, None]
-        probs = torch.where(probs < kth, torch.zeros_like(probs), probs)
-    if top_p < 1.0:
-        sp, si = torch.sort(probs, descending=True, dim=-1)
-        cum = torch.cumsum(sp, dim=-1)
-        sp = torch.where(cum - sp > top_p, torch.zeros_like(sp), sp)
-        probs = torch.zeros_like(probs).scatter_(-1, si, sp)
-    return probs / probs.sum(dim=-1, keepdim=True).clamp_min(1e-9)
 
 
 class Sampler:
@@ -75,18 +62,14 @@ class Sampler:
             return ops.sample(logits)
         temps = torch.full((B,), T, dtype=torch.float32, device=logits.device)
         if sampling_params.top_k > 0 or sampling_params.top_p < 1.0:
-            if logits.dtype in (torch.bfloat16, torch.float16):
-                # fused: filter + Gumbel-max in one launch, no probability tensor
-                ks = torch.full((B,), int(sampling_params.top_k), dtype=torch.int32,
-                                device=logits.device)
-                ps = torch.full((B,), float(sampling_params.top_p), dtype=torch.float32,
-                                device=logits.device)
-                return ops.sample_filtered(logits, temps, ks, ps,
-                                           seed=Sampler._seed(sampling_params),
-                                           offset=Sampler._next_offset())
-            probs = ops.softmax_temp(logits, temps)
-            probs = _apply_top_k_top_p(probs, sampling_params.top_k, sampling_params.top_p)
-            return torch.multinomial(probs, num_samples=1).squeeze(-1)
+            # fused: filter + Gumbel-max in one launch, no probability tensor
+            ks = torch.full((B,), int(sampling_params.top_k), dtype=torch.int32,
+                            device=logits.device)
+            ps = torch.full((B,), float(sampling_params.top_p), dtype=torch.float32,
+                            device=logits.device)
+            return ops.sample_filtered(logits, temps, ks, ps,
+                                       seed=Sampler._seed(sampling_params),
+                                       offset=Sampler._next_offset())
         return ops.sample(
             logits, temps, seed=Sampler._seed(sampling_params), offset=Sampler._next_offset()
         )
@@ -109,7 +92,7 @@ class Sampler:
         """One sampler launch for a whole step: rows with temperature 0 are
         greedy, the others Gumbel-max at their own temperature; with per-row
         top_k (int32, <= 0 off) / top_p (fp32, >= 1 off) the fused filtered
-        kernel runs instead (16-bit logits)."""
+        kernel runs instead."""
         if temperatures is not None and temperatures.dtype != torch.float32:
             temperatures = temperatures.float()
         if top_k is not None or top_p is not None:

@@ -19,11 +19,12 @@ class SP:
         self.repetition_penalty, self.seed = repetition_penalty, seed
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("V", [1000, 8192, 151936])
-def test_filtered_noise_given_matches_oracle(cuda, V):
+def test_filtered_noise_given_matches_oracle(cuda, V, dtype):
     g = torch.Generator().manual_seed(V)
     B = 12
-    x = (torch.randn((B, V), generator=g) * 2).bfloat16()
+    x = (torch.randn((B, V), generator=g) * 2).to(dtype)
     temps = torch.tensor([0.7, 1.0, 1.3, 0.5] * 3)
     ks = torch.tensor([1, 5, 50, 0, 0, 0, 20, 1000, 3, 0, 7, 0], dtype=torch.int32)
     ps = torch.tensor([1.0, 1.0, 1.0, 0.9, 0.5, 0.1, 0.8, 0.95, 1.0, 0.999, 0.3, 1.0])
@@ -46,6 +47,34 @@ def test_reference_top_k_top_p_vectors(cuda):
     logits = torch.tensor([[10.0, 9.5, -100.0, -100.0]], device=cuda, dtype=torch.bfloat16)
     for _ in range(20):
         assert Sampler.sample(logits, SP(temperature=1.0, top_p=0.9)).tolist()[0] in (0, 1)
+
+
+def test_reference_top_k_top_p_vectors_fp32(cuda):
+    """The same vectors as the reference's tests use them, fp32 logits: the
+    fused kernel, no torch sort / multinomial."""
+    logits = torch.zeros(1, 8, device=cuda)
+    logits[0, 3] = 100.0
+    for _ in range(5):
+        assert Sampler.sample(logits, SP(temperature=1.0, top_k=1)).tolist() == [3]
+    logits = torch.tensor([[10.0, 9.5, -100.0, -100.0]], device=cuda)
+    for _ in range(20):
+        assert Sampler.sample(logits, SP(temperature=1.0, top_p=0.9)).tolist()[0] in (0, 1)
+
+
+def test_fp32_top_k_keeps_probability_ties(cuda):
+    """fp32 logits one ulp apart have the same probability after rounding;
+    the reference keeps every token whose probability equals the k-th
+    largest, so top_k=1 over such a pair must be able to draw either."""
+    x = torch.full((1, 64), -30.0)
+    x[0, 10] = 1e-3
+    x[0, 20] = float(np.nextafter(np.float32(1e-3), np.float32(0.0)))
+    kept, _ = osamp.filtered_kept(x[0].numpy(), 1.0, 1, 1.0)
+    assert kept[10] and kept[20]  # the reference keeps both
+    N = 4000
+    ids = ops.sample_filtered(x.repeat(N, 1).to(cuda), torch.ones(N, device=cuda),
+                              torch.ones(N, dtype=torch.int32, device=cuda), None,
+                              seed=3, offset=1).cpu()
+    assert set(ids.tolist()) == {10, 20}
 
 
 @pytest.mark.parametrize("k,p", [(5, 1.0), (0, 0.7), (10, 0.6)])
