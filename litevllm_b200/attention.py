@@ -159,7 +159,10 @@ class Attention(nn.Module):
                 cu_seqlens_q = torch.tensor([0, S], dtype=torch.int32, device=query.device)
                 max_q_len = S
             if max_q_len is None:
-                max_q_len = int((cu_seqlens_q[1:] - cu_seqlens_q[:-1]).max().item())
+                # an upper bound, known on the host: reading the longest chunk
+                # back from cu_seqlens_q would wait for the device; query tiles
+                # past a chunk's end take no work
+                max_q_len = query.shape[0]
             return ops.paged_prefill(
                 query, key_cache, value_cache, cu_seqlens_q, max_q_len, self.scale,
                 block_tables=block_table, context_lens=context_lens,

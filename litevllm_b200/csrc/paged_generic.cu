@@ -163,8 +163,13 @@ __global__ void __launch_bounds__(kGThreads) generic_attn_kernel(GenericParams p
   }
   // keys [0, kv_end) feed this tile's rows; this CTA takes [kv_beg, kv_stop)
   const int kv_end = max(0, prior + i0 + ntok);
-  const int kv_beg = sp * p.split_keys;
-  const int kv_stop = p.nsplit > 1 ? min(kv_end, kv_beg + p.split_keys) : kv_end;
+  // split bounds in 64 bits: near INT_MAX keys the last split's end would
+  // overflow; a split that starts past kv_end is empty
+  const int64_t beg64 = static_cast<int64_t>(sp) * p.split_keys;
+  const int kv_beg = static_cast<int>(min(beg64, static_cast<int64_t>(kv_end)));
+  const int kv_stop = p.nsplit > 1
+                          ? static_cast<int>(min(static_cast<int64_t>(kv_end), beg64 + p.split_keys))
+                          : kv_end;
 
   // Q rows of the tile: row r = (token i0 + r / G, head kvh * G + r % G).
   const T* q = static_cast<const T*>(p.q);

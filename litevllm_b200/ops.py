@@ -182,7 +182,7 @@ def paged_decode(
             num_splits = decode_num_splits(B, H_kv, max_blocks, bs)
         need = decode_workspace_bytes(B, H, H_kv, D, num_splits)
         want = need
-        if not tuned_attention_shape(query.dtype, D, bs, H // H_kv):
+        if not _decode_takes_split_kernel(query.dtype, D, bs, H // H_kv):
             # room for the generic kernel's split-KV partials (less only means fewer splits)
             want = max(need, int(lib().lk_paged_attention_generic_workspace_bytes(
                 B, H, D, max_blocks, bs)))
@@ -366,10 +366,21 @@ def paged_prefill(
     return out
 
 
+def _decode_takes_split_kernel(dtype: torch.dtype, head_dim: int, block_size: int, G: int) -> bool:
+    """lk_paged_decode's own routing: 16-bit caches, head_dim 128, block sizes
+    that are multiples of 16 and G <= 8 run the split kernel (G need not be a
+    power of two there); everything else the generic kernel, whose split-KV
+    partials want a larger workspace."""
+    return (dtype in (torch.float16, torch.bfloat16) and head_dim == 128
+            and block_size % 16 == 0 and G <= 8)
+
+
 def tuned_attention_shape(dtype: torch.dtype, head_dim: int, block_size: int, G: int) -> bool:
-    """True when the tuned decode / prefill / shared-prefix kernels take this
-    shape; other shapes run the generic CUDA-core kernel (fp32 caches, head
-    dims other than 128, block sizes not a multiple of 16, G not 1/2/4/8)."""
+    """True when the tuned prefill and shared-prefix kernels take this shape
+    (their tensor-core tiles hold 128 / G positions, so G is 1, 2, 4 or 8);
+    other shapes run the generic CUDA-core kernel (fp32 caches, head dims
+    other than 128, block sizes not a multiple of 16, other G). The decode
+    split kernel takes every G <= 8 (_decode_takes_split_kernel)."""
     return (dtype in (torch.float16, torch.bfloat16) and head_dim == 128
             and block_size % 16 == 0 and G in (1, 2, 4, 8))
 
@@ -414,8 +425,8 @@ def paged_attention_generic(
     else:
         cu_seqlens_q = cu_seqlens_q.contiguous()
         S = cu_seqlens_q.numel() - 1
-        mq = int(max_q_len) if max_q_len is not None else int(
-            (cu_seqlens_q[1:] - cu_seqlens_q[:-1]).max().item())
+        # without max_q_len, the row count bounds every chunk (no device read)
+        mq = int(max_q_len) if max_q_len is not None else T
     code = _dtype_code(query, (torch.float32, torch.float16, torch.bfloat16))
     out = torch.empty((T, H, D), dtype=query.dtype, device=dev)
     with _on(dev):

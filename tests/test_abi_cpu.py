@@ -143,6 +143,13 @@ def test_generic_shape_routing_and_workspace_sizes():
     assert not ops.tuned_attention_shape(torch.bfloat16, 64, 16, 4)
     assert not ops.tuned_attention_shape(torch.bfloat16, 128, 8, 4)
     assert not ops.tuned_attention_shape(torch.bfloat16, 128, 16, 3)
+    # the decode workspace follows lk_paged_decode's routing: G = 3 takes the
+    # split kernel there, so its default workspace is the split kernel's
+    for G, split in ((1, True), (3, True), (7, True), (8, True), (16, False)):
+        assert ops._decode_takes_split_kernel(torch.bfloat16, 128, 16, G) is split
+    assert not ops._decode_takes_split_kernel(torch.float32, 128, 16, 4)
+    assert not ops._decode_takes_split_kernel(torch.bfloat16, 64, 16, 4)
+    assert not ops._decode_takes_split_kernel(torch.bfloat16, 128, 8, 4)
     f = _lib.lib().lk_paged_attention_generic_workspace_bytes
     head = 256 + 65536 * 4
     assert f(256, 32, 64, 32, 16) == 256          # 512 keys: one split, status word only

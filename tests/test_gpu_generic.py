@@ -234,15 +234,20 @@ def test_generic_decode_unaligned_caches(cuda):
     assert torch.equal(out, aligned)
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_generic_split_decode_matches_single_pass(cuda, dtype):
+@pytest.mark.parametrize("D,dtype,H,H_kv", [
+    (64, torch.bfloat16, 32, 8), (64, torch.float32, 32, 8), (64, torch.float16, 32, 8),
+    (32, torch.bfloat16, 32, 8), (96, torch.float16, 16, 4), (128, torch.float32, 32, 8),
+    (256, torch.bfloat16, 16, 8), (128, torch.bfloat16, 32, 2), (128, torch.float16, 64, 4)])
+def test_generic_split_decode_matches_single_pass(cuda, D, dtype, H, H_kv):
     """lk_paged_decode splits long contexts across CTAs for the generic kernel
     (partials merged by a second launch); lk_paged_attention_generic runs one
     CTA per row. Both match the oracle, an empty split included (row 3 is far
-    shorter than the table)."""
-    b = workloads.make_decode_batch(2, 5, seed=27, ctx=[5000, 700, 31, 2048, 0], H=32, H_kv=8,
-                                    D=64, dtype=dtype, device=cuda)
-    assert _lib.lib().lk_paged_attention_generic_workspace_bytes(5, 32, 64, 313, 16) > 256
+    shorter than the table), over head dims 32-256, three dtypes and G = 16
+    (the split kernel takes G <= 8 only)."""
+    b = workloads.make_decode_batch(2, 5, seed=27 + D, ctx=[5000, 700, 31, 2048, 0], H=H,
+                                    H_kv=H_kv, D=D, dtype=dtype, device=cuda)
+    mb = b.block_tables.shape[1]
+    assert _lib.lib().lk_paged_attention_generic_workspace_bytes(5, H, D, mb, 16) > 256
     split = ops.paged_decode(b.query, b.key_cache, b.value_cache, b.block_tables,
                              b.context_lens, b.scale)
     single = ops.paged_attention_generic(b.query, b.key_cache, b.value_cache, b.scale,
