@@ -59,9 +59,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-sub", action="store_true",
                     help="skip the sub-records (sampler, cfg5, cfg3, cfg4) of the default line")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4", "cfg5"],
-                    help="cfg2 (default) is the contract's workload; cfg3 / cfg5 print a "
-                         "secondary line for the mixed prefill step / long-context decode")
+    ap.add_argument("--workload", default="cfg2",
+                    choices=["cfg2", "cfg3", "cfg4", "cfg5", "sampler"],
+                    help="cfg2 (default) is the contract's workload; the others print one "
+                         "sub-record alone (cfg3 mixed prefill step, cfg4 prefix-shared "
+                         "decode, cfg5 long-context decode, sampler greedy + in-kernel noise)")
     return ap.parse_args()
 
 
@@ -804,7 +806,11 @@ def main():
         torch.cuda.set_device(local)
         torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local))
     if args.workload != "cfg2":
-        rec = measure_sub(args.workload, args.steps, args.warmup, ws, rank, local)
+        if args.workload == "sampler":
+            torch.cuda.set_device(local)
+            rec = {"workload": "sampler", **measure_sampler(args.steps, args.warmup, ws, local)}
+        else:
+            rec = measure_sub(args.workload, args.steps, args.warmup, ws, rank, local)
         if rank == 0:
             print(json.dumps(rec), flush=True)
         if ws > 1:
