@@ -60,7 +60,7 @@ def parse():
     ap.add_argument("--no-sub", action="store_true",
                     help="skip the sub-records (sampler, cfg5, cfg3, cfg4) of the default line")
     ap.add_argument("--workload", default="cfg2",
-                    choices=["cfg2", "cfg3", "cfg4", "cfg5", "sampler"],
+                    choices=["cfg2", "cfg3", "cfg4", "cfg5", "sampler", "mma_rate"],
                     help="cfg2 (default) is the contract's workload; the others print one "
                          "sub-record alone (cfg3 mixed prefill step, cfg4 prefix-shared "
                          "decode, cfg5 long-context decode, sampler greedy + in-kernel noise)")
@@ -787,6 +787,41 @@ def measure_sampler(steps, warmup, ws, local):
     return rec
 
 
+def measure_mma_rate(local, n_mma=8192):
+    """Issue rate of tcgen05.mma on this GPU (lk_selftest_mma_rate): one CTA per
+    SM issues n_mma back-to-back M = 128, K = 16 bf16 MMAs of one shape; the
+    per-instruction cycles and the implied whole-GPU TFLOP/s (CUDA events)."""
+    from litevllm_b200 import _lib
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    nsm = torch.cuda.get_device_properties(dev).multi_processor_count
+    cycles = torch.zeros(nsm, dtype=torch.int64, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    peak_tf, kind = measured_tflops()
+    rec = {"n_mma": n_mma, "ctas": nsm}
+    for shape, name, N in ((0, "ss_128x128x16", 128), (1, "ss_128x256x16", 256),
+                           (2, "ts_128x128x16", 128)):
+        run = lambda: _lib.check(_lib.lib().lk_selftest_mma_rate(
+            n_mma, shape, cycles.data_ptr(), status.data_ptr(), stream.cuda_stream))
+        for _ in range(3):
+            run()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        run()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        c = cycles.double()
+        flops = nsm * n_mma * 2.0 * 128 * N * 16
+        tf = flops / (e0.elapsed_time(e1) * 1e-3) / 1e12
+        rec[name] = {"cycles_per_mma": round(float(c.median()) / n_mma, 1),
+                     "tflops": round(tf, 1), "frac_of_bf16_peak": round(tf / peak_tf, 4)}
+    rec["status"] = int(status.item())
+    rec["peak"] = f"{peak_tf} TFLOP/s ({kind} bf16 burst)"
+    return rec
+
+
 def _decode_launches(num_splits: int) -> int:
     """Kernels one ops.paged_decode call launches (mirrors the library's
     LITEKERN_DECODE_ORDER switch: the longest-first ordering kernel runs before
@@ -809,6 +844,8 @@ def main():
         if args.workload == "sampler":
             torch.cuda.set_device(local)
             rec = {"workload": "sampler", **measure_sampler(args.steps, args.warmup, ws, local)}
+        elif args.workload == "mma_rate":
+            rec = {"workload": "mma_rate", **measure_mma_rate(local)}
         else:
             rec = measure_sub(args.workload, args.steps, args.warmup, ws, rank, local)
         if rank == 0:

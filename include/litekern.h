@@ -365,6 +365,17 @@ int lk_selftest_sampler_div(float* out, const float* x, int32_t n, const float* 
 int lk_selftest_gumbel(float* out, const uint32_t* bits, int32_t n, void* stream);
 
 /*
+ * Tensor-core issue-rate self-test (no counterpart in the reference): one CTA
+ * per SM issues n_mma back-to-back tcgen05.mma (bf16, fp32 accumulator in
+ * TMEM, M = 128; shape 0: A and B in shared memory, N = 128; 1: N = 256;
+ * 2: A in TMEM, N = 128) and writes the SM cycles from first issue to
+ * completion to cycles[cta] (gridDim = number of SMs), -1 and
+ * LK_STATUS_WAIT_TIMEOUT in *status if the completion wait (100 ms) ran out.
+ */
+int lk_selftest_mma_rate(int32_t n_mma, int32_t shape, int64_t* cycles, int32_t* status,
+                         void* stream);
+
+/*
  * Allocation-free variant of lk_sample. It has no counterpart in the
  * reference. It is for callers that cannot call cudaMalloc at the point where
  * they sample: code running while another component owns the allocator

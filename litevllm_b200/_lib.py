@@ -89,6 +89,7 @@ SIGNATURES: dict[str, tuple] = {
     "lk_selftest_wait_timeout": (c_int32, [c_void_p, c_uint64, c_void_p]),
     "lk_selftest_sampler_div": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_void_p]),
     "lk_selftest_gumbel": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p]),
+    "lk_selftest_mma_rate": (c_int32, [c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
     "lk_sample_filtered": (
         c_int32,
         [c_void_p, c_void_p, c_int32, c_int32, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,

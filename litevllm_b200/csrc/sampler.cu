@@ -277,6 +277,9 @@ LK_DEVINL void finish_row(const SampleParams& p, int b, int ch, float best, int 
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(kSampThreads, kSampCtasPerSm) sample_kernel(const SampleParams p) {
   lk::pdl_wait();  // launched to overlap the kernel ahead of it: wait for it before reading
+  // a kernel launched after this one may place its CTAs in the SM slots this grid
+  // leaves free (it still waits for this grid to complete before reading)
+  lk::pdl_launch_dependents();
   const int ch = blockIdx.x, b = blockIdx.y;
   const float temp = p.temps ? p.temps[b] : 0.f;
   const int v0 = ch * p.chunk, v1 = min(p.V, v0 + p.chunk);
@@ -497,6 +500,9 @@ LK_DEVINL void resolve_index(const uint4& braw, float best, int& besti) {
 template <typename T, int kU, int kMinBlocks, bool kCluster>
 __global__ void __launch_bounds__(kSampThreads, kMinBlocks) argmax_kernel(const SampleParams p) {
   lk::pdl_wait();  // launched to overlap the kernel ahead of it: wait for it before reading
+  // a kernel launched after this one may place its CTAs in the SM slots this grid
+  // leaves free (it still waits for this grid to complete before reading)
+  lk::pdl_launch_dependents();
   const int ch = blockIdx.x, b = blockIdx.y;
   const int v0 = ch * p.chunk, v1 = min(p.V, v0 + p.chunk);
   const T* row = static_cast<const T*>(p.logits) + static_cast<int64_t>(b) * p.ld;
@@ -750,6 +756,9 @@ LK_DEVINL void gumbel_segment(const SampleParams& p, int b, int j0, int j1, bool
 template <typename T>
 __global__ void __launch_bounds__(kSampThreads, kGumbelCtasPerSm) gumbel_kernel(const SampleParams p) {
   lk::pdl_wait();  // launched to overlap the kernel ahead of it: wait for it before reading
+  // a kernel launched after this one may place its CTAs in the SM slots this grid
+  // leaves free (it still waits for this grid to complete before reading)
+  lk::pdl_launch_dependents();
   const int ch = blockIdx.x, b = blockIdx.y;
   const float temp = p.temps[b];
   const int cv = p.chunk / kVec;  // vectors per chunk
