@@ -507,6 +507,28 @@ def _time_events(stream, fn, K, warmup):
     return t0.elapsed_time(t1) / K, evs
 
 
+def _time_graph(fn, K, warmup, dev):
+    """fn() enqueued K times into one CUDA graph, replayed and timed with
+    CUDA events: ms per call on the device alone (the host's Python and
+    launch time, which can exceed a short kernel's, is not in the region)."""
+    for _ in range(max(1, warmup)):
+        fn()
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(K):
+            fn()
+    g.replay()
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / K
+
+
 def measure_sub(workload, steps, warmup, ws, rank, local):
     """Secondary workloads, device-timed per kernel with CUDA events, max over
     ranks: "cfg3" (mixed chunked-prefill + decode step), "cfg4" (prefix-shared
@@ -559,10 +581,20 @@ def measure_sub(workload, steps, warmup, ws, rank, local):
         dec_r = sum(a.elapsed_time(c) for a, c in evs) / len(evs)
         ms, evs = _time_events(stream, make_step(True), args.steps, max(3, args.warmup))
         dec_ms = sum(a.elapsed_time(c) for a, c in evs) / len(evs)
-        t = torch.tensor([ms, dec_ms, ms_r, dec_r], device=dev)
+        # device time alone, from CUDA graphs (see cfg3)
+        K = max(8, args.steps)
+        g_dec = _time_graph(lambda: ops.paged_decode_shared_prefix(
+            b.query, b.key_cache, b.value_cache, b.block_tables, b.context_lens, b.scale,
+            prefix_tokens, out=out), K, 3, dev)
+        g_dec_r = _time_graph(lambda: ops.paged_decode(
+            b.query, b.key_cache, b.value_cache, b.block_tables, b.context_lens, b.scale,
+            num_splits=nsplit, out=out), K, 3, dev)
+        step_s = make_step(True)
+        g_step = _time_graph(lambda: step_s(None), K, 3, dev)
+        t = torch.tensor([ms, dec_ms, ms_r, dec_r, g_dec, g_dec_r, g_step], device=dev)
         if ws > 1:
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, dec_ms, ms_r, dec_r = (float(x) for x in t)
+        ms, dec_ms, ms_r, dec_r, g_dec, g_dec_r, g_step = (float(x) for x in t)
         logical = decode_bytes(b.ctx, B)
         unique = b.key_cache.numel() * 2 * 2 + B * H * D * 4
         line = {"workload": "cfg4", "metric": METRIC, "n_gpus": ws, "steps": args.steps,
@@ -571,18 +603,22 @@ def measure_sub(workload, steps, warmup, ws, rank, local):
                            "+ a copy-on-write fork of the 128th (2048-token prefix) then 16 "
                            "private blocks; T=0.7 Gumbel-max (in-kernel Philox) over 151936",
                            "parallelism": f"request-sharded x{ws}"},
-                "ms_per_step": round(ms, 4), "sampled_tok_s": round(B * ws / (ms * 1e-3), 1),
-                "value": round(logical / (dec_ms * 1e-3) / 1e9, 1), "unit": "GB/s (logical)",
+                "ms_per_step": round(g_step, 4), "ms_per_step_eager": round(ms, 4),
+                "sampled_tok_s": round(B * ws / (g_step * 1e-3), 1),
+                "timing": "CUDA graphs of `steps` calls, replayed (device time); *_eager: "
+                          "the same calls one by one with events",
+                "value": round(logical / (g_dec * 1e-3) / 1e9, 1), "unit": "GB/s (logical)",
                 "decode": {"kernel": "paged_decode_shared_prefix (prefix on tensor cores + "
-                                     "suffix split decode)", "ms": round(dec_ms, 4),
-                           "logical_gbs": round(logical / (dec_ms * 1e-3) / 1e9, 1),
-                           "unique_gbs": round(unique / (dec_ms * 1e-3) / 1e9, 1),
+                                     "suffix split decode)", "ms": round(g_dec, 4),
+                           "ms_eager": round(dec_ms, 4),
+                           "logical_gbs": round(logical / (g_dec * 1e-3) / 1e9, 1),
+                           "unique_gbs": round(unique / (g_dec * 1e-3) / 1e9, 1),
                            "note": "logical = bytes a per-row decode reads; unique = bytes "
                                    "in the pool"},
                 "decode_per_row": {"kernel": "paged_decode (every row streams the prefix, "
-                                             "L2-resident)", "ms": round(dec_r, 4),
-                                   "step_ms": round(ms_r, 4),
-                                   "logical_gbs": round(logical / (dec_r * 1e-3) / 1e9, 1)}}
+                                             "L2-resident)", "ms": round(g_dec_r, 4),
+                                   "ms_eager": round(dec_r, 4), "step_ms_eager": round(ms_r, 4),
+                                   "logical_gbs": round(logical / (g_dec_r * 1e-3) / 1e9, 1)}}
     elif args.workload == "cfg5":
         # 64 sequences dealt to the ranks by context length (equal counts)
         lens = [workloads.context_len(5, 0, i) for i in range(64)]
@@ -702,32 +738,49 @@ def measure_sub(workload, steps, warmup, ws, rank, local):
                                          num_splits=nsplit, out=dout))
 
         ov_ms, _ = _time_events(stream, step_overlapped, args.steps, max(3, args.warmup))
-        t = torch.tensor([ms, pre_ms, dec_ms, ov_ms], device=dev)
+        # the same from CUDA graphs: the device's time alone (one ops call's host
+        # time, ~15-25 us, leaves the GPU idle between these short kernels)
+        K = max(8, args.steps)
+        g_pre = _time_graph(lambda: ops.paged_prefill(
+            pf.query, pf.key_cache, pf.value_cache, pf.cu_seqlens_q, 512, pf.scale,
+            block_tables=pf.block_tables, context_lens=pf.context_lens, out=pout), K, 3, dev)
+        g_dec = _time_graph(lambda: ops.paged_decode(
+            dec.query, dec.key_cache, dec.value_cache, dec.block_tables, dec.context_lens,
+            dec.scale, num_splits=nsplit, out=dout), K, 3, dev)
+        g_step = _time_graph(lambda: step(None), K, 3, dev)
+        g_ov = _time_graph(lambda: step_overlapped(None), K, 3, dev)
+        t = torch.tensor([ms, pre_ms, dec_ms, ov_ms, g_pre, g_dec, g_step, g_ov], device=dev)
         if ws > 1:
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, pre_ms, dec_ms, ov_ms = (float(x) for x in t)
+        ms, pre_ms, dec_ms, ov_ms, g_pre, g_dec, g_step, g_ov = (float(x) for x in t)
         flops = sum(4 * H * D * 512 * (p_ + (512 + 1) / 2) for p_ in prior)
         dec_b = decode_bytes(dec.ctx, 252)
-        tf = flops / (pre_ms * 1e-3) / 1e12
+        tf = flops / (g_pre * 1e-3) / 1e12
+        tf_eager = flops / (pre_ms * 1e-3) / 1e12
         line = {"workload": "cfg3", "metric": METRIC, "n_gpus": ws, "steps": args.steps,
                 "config": {"workload": "config 3: bf16 mixed step, Qwen3-8B attention (32 Q / 8 KV "
                            "heads, D=128): 4 prefill chunks of 512 on prior context "
                            f"{prior} + 252 decode sequences (context U[64,2048]); 2300 new "
                            "tokens stored; 65536-block pool", "parallelism": f"replica x{ws}"},
-                "ms_per_step": round(ms, 4), "unit": "TFLOP/s",
+                "ms_per_step": round(g_step, 4), "unit": "TFLOP/s",
                 "value": round(tf, 1),
-                "prefill": {"ms": round(pre_ms, 4), "tflops": round(tf, 1),
+                "timing": "CUDA graphs of `steps` calls, replayed (device time); the *_eager "
+                          "figures time the same calls one by one with events",
+                "prefill": {"ms": round(g_pre, 4), "tflops": round(tf, 1),
+                            "ms_eager": round(pre_ms, 4), "tflops_eager": round(tf_eager, 1),
                             "roofline": {"kernel": "paged_prefill_pp_kernel", "bound": "tensor",
                                          "achieved": round(tf, 1), "peak": peak_tf,
                                          "peak_source": f"{tf_kind} bf16 burst", "unit": "TFLOP/s",
                                          "frac": round(tf / peak_tf, 4)}},
-                "decode": {"ms": round(dec_ms, 4),
-                           "gbs": round(dec_b / (dec_ms * 1e-3) / 1e9, 1),
-                           "frac_of_hbm_peak": round(dec_b / (dec_ms * 1e-3) / 1e9 / peak_hbm, 4)},
-                "step_overlapped": {"ms": round(ov_ms, 4),
+                "decode": {"ms": round(g_dec, 4),
+                           "gbs": round(dec_b / (g_dec * 1e-3) / 1e9, 1),
+                           "frac_of_hbm_peak": round(dec_b / (g_dec * 1e-3) / 1e9 / peak_hbm, 4),
+                           "ms_eager": round(dec_ms, 4)},
+                "ms_per_step_eager": round(ms, 4),
+                "step_overlapped": {"ms": round(g_ov, 4), "ms_eager": round(ov_ms, 4),
                                     "note": "store, then prefill and decode on two streams "
                                             "(Attention.forward_mixed); ms_per_step runs them "
-                                            "one after the other to time each"}}
+                                            "one after the other"}}
     return line
 
 
