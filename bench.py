@@ -57,6 +57,9 @@ def parse():
     ap.add_argument("--num-splits", type=int, default=0, help="decode split-KV override (0=auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cfg5-seqs", type=int, default=64,
+                    help="config 5's global sequence count (64; fewer only for a small "
+                         "profiling case)")
     ap.add_argument("--no-sub", action="store_true",
                     help="skip the sub-records (sampler, cfg5, cfg3, cfg4) of the default line")
     ap.add_argument("--workload", default="cfg2",
@@ -621,7 +624,8 @@ def measure_sub(workload, steps, warmup, ws, rank, local):
                                    "logical_gbs": round(logical / (g_dec_r * 1e-3) / 1e9, 1)}}
     elif args.workload == "cfg5":
         # 64 sequences dealt to the ranks by context length (equal counts)
-        lens = [workloads.context_len(5, 0, i) for i in range(64)]
+        nseq = int(os.environ.get("BENCH_CFG5_SEQS", "64"))
+        lens = [workloads.context_len(5, 0, i) for i in range(nseq)]
         mine = balanced_shard(lens, ws, rank)
         B = len(mine)
         b = workloads.make_decode_batch(5, B, seed=0, first_seq=rank * 64,
@@ -670,14 +674,14 @@ def measure_sub(workload, steps, warmup, ws, rank, local):
             rates = [float(own)]
         dec_gbs = statistics.median(rates)
         line = {"workload": "cfg5", "metric": METRIC, "n_gpus": ws, "steps": args.steps,
-                "config": {"workload": "config 5: bf16 long-context decode, 64 sequences in total "
+                "config": {"workload": f"config 5: bf16 long-context decode, {nseq} sequences in total "
                            f"({B} per GPU), context U[32768,131072], 32 Q / 8 KV heads, D=128, "
                            "block 16, split-KV, + T=1.0 Gumbel-max sampler (in-kernel Philox) "
                            "over 151936", "parallelism": f"request-sharded x{ws}",
                            "l2": f"inputs larger than L2: {job_dec_b / ws / 1e9:.1f} GB of KV per GPU"},
                 "scaling": "strong",
                 "value": round(job_b / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-                "ms_per_step": round(ms, 4), "sampled_tok_s": round(64 / (ms * 1e-3), 1),
+                "ms_per_step": round(ms, 4), "sampled_tok_s": round(nseq / (ms * 1e-3), 1),
                 "decode_split_kv": nsplit,
                 "decode": {"ms": round(dec_ms, 4),
                            "job_gbs": round(job_dec_b / (dec_ms * 1e-3) / 1e9, 1)},
@@ -886,6 +890,7 @@ def _decode_launches(num_splits: int) -> int:
 
 def main():
     args = parse()
+    os.environ["BENCH_CFG5_SEQS"] = str(args.cfg5_seqs)
     ws, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, ws, rank)
