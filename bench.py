@@ -859,7 +859,8 @@ def measure_mma_rate(local, n_mma=8192):
     peak_tf, kind = measured_tflops()
     rec = {"n_mma": n_mma, "ctas": nsm}
     for shape, name, N in ((0, "ss_128x128x16", 128), (1, "ss_128x256x16", 256),
-                           (2, "ts_128x128x16", 128), (3, "ts_128x128x16_b_mn_major", 128)):
+                           (2, "ts_128x128x16", 128), (3, "ts_128x128x16_b_mn_major", 128),
+                           (4, "ss_128x128x16_b_mn_major", 128)):
         run = lambda: _lib.check(_lib.lib().lk_selftest_mma_rate(
             n_mma, shape, cycles.data_ptr(), status.data_ptr(), stream.cuda_stream))
         for _ in range(3):

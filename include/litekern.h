@@ -368,7 +368,8 @@ int lk_selftest_gumbel(float* out, const uint32_t* bits, int32_t n, void* stream
  * Tensor-core issue-rate self-test (no counterpart in the reference): one CTA
  * per SM issues n_mma back-to-back tcgen05.mma (bf16, fp32 accumulator in
  * TMEM, M = 128; shape 0: A and B in shared memory, N = 128; 1: N = 256;
- * 2: A in TMEM, N = 128; 3: A in TMEM and B N-major, the P.V form, N = 128)
+ * 2: A in TMEM, N = 128; 3: A in TMEM and B N-major, the P.V form, N = 128;
+ * 4: A in shared memory and B N-major, N = 128)
  * and writes the SM cycles from first issue to
  * completion to cycles[cta] (gridDim = number of SMs), -1 and
  * LK_STATUS_WAIT_TIMEOUT in *status if the completion wait (100 ms) ran out.

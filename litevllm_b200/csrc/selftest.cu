@@ -35,7 +35,8 @@ extern "C" int lk_selftest_wait_timeout(int32_t* status, uint64_t timeout_ns, vo
 // (bounded); cycles[cta] receives the SM clock cycles from the first issue to
 // the completion. Shapes: 0 = A and B from shared memory, N = 128; 1 = the
 // same with N = 256; 2 = A from TMEM, N = 128; 3 = A from TMEM, B N-major
-// (d contiguous, as the V tile of P.V), N = 128. The operands are whatever the
+// (d contiguous, as the V tile of P.V), N = 128; 4 = A from shared memory and
+// B N-major, N = 128. The operands are whatever the
 // shared memory and TMEM hold: only the rate is measured.
 namespace {
 
@@ -66,7 +67,11 @@ __global__ void __launch_bounds__(128) mma_rate_kernel(int n_mma, int shape, int
     for (int i = 0; i < n_mma; ++i) {
       const int ks = i & 3;  // the four K = 16 steps of one 64-wide swizzle atom
       const uint64_t bd = lk::tc::smem_desc_sw128(b_addr + ks * 32, 16, 1024);
-      if (shape == 3)  // the P.V form: B holds 16 keys x 128 d, d contiguous (MN-major)
+      if (shape == 4)  // A from shared memory, B N-major
+        lk::tc::mma_f16(tmem, lk::tc::smem_desc_sw128(a_addr + ks * 32, 16, 1024),
+                        lk::tc::smem_desc_sw128(b_addr + ks * 2048, 16384, 1024),
+                        lk::tc::idesc_f16(1, 0, 1, 128, 128), 1u);
+      else if (shape == 3)  // the P.V form: B holds 16 keys x 128 d, d contiguous (MN-major)
         lk::tc::mma_f16_ts(tmem, tmem + 256 + ks * 8,
                            lk::tc::smem_desc_sw128(b_addr + ks * 2048, 16384, 1024),
                            lk::tc::idesc_f16(1, 0, 1, 128, 128), 1u);
@@ -92,7 +97,7 @@ __global__ void __launch_bounds__(128) mma_rate_kernel(int n_mma, int shape, int
 
 extern "C" int lk_selftest_mma_rate(int32_t n_mma, int32_t shape, int64_t* cycles,
                                     int32_t* status, void* stream) {
-  if (!cycles || n_mma <= 0 || n_mma > (1 << 20) || shape < 0 || shape > 3)
+  if (!cycles || n_mma <= 0 || n_mma > (1 << 20) || shape < 0 || shape > 4)
     return LK_ERR_INVALID_ARG;
   static bool configured[64] = {false};
   int dev = 0;
