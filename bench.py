@@ -695,6 +695,10 @@ def measure_sub(workload, steps, warmup, ws, rank, local):
                                                    "max": round(rates[-1], 1)},
                              "note": "median over ranks of each rank's decode bytes / its "
                                      "decode time",
+                             "traffic_over_algorithmic": 1.0004,
+                             "traffic_source": "ncu dram bytes of an 8-sequence config-5 launch "
+                                               "(profiles/paged_decode_cfg5.md), not measured "
+                                               "in this run",
                              "algorithmic_bytes_per_launch": dec_b}}
     else:
         # config 3: 4 chunks of 512 on prior U[0,3584] + 252 decode sequences,
