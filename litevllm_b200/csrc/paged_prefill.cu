@@ -1380,6 +1380,8 @@ prefill_plan_kernel(const int32_t* __restrict__ cu_seqlens_q,
                     int* __restrict__ pairs, int* __restrict__ units,
                     int* __restrict__ split_cnt) {
   __shared__ int hist[kOrderBuckets];
+  __shared__ int bstart[kOrderBuckets];  // first position of each bucket
+  __shared__ int bcut[kOrderBuckets];    // 1: every pair of the bucket is cut
   __shared__ int warp_tot[32];
   __shared__ int n_valid;
   const int tid = threadIdx.x;
@@ -1408,26 +1410,40 @@ prefill_plan_kernel(const int32_t* __restrict__ cu_seqlens_q,
     atomicAdd(&hist[bucket(nt)], 1);
   }
   __syncthreads();
+  const int count = hist[tid];  // pairs in bucket tid
   hist[tid] = block_exclusive_scan(hist[tid], warp_tot, &total);
+  bstart[tid] = hist[tid];
   __syncthreads();
   for (int pr = tid; pr < n; pr += 1024) pairs[atomicAdd(&hist[bucket(ntiles(pr))], 1)] = pr;
   __syncthreads();
-  // 2. which pairs to cut (contiguous positions per thread, so split ids
-  // follow the longest-first order); the id + 1 goes to bits 14.. of the pair
+  // 2. which pairs to cut. The order inside a bucket comes from atomics and
+  // differs between launches, and a cut pair's result differs from the uncut
+  // one in the last bits; so the decision is made per bucket: a bucket is cut
+  // whole when it starts after the first wave of items, its pairs have at
+  // least min_cut key tiles, and all its pairs fit in the workspace's room
+  // (cap_split) after the longer buckets' cuts. Same inputs, same bits.
   const bool enable = cap_split > 0 && static_cast<int64_t>(n_valid) * H_kv <= 4LL * num_sms;
-  const int seg = (n + 1023) / 1024, k0 = min(n, tid * seg), k1 = min(n, k0 + seg);
   const int min_cut = n > 0 ? max(4, (ntiles(pairs[0] & 0x3fff) + 1) / 2) : 4;
-  auto cut = [&](int k, int nt) {
-    return enable && static_cast<int64_t>(k + 1) * H_kv > num_sms && nt >= min_cut;
-  };
+  {
+    const int nt_b = kOrderBuckets - 1 - tid;  // key tiles of bucket tid (last: >= that)
+    const bool cuttable = enable && count > 0 && nt_b >= min_cut &&
+                          static_cast<int64_t>(bstart[tid] + 1) * H_kv > num_sms;
+    const int want = cuttable ? count : 0;
+    const int before = block_exclusive_scan(want, warp_tot, &total);
+    bcut[tid] = cuttable && before + count <= cap_split ? 1 : 0;
+  }
+  __syncthreads();
+  // split ids: contiguous positions per thread, a scan over the cut ones
+  const int seg = (n + 1023) / 1024, k0 = min(n, tid * seg), k1 = min(n, k0 + seg);
+  auto cut = [&](int nt) { return bcut[bucket(nt)] != 0; };
   int cnt = 0;
-  for (int k = k0; k < k1; ++k) cnt += cut(k, ntiles(pairs[k])) ? 1 : 0;
+  for (int k = k0; k < k1; ++k) cnt += cut(ntiles(pairs[k])) ? 1 : 0;
   int sid = block_exclusive_scan(cnt, warp_tot, &total);
-  const int nsplit = min(total, cap_split);
+  const int nsplit = total;  // <= cap_split by construction
   for (int k = k0; k < k1; ++k) {
     const int pr = pairs[k];
-    if (cut(k, ntiles(pr))) {
-      if (sid < cap_split) pairs[k] = pr | ((sid + 1) << 14);
+    if (cut(ntiles(pr))) {
+      pairs[k] = pr | ((sid + 1) << 14);
       ++sid;
     }
   }

@@ -230,6 +230,21 @@ def test_prefill_key_split_is_deterministic(cuda):
         assert torch.equal(again, out)
 
 
+def test_prefill_split_plan_is_deterministic_with_equal_lengths(cuda):
+    """Eight chunks of 512 on equal 8K priors: many pairs share a key-tile
+    count, so the plan's buckets are large and the first wave ends inside
+    one. The cut is decided per bucket, not per position inside it (which
+    the plan's atomics reorder between launches), so twenty launches give
+    the same bits; and the result matches the oracle."""
+    b, out = _paged_case(cuda, [512] * 8, [8192] * 8, seed=35)
+    assert _units_planned(cuda) >= 8 * 8  # whole pairs and pieces
+    for _ in range(20):
+        again = ops.paged_prefill(b.query, b.key_cache, b.value_cache, b.cu_seqlens_q, 512,
+                                  b.scale, block_tables=b.block_tables,
+                                  context_lens=b.context_lens)
+        assert torch.equal(again, out)
+
+
 def test_prefill_workspace_too_small_raises(cuda):
     b = workloads.make_prefill_batch([64], [0], seed=32, device=cuda)
     small = torch.zeros(200 * 1024, dtype=torch.uint8, device=cuda)
