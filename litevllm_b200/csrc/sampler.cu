@@ -9,11 +9,19 @@
 // reproducible from a noise tensor, which torch.multinomial's is not.
 //
 // B200 design: the vocabulary of each row is cut into chunks, one CTA per
-// (chunk, row), so that even a handful of rows covers every SM. Each thread
-// streams 16-byte vectors (8 bf16 logits) with several loads in flight, keeps
-// a running (key, index) best, and the CTA reduces with warp shuffles then
-// shared memory. The last CTA of a row to finish (atomic counter, no
-// waiting) reduces the per-chunk winners and writes the int64 token id.
+// (chunk, row). Each thread streams 16-byte vectors (8 16-bit logits) with
+// several loads in flight, keeps a running (key, index) best, and the CTA
+// reduces with warp shuffles then shared memory. The last CTA of a row to
+// finish (atomic counter, no waiting) reduces the per-chunk winners and
+// writes the int64 token id; all-greedy rows with 2-8 chunks merge inside a
+// thread-block cluster instead. Three kernels share this frame:
+//   argmax_kernel  all-greedy 16-bit rows, HBM bound: few long chunks
+//                  (ceil(SMs / B) per row);
+//   gumbel_kernel  in-kernel-noise 16-bit rows, bound by instruction issue:
+//                  many chunks of ~8K elements so the CTA dispatcher balances
+//                  SMs whose speeds differ;
+//   sample_kernel  everything else (a noise tensor, fp32 logits, unaligned
+//                  rows), one wave of chunks.
 //
 // In-kernel noise (lk_philox.cuh): u = ((r >> 9) + 0.5) * 2^-23 with r from
 // Philox4x32-10 keyed by the 64-bit seed, counter (v / 4, b, offset_lo,
