@@ -842,7 +842,8 @@ def measure_sampler(steps, warmup, ws, local):
                      "frac_of_hbm_peak": round(gbs / peak, 4)}
         del bufs
     rec["gumbel_rng"]["bound"] = ("instruction issue: per element a quarter Philox4x32-10 "
-                                  "block, two hardware logarithms and the division")
+                                  "block; keys (Gumbel map, division) only for vectors "
+                                  "whose bound can beat the CTA's best")
     rec["timing"] = ("`steps` calls captured in one CUDA graph over 4 rotating buffers > L2, "
                      "replayed and timed with CUDA events")
     return rec

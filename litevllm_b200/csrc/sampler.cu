@@ -335,21 +335,17 @@ struct FastDiv {
   }
 };
 
-template <typename T>
-LK_DEVINL void gumbel_keys(const SampleParams& p, const FastDiv& dv, int b, int vv,
-                           const uint4& raw, float (&key)[8], float* drow) {
-  float f[8];
-  Load16<T>::cvt(raw, f);
+// The 8 keys of one 16-byte vector from its logits f and its two Philox
+// blocks r (words 0-3: elements vv..vv+3, 4-7: vv+4..vv+7).
+LK_DEVINL void gumbel_keys(const FastDiv& dv, int vv, const float (&f)[8], const U4 (&r)[2],
+                           float (&key)[8], float* drow) {
   float g[8];
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    const U4 r = lk::philox4x32_10(
-        U4{static_cast<uint32_t>((vv >> 2) + h), static_cast<uint32_t>(b), p.off_lo, p.off_hi},
-        p.key);
-    g[4 * h + 0] = lk::gumbel_from_bits(r.x);
-    g[4 * h + 1] = lk::gumbel_from_bits(r.y);
-    g[4 * h + 2] = lk::gumbel_from_bits(r.z);
-    g[4 * h + 3] = lk::gumbel_from_bits(r.w);
+    g[4 * h + 0] = lk::gumbel_from_bits(r[h].x);
+    g[4 * h + 1] = lk::gumbel_from_bits(r[h].y);
+    g[4 * h + 2] = lk::gumbel_from_bits(r[h].z);
+    g[4 * h + 3] = lk::gumbel_from_bits(r[h].w);
   }
   if (drow) {
     reinterpret_cast<float4*>(drow + vv)[0] = make_float4(g[0], g[1], g[2], g[3]);
@@ -370,6 +366,18 @@ LK_DEVINL void gumbel_keys(const SampleParams& p, const FastDiv& dv, int b, int 
   for (int e = 0; e < 8; ++e) key[e] = __fadd_rn(q[e], g[e]);
 }
 
+// fp32 <-> int with the same order (for atomicMax on keys); NaN (positive
+// sign bit clear) maps above +infinity.
+LK_DEVINL int float_to_ordered(float x) {
+  const int i = __float_as_int(x);
+  return i >= 0 ? i : i ^ 0x7fffffff;
+}
+LK_DEVINL float ordered_to_float(int i) { return __int_as_float(i >= 0 ? i : i ^ 0x7fffffff); }
+
+// Margin added to the vector bound's Gumbel value: the map is within 2e-5
+// of the exact, monotone -ln(-ln u) everywhere (tested over all uniforms),
+// so g(u_e) <= g(u_max) + 4e-5 for every element of the vector.
+constexpr float kGumbelBoundMargin = 1e-3f;
 
 // ---------------------------------------------------- softmax(x / T) ---
 template <typename T>
@@ -704,56 +712,85 @@ __global__ void __launch_bounds__(kSampThreads) argmax_bulk_kernel(const SampleP
 
 // One row segment [j0, j1) of 16-byte vectors (plus, with tail, the row's
 // V % 8 ragged elements) of an in-kernel-noise row.
+//
+// Without a noise dump, most vectors need no keys: each key fl(fl(x / T) + g)
+// is at most fl(fl(x_max / T) + g(u_max) + margin) — division, the Gumbel map
+// and rounding are monotone, and the map's error is far below the margin —
+// so a vector whose bound is below a key already reached in this CTA cannot
+// hold the row's winner (nor tie it) and is skipped after its Philox words.
+// A NaN logit makes the bound NaN: its vector is always computed (a NaN key
+// wins). With a noise dump every key is computed.
 template <typename T>
 LK_DEVINL void gumbel_segment(const SampleParams& p, int b, int j0, int j1, bool tail, float temp,
                               float& best, int& besti) {
   const T* row = static_cast<const T*>(p.logits) + static_cast<int64_t>(b) * p.ld;
   const int nv = p.nv;
-      float* drow = p.noise_dump ? p.noise_dump + static_cast<int64_t>(b) * p.V : nullptr;
-      const FastDiv dv = FastDiv::make(temp);
-      // Each thread takes vectors j, j + 256, ... of the segment, loading two
-      // before computing them; a vector's keys are compared once through
-      // their NaN-propagating max, and only a vector that improves the
-      // running best is searched for the element (rare after the first few).
-      // Measured against computing two vectors before comparing either and
-      // loading the next two ahead: that form ran 10 % slower here.
-      const uint4* rowv = reinterpret_cast<const uint4*>(row);
-      auto consider = [&](const uint4& raw, int j) {
-        float k[8];
-        gumbel_keys<T>(p, dv, b, j * kVec, raw, k, drow);
-        const float m = fmax_nan(fmax_nan(fmax_nan(k[0], k[1]), fmax_nan(k[2], k[3])),
-                                 fmax_nan(fmax_nan(k[4], k[5]), fmax_nan(k[6], k[7])));
-        if (beats_later(m, best)) {
-          const bool want_nan = m != m;
-          int e = 7;
+  float* drow = p.noise_dump ? p.noise_dump + static_cast<int64_t>(b) * p.V : nullptr;
+  const FastDiv dv = FastDiv::make(temp);
+  const uint4* rowv = reinterpret_cast<const uint4*>(row);
+  // The CTA's best key so far, as an order-preserving int (a NaN key maps
+  // above every number).
+  __shared__ int s_best;
+  if (threadIdx.x == 0) s_best = float_to_ordered(-INFINITY);
+  __syncthreads();
+
+  // the largest noise the map gives (every bit set), plus the margin
+  const float g_cap = lk::gumbel_from_bits(0xffffffffu) + kGumbelBoundMargin;
+
+  for (int j = j0 + threadIdx.x; j < j1; j += kSampThreads) {
+    const int vv = j * kVec;
+    const uint4 raw = __ldcs(rowv + j);
+    float f[8];
+    Load16<T>::cvt(raw, f);
+    float qm = 0.f, thr = 0.f;
+    if (!drow) {
+      // logits alone: even the largest noise cannot lift this vector to the
+      // best key, so its Philox blocks are not needed either
+      const float xm = fmax_nan(fmax_nan(fmax_nan(f[0], f[1]), fmax_nan(f[2], f[3])),
+                                fmax_nan(fmax_nan(f[4], f[5]), fmax_nan(f[6], f[7])));
+      qm = dv.in_range(xm) ? dv.fast(xm) : __fdiv_rn(xm, dv.t);
+      thr = fmaxf(best, ordered_to_float(*static_cast<volatile int*>(&s_best)));
+      if (__fadd_rn(qm, g_cap) < thr) continue;
+    }
+    U4 r[2];
 #pragma unroll
-          for (int q = 7; q >= 0; --q) e = (want_nan ? k[q] != k[q] : k[q] == m) ? q : e;
-          best = m;
-          besti = j * kVec + e;
-        }
-      };
-      int j = j0 + threadIdx.x;
-      for (; j + kSampThreads < j1; j += 2 * kSampThreads) {
-        const uint4 r0 = __ldcs(rowv + j), r1 = __ldcs(rowv + j + kSampThreads);
-        consider(r0, j);
-        consider(r1, j + kSampThreads);
+    for (int h = 0; h < 2; ++h)
+      r[h] = lk::philox4x32_10(
+          U4{static_cast<uint32_t>((vv >> 2) + h), static_cast<uint32_t>(b), p.off_lo, p.off_hi},
+          p.key);
+    if (!drow) {
+      const uint32_t rm = max(max(max(r[0].x, r[0].y), max(r[0].z, r[0].w)),
+                              max(max(r[1].x, r[1].y), max(r[1].z, r[1].w)));
+      if (__fadd_rn(qm, lk::gumbel_from_bits(rm) + kGumbelBoundMargin) < thr) continue;
+    }
+    float k[8];
+    gumbel_keys(dv, vv, f, r, k, drow);
+    const float m = fmax_nan(fmax_nan(fmax_nan(k[0], k[1]), fmax_nan(k[2], k[3])),
+                             fmax_nan(fmax_nan(k[4], k[5]), fmax_nan(k[6], k[7])));
+    const bool want_nan = m != m;
+    int e = 7;
+#pragma unroll
+    for (int qq = 7; qq >= 0; --qq) e = (want_nan ? k[qq] != k[qq] : k[qq] == m) ? qq : e;
+    if (beats(m, vv + e, best, besti)) {
+      best = m;
+      besti = vv + e;
+      if (!drow) atomicMax(&s_best, float_to_ordered(m));
+    }
+  }
+  if (tail) {  // the row's ragged tail (indices above every vector's)
+    for (int t = nv * kVec + threadIdx.x; t < p.V; t += kSampThreads) {
+      const U4 r = lk::philox4x32_10(
+          U4{static_cast<uint32_t>(t >> 2), static_cast<uint32_t>(b), p.off_lo, p.off_hi}, p.key);
+      const uint32_t w = (t & 3) == 0 ? r.x : (t & 3) == 1 ? r.y : (t & 3) == 2 ? r.z : r.w;
+      const float g = lk::gumbel_from_bits(w);
+      if (drow) drow[t] = g;
+      const float key = __fadd_rn(__fdiv_rn(lk::Elem<T>::to_f(row[t]), temp), g);
+      if (beats(key, t, best, besti)) {
+        best = key;
+        besti = t;
       }
-      if (j < j1) consider(__ldcs(rowv + j), j);
-      if (tail) {  // the row's ragged tail
-        for (int t = nv * kVec + threadIdx.x; t < p.V; t += kSampThreads) {
-          const U4 r = lk::philox4x32_10(
-              U4{static_cast<uint32_t>(t >> 2), static_cast<uint32_t>(b), p.off_lo, p.off_hi},
-              p.key);
-          const uint32_t w = (t & 3) == 0 ? r.x : (t & 3) == 1 ? r.y : (t & 3) == 2 ? r.z : r.w;
-          const float g = lk::gumbel_from_bits(w);
-          if (drow) drow[t] = g;
-          const float key = __fadd_rn(__fdiv_rn(lk::Elem<T>::to_f(row[t]), temp), g);
-          if (beats_later(key, best)) {
-            best = key;
-            besti = t;
-          }
-        }
-      }
+    }
+  }
 }
 
 // Grid (chunk, row): each CTA takes one chunk of a row's vectors (the last
@@ -934,20 +971,31 @@ int launch_sample(const SampleParams& p, int B, bool vec, cudaStream_t s) {
   return e == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 
-// gumbel_kernel's chunk: vectors per thread per CTA (LITEKERN_GUMBEL_VPT,
-// read once; default 4), so chunks of 8 * 256 * vpt elements.
-int gumbel_vpt() {
+// gumbel_kernel's chunks per row; the row's vectors are split evenly over
+// them. Long chunks let a CTA's running best skip more vectors; small batches
+// still need enough CTAs to reach the SMs. The rule: at least 4 chunks a row
+// and about 256 CTAs in all, no chunk under one vector per thread. Measured
+// from a CUDA graph at V = 151936, T = 0.7, best count per batch (us): B = 1
+// 74 chunks (5.5), 16 16 (9.7), 32 8 (13.0), 64 4 (20.9; 9 chunks 20.0),
+// 128 4 (33.1; 6 chunks 32.8), 256 4 (52.3); 2 chunks or 16+ chunks at
+// B >= 128 were 3-40 % slower. LITEKERN_GUMBEL_CHUNKS (read once) fixes it.
+int gumbel_chunks_env() {
   static int v = [] {
-    const char* e = getenv("LITEKERN_GUMBEL_VPT");
-    const int x = e ? atoi(e) : 4;
-    return x >= 1 && x <= 64 ? x : 4;
+    const char* e = getenv("LITEKERN_GUMBEL_CHUNKS");
+    const int x = e ? atoi(e) : 0;
+    return x >= 1 && x <= 4096 ? x : 0;
   }();
   return v;
 }
 bool use_gumbel(int V, bool vec, bool rng) { return rng && vec && V >= kVec && !gumbel_generic(); }
-int gumbel_chunks(int V) {
-  const int cv = gumbel_vpt() * kSampThreads;
-  return std::max(1, (V / kVec + cv - 1) / cv);
+int gumbel_chunks(int B, int V) {
+  const int64_t nvr = V / kVec;
+  int64_t n = gumbel_chunks_env();
+  if (n == 0) {
+    n = std::max<int64_t>(4, (256 + B - 1) / B);
+    n = std::min<int64_t>(n, std::max<int64_t>(1, nvr / kSampThreads));
+  }
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(n, nvr)));
 }
 
 // Chunks (CTAs) per row for one call: all-greedy 16-bit rows reduce their
@@ -968,7 +1016,7 @@ int chunks_for(int B, int V, bool vec, bool greedy_only, bool rng) {
     if (sample_cluster()) n = std::min<int64_t>(n, kMaxCluster);
     return static_cast<int>(std::max<int64_t>(1, n));
   }
-  if (use_gumbel(V, vec, rng)) return gumbel_chunks(V);
+  if (use_gumbel(V, vec, rng)) return gumbel_chunks(B, V);
   return choose_chunks(B, V);
 }
 
@@ -998,10 +1046,10 @@ int prepare(SampleParams& p, bool& vec, int64_t* out_ids, const void* logits, in
                          temperatures != nullptr && noise == nullptr);
   if (use_gumbel(V, vec, temperatures != nullptr && noise == nullptr)) {
     // whole vectors per chunk; the ragged tail joins the last chunk
-    int64_t cv = static_cast<int64_t>(gumbel_vpt()) * kSampThreads;
     const int64_t nvr = V / kVec;
     const int64_t nmax = std::max<int64_t>(1, max_partials / B);
-    if ((nvr + cv - 1) / cv > nmax) cv = (nvr + nmax - 1) / nmax;  // fewer, longer chunks
+    const int64_t n = std::min<int64_t>(gumbel_chunks(B, V), nmax);
+    const int64_t cv = (nvr + n - 1) / n;  // even split; the last chunk may be shorter
     p.chunk = static_cast<int>(cv * kVec);
     p.nchunks = static_cast<int>((nvr + cv - 1) / cv);
     p.gumbel = 1;
@@ -1035,7 +1083,7 @@ int launch(const SampleParams& p, int B, bool vec, int32_t dtype, cudaStream_t s
 }
 
 // Largest chunk count any call shape (B, V) can take: the workspace covers it.
-int max_chunks(int B, int V) { return std::max(choose_chunks(B, V), gumbel_chunks(V)); }
+int max_chunks(int B, int V) { return std::max(choose_chunks(B, V), gumbel_chunks(B, V)); }
 
 }  // namespace
 

@@ -301,3 +301,27 @@ def test_in_kernel_noise_edge_values(cuda):
     want = osamp.gumbel(x.float().numpy(), t.numpy(), dump.cpu().numpy())
     assert np.array_equal(ids, want), (ids, want)
     assert ids[1] == 0 and ids[2] == 777 and ids[3] == 1234
+
+
+@pytest.mark.parametrize("B,V,T,spread", [(128, 151936, 0.7, 1.0), (64, 151936, 1.0, 1.0),
+                                          (16, 32000, 0.05, 1.0), (8, 4096, 30.0, 1.0),
+                                          (32, 151936, 0.7, 8.0), (8, 128256, 1.0, 20.0)])
+def test_in_kernel_noise_vector_skip_is_exact(cuda, B, V, T, spread):
+    """Without a noise dump the kernel skips vectors whose key bound cannot beat
+    the running best (wide logit spreads also skip the noise of most vectors);
+    with a dump it computes every key. Same (seed, offset): the same ids, equal
+    to the oracle's given the dumped noise — planted masks, ties and NaN
+    included."""
+    x = (workloads.make_logits(4, B, V, seed=B + V, device=cuda).float() * spread).to(torch.bfloat16)
+    x[0, ::3] = float("-inf")
+    x[1, 100] = x[1, V - 50] = x[1].max() + 2   # a tie in logits far apart
+    x[2, V // 2] = float("nan")
+    t = torch.full((B,), T, device=cuda)
+    for offset in (1, 2):
+        dump = torch.zeros((B, V), device=cuda)
+        full = ops.sample(x, t, seed=77, offset=offset, noise_dump=dump)
+        skip = ops.sample(x, t, seed=77, offset=offset)
+        assert torch.equal(full, skip)
+        want = osamp.gumbel(x.float().cpu().numpy(), t.cpu().numpy(), dump.cpu().numpy())
+        assert np.array_equal(skip.cpu().numpy(), want)
+        assert int(skip[2]) == V // 2
