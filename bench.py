@@ -865,7 +865,12 @@ def measure_mma_rate(local, n_mma=8192):
     rec = {"n_mma": n_mma, "ctas": nsm}
     for shape, name, N in ((0, "ss_128x128x16", 128), (1, "ss_128x256x16", 256),
                            (2, "ts_128x128x16", 128), (3, "ts_128x128x16_b_mn_major", 128),
-                           (4, "ss_128x128x16_b_mn_major", 128)):
+                           (4, "ss_128x128x16_b_mn_major", 128), (5, "ss_128x128x16_b_sw32", 128),
+                           (6, "ss_128x128x16_ab_sw32", 128), (7, "ss_128x256x16_b_sw32", 256),
+                           (8, "rot_ss_128x128x16", 128), (9, "rot_ss_128x256x16", 256),
+                           (10, "rot_ts_128x128x16", 128), (11, "rot_ts_128x128x16_b_mn_major", 128),
+                           (12, "rot_ss_128x128x16_b_mn_major", 128),
+                           (13, "rot_ss_128x128x16_b_sw32", 128)):
         run = lambda: _lib.check(_lib.lib().lk_selftest_mma_rate(
             n_mma, shape, cycles.data_ptr(), status.data_ptr(), stream.cuda_stream))
         for _ in range(3):

@@ -369,7 +369,10 @@ int lk_selftest_gumbel(float* out, const uint32_t* bits, int32_t n, void* stream
  * per SM issues n_mma back-to-back tcgen05.mma (bf16, fp32 accumulator in
  * TMEM, M = 128; shape 0: A and B in shared memory, N = 128; 1: N = 256;
  * 2: A in TMEM, N = 128; 3: A in TMEM and B N-major, the P.V form, N = 128;
- * 4: A in shared memory and B N-major, N = 128)
+ * 4: A in shared memory and B N-major, N = 128; 5: as 0 with B in the
+ * 32-byte swizzle; 6: as 0 with A and B in the 32-byte swizzle; 7: as 1 with B
+ * in the 32-byte swizzle; 8-15: shapes 0-7 with consecutive MMAs rotating
+ * over independent accumulators, 4 for N = 128 with A in shared memory, else 2)
  * and writes the SM cycles from first issue to
  * completion to cycles[cta] (gridDim = number of SMs), -1 and
  * LK_STATUS_WAIT_TIMEOUT in *status if the completion wait (100 ms) ran out.

@@ -301,6 +301,14 @@ LK_DEVINL uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t 
          (static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
 
+// Shared-memory matrix descriptor with a 32-byte swizzle, K-major: a K = 16
+// (32-byte) slice of R rows is one contiguous R x 32-byte block, 8-row groups
+// sbo_bytes apart (256 when packed); the leading offset is unused.
+LK_DEVINL uint64_t smem_desc_sw32(uint32_t saddr, uint32_t sbo_bytes) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) |
+         (static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (6ull << 61);
+}
+
 // Instruction descriptor for kind::f16 with fp32 accumulation.
 // fmt: 0 = f16, 1 = bf16 (A and B the same type); major: 0 = K-major, 1 = MN-major.
 LK_DEVINL constexpr uint32_t idesc_f16(int fmt, int a_major, int b_major, int M, int N) {

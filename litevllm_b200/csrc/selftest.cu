@@ -60,26 +60,42 @@ __global__ void __launch_bounds__(128) mma_rate_kernel(int n_mma, int shape, int
   __syncthreads();
   lk::tc::fence_after();
   const uint32_t tmem = tmem_slot;
-  const int N = shape == 1 ? 256 : 128;
+  // shapes 8-15: shapes 0-7 with consecutive MMAs rotating over independent
+  // accumulators (4 for N = 128 from shared memory, 2 otherwise), so no MMA
+  // waits for the previous one's result
+  const bool rotate = shape >= 8;
+  shape &= 7;
+  const int N = (shape == 1 || shape == 7) ? 256 : 128;
+  const bool a_tmem = shape == 2 || shape == 3;
+  const int nacc = !rotate ? 1 : (N == 128 && !a_tmem) ? 4 : 2;
   if (threadIdx.x == 0) {
     const uint32_t idesc = lk::tc::idesc_f16(1, 0, 0, 128, N);
     const long long t0 = clock64();
     for (int i = 0; i < n_mma; ++i) {
       const int ks = i & 3;  // the four K = 16 steps of one 64-wide swizzle atom
+      const uint32_t d = tmem + static_cast<uint32_t>((i % nacc) * N);
       const uint64_t bd = lk::tc::smem_desc_sw128(b_addr + ks * 32, 16, 1024);
-      if (shape == 4)  // A from shared memory, B N-major
-        lk::tc::mma_f16(tmem, lk::tc::smem_desc_sw128(a_addr + ks * 32, 16, 1024),
+      if (shape == 5)  // B K-major with a 32-byte swizzle: each K step one 4 KiB block
+        lk::tc::mma_f16(d, lk::tc::smem_desc_sw128(a_addr + ks * 32, 16, 1024),
+                        lk::tc::smem_desc_sw32(b_addr + ks * 4096, 256), idesc, 1u);
+      else if (shape == 6)  // A and B K-major with a 32-byte swizzle
+        lk::tc::mma_f16(d, lk::tc::smem_desc_sw32(a_addr + ks * 4096, 256),
+                        lk::tc::smem_desc_sw32(b_addr + ks * 4096, 256), idesc, 1u);
+      else if (shape == 7)  // N = 256, B with a 32-byte swizzle (8 KiB per K step)
+        lk::tc::mma_f16(d, lk::tc::smem_desc_sw128(a_addr + ks * 32, 16, 1024),
+                        lk::tc::smem_desc_sw32(b_addr + ks * 8192, 256), idesc, 1u);
+      else if (shape == 4)  // A from shared memory, B N-major
+        lk::tc::mma_f16(d, lk::tc::smem_desc_sw128(a_addr + ks * 32, 16, 1024),
                         lk::tc::smem_desc_sw128(b_addr + ks * 2048, 16384, 1024),
                         lk::tc::idesc_f16(1, 0, 1, 128, 128), 1u);
       else if (shape == 3)  // the P.V form: B holds 16 keys x 128 d, d contiguous (MN-major)
-        lk::tc::mma_f16_ts(tmem, tmem + 256 + ks * 8,
+        lk::tc::mma_f16_ts(d, tmem + 256 + ks * 8,
                            lk::tc::smem_desc_sw128(b_addr + ks * 2048, 16384, 1024),
                            lk::tc::idesc_f16(1, 0, 1, 128, 128), 1u);
       else if (shape == 2)
-        lk::tc::mma_f16_ts(tmem, tmem + 256 + ks * 8, bd, idesc, 1u);
+        lk::tc::mma_f16_ts(d, tmem + 256 + ks * 8, bd, idesc, 1u);
       else
-        lk::tc::mma_f16(tmem, lk::tc::smem_desc_sw128(a_addr + ks * 32, 16, 1024), bd, idesc,
-                        1u);
+        lk::tc::mma_f16(d, lk::tc::smem_desc_sw128(a_addr + ks * 32, 16, 1024), bd, idesc, 1u);
     }
     lk::tc::commit(&done);
     const bool ok = lk::mbar_wait(&done, 0, 100000000ull);  // 100 ms
@@ -97,7 +113,7 @@ __global__ void __launch_bounds__(128) mma_rate_kernel(int n_mma, int shape, int
 
 extern "C" int lk_selftest_mma_rate(int32_t n_mma, int32_t shape, int64_t* cycles,
                                     int32_t* status, void* stream) {
-  if (!cycles || n_mma <= 0 || n_mma > (1 << 20) || shape < 0 || shape > 4)
+  if (!cycles || n_mma <= 0 || n_mma > (1 << 20) || shape < 0 || shape > 15)
     return LK_ERR_INVALID_ARG;
   static bool configured[64] = {false};
   int dev = 0;

@@ -40,11 +40,11 @@ def test_mma_rate_selftest_completes(cuda):
     nsm = torch.cuda.get_device_properties(cuda).multi_processor_count
     cycles = torch.zeros(nsm, dtype=torch.int64, device=cuda)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
-    for shape in (0, 1, 2, 3, 4):
+    for shape in range(16):
         rc = _lib.lib().lk_selftest_mma_rate(256, shape, cycles.data_ptr(), status.data_ptr(),
                                             None)
         assert rc == 0
         torch.cuda.synchronize()
         assert int(status.item()) == 0 and (cycles > 0).all()
     assert _lib.lib().lk_selftest_mma_rate(0, 0, cycles.data_ptr(), None, None) == -1
-    assert _lib.lib().lk_selftest_mma_rate(16, 5, cycles.data_ptr(), None, None) == -1
+    assert _lib.lib().lk_selftest_mma_rate(16, 16, cycles.data_ptr(), None, None) == -1
