@@ -157,7 +157,11 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
   // for it (and through it for the KV store) before reading anything. The
   // kernel after this one (the sampler) may then start launching: its blocks
   // wait for this grid to complete, and take SMs as the last wave drains.
-  lk::pdl_wait();
+  // Shared-prefix mode (part_offset > 0): the grid ahead is the prefix kernel,
+  // a plain launch behind the ordering kernel and the store, so everything
+  // but the prefix partials is complete once this grid starts; the wait
+  // moves to the merge, which reads those partials.
+  if (p.part_offset == 0) lk::pdl_wait();
   lk::pdl_launch_dependents();
   int2 unit;
   if (p.order != nullptr) {
@@ -439,6 +443,7 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
   }
   __syncthreads();
   if (!s_last) return;
+  if (p.part_offset > 0) lk::pdl_wait();  // the prefix kernel's partials
   __threadfence();
   const int nq = HPC * G;
   const int qbase = hg * nq;
@@ -1561,7 +1566,10 @@ PrefixPlan prefix_plan(int B, int H_kv, int max_blocks, int block_size, int pref
   const int rows_per_item = 256 / G;  // query rows of one prefix work item
   const int items_per_range = ((B + rows_per_item - 1) / rows_per_item) * H_kv;
   const int tiles = (prefix_tokens + 127) / 128;
-  int ranges = sms / (items_per_range > 0 ? items_per_range : 1);
+  // About half the SMs: the suffix decode runs beside the prefix kernel on the
+  // rest (measured on config 4, decode step: 8 ranges on 128 SMs 54.8 us, 4
+  // on 64 SMs 50.7, 2 on 32 SMs 61.6).
+  int ranges = sms / (2 * (items_per_range > 0 ? items_per_range : 1));
   static const int ranges_env = [] {
     const char* e = getenv("LITEKERN_PREFIX_RANGES");
     return e ? atoi(e) : 0;

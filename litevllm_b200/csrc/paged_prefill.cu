@@ -862,6 +862,16 @@ paged_prefill_pp_kernel(const __grid_constant__ CUtensorMap kmap,
   __syncthreads();
   lk::tc::fence_after();
   const uint32_t tmem = tmem_slot;
+  if constexpr (PREFIX) {
+    // Launched to overlap the ordering kernel ahead of it (the set-up above
+    // touches no global memory): wait for it, and through it for the step's
+    // KV store. Then the split decode kernel launched after this one may
+    // start on the SMs this grid leaves free: everything it reads first is
+    // complete by now, and it waits for this grid before merging in the
+    // prefix partials.
+    lk::pdl_wait();
+    lk::pdl_launch_dependents();
+  }
   // Consumers: the n-th item this CTA processes (num_items = no more work).
   // Lane 0 waits, reads and releases the slot; the result goes to all lanes.
   auto next_item = [&](int n, bool& ok) -> int {
@@ -1635,8 +1645,9 @@ int launch_prefix_pp(const CUtensorMap& km, const CUtensorMap& vm, PrefillParams
     if (cudaMemsetAsync(p.sched, 0, sizeof(int), s) != cudaSuccess) return LK_ERR_CUDA;
   }
   const int grid = static_cast<int>(items < lk::num_sms() ? items : lk::num_sms());
-  paged_prefill_pp_kernel<T, true><<<grid, kPpThreads, kPpSmem, s>>>(km, vm, p);
-  return lk::check_launch();
+  const cudaError_t e = lk::launch_after_previous(paged_prefill_pp_kernel<T, true>, dim3(grid),
+                                                  dim3(kPpThreads), kPpSmem, s, km, vm, p);
+  return e == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 
 // Prefill kernel choice: the two-sub-tile ping-pong kernel by default;
