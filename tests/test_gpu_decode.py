@@ -302,6 +302,44 @@ def test_attention_forward_uses_the_shared_prefix_hint(cuda):
     assert torch.equal(again, plain)
 
 
+def test_shared_prefix_decode_back_to_back_is_exact(cuda):
+    """The suffix decode starts beside the prefix kernel and waits for it only
+    before merging the prefix partials. Back-to-back calls alternating two
+    query tensors (eagerly and from a CUDA graph) must each give the bits of
+    a call made alone: a merge that read the other call's partials, or this
+    call's before they were written, would not."""
+    b = workloads.make_prefix_batch(128, seed=5, device=cuda)
+    q2 = torch.flip(b.query, dims=[0]).contiguous()
+    args = (b.key_cache, b.value_cache, b.block_tables, b.context_lens, b.scale, 127 * 16)
+    want = []
+    for q in (b.query, q2):
+        want.append(ops.paged_decode_shared_prefix(q, *args).clone())
+        torch.cuda.synchronize()
+    outs = [torch.empty_like(b.query) for _ in range(16)]
+    for i, o in enumerate(outs):
+        ops.paged_decode_shared_prefix(b.query if i % 2 == 0 else q2, *args, out=o)
+    torch.cuda.synchronize()
+    for i, o in enumerate(outs):
+        assert torch.equal(o, want[i % 2]), i
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i, o in enumerate(outs):  # warm-up on the capture stream
+            ops.paged_decode_shared_prefix(b.query if i % 2 == 0 else q2, *args, out=o)
+        with torch.cuda.graph(g, stream=s):
+            for i, o in enumerate(outs):
+                ops.paged_decode_shared_prefix(b.query if i % 2 == 0 else q2, *args, out=o)
+    torch.cuda.current_stream().wait_stream(s)
+    for o in outs:
+        o.zero_()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    for i, o in enumerate(outs):
+        assert torch.equal(o, want[i % 2]), i
+
+
 def test_shared_prefix_longer_than_a_row_is_flagged(cuda):
     q, kc, vc, bt, ctx = _shared_prefix_batch(cuda, 6, 10, [5, 40, 0, 7, 9, 30], seed=12)
     ctx[2] = 100  # shorter than the declared 160-token prefix
