@@ -259,6 +259,11 @@ def run_ours(args, ws, rank, local):
         torch.distributed.barrier()
     torch.cuda.synchronize(dev)
     with ClockSampler(local) as clk:
+        # ~0.5 ms of device sleep ahead of the start event: the host enqueues
+        # the first steps meanwhile, so a short run does not time the host's
+        # first launches on an idle GPU (a host slower than the GPU in steady
+        # state still drains the queue and shows in the time)
+        torch.cuda._sleep(1_000_000)
         t0.record(stream)
         h0 = time.perf_counter()
         for i in range(K):
