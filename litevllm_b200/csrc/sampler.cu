@@ -18,8 +18,9 @@
 //   argmax_kernel  all-greedy 16-bit rows, HBM bound: few long chunks
 //                  (ceil(SMs / B) per row);
 //   gumbel_kernel  in-kernel-noise 16-bit rows, bound by instruction issue:
-//                  many chunks of ~8K elements so the CTA dispatcher balances
-//                  SMs whose speeds differ;
+//                  max(4, ceil(256 / B)) equal chunks per row; vectors whose
+//                  key bound cannot beat the CTA's best key are skipped
+//                  (exactly), most of them right after their Philox words;
 //   sample_kernel  everything else (a noise tensor, fp32 logits, unaligned
 //                  rows), one wave of chunks.
 //
@@ -301,8 +302,9 @@ __global__ void __launch_bounds__(kSampThreads, kSampCtasPerSm) sample_kernel(co
 
 // In-kernel-noise rows of 16-bit logits (16-byte aligned rows, gumbel_kernel
 // below): the sampled path of config 4 / 5. It is bound by instruction issue, not HBM: per
-// element a quarter Philox block, two hardware logarithms and the division,
-// so every step here is trimmed to few instructions:
+// element a quarter Philox block, and for the few vectors whose key bound can
+// beat the CTA's best (gumbel_segment) two hardware logarithms and the
+// division, so every step here is trimmed to few instructions:
 //  * Philox round keys arrive as kernel parameters (constant operands);
 //  * x / T is the IEEE quotient computed as in Markstein's theorem (P.
 //    Markstein, "Computation of elementary functions on the IBM RISC
@@ -821,11 +823,13 @@ LK_DEVINL void gumbel_segment(const SampleParams& p, int b, int j0, int j1, bool
   }
 }
 
-// Grid (chunk, row): each CTA takes one chunk of a row's vectors (the last
-// chunk also the ragged tail). The compute-bound loop makes the SMs' speeds
-// differ by ~15 %, so many chunks of a few vectors per thread (several waves)
-// let the hardware's CTA dispatch balance them; a static cut of the batch
-// into one CTA per resident slot ran 20 % slower for that reason.
+// Grid (chunk, row): each CTA takes one of the row's equal chunks of vectors
+// (the last chunk also the ragged tail); gumbel_chunks sets how many. Long
+// chunks let the CTA's running best skip more vectors, so large batches take
+// 4 chunks a row (under one wave); small ones take more to reach the SMs.
+// Measured slower: a static cut of the batch into one equal range per
+// resident slot, crossing row boundaries (the SMs' speeds differ on this
+// compute-bound loop), and a persistent grid pulling items from a counter.
 template <typename T>
 __global__ void __launch_bounds__(kSampThreads, kGumbelCtasPerSm) gumbel_kernel(const SampleParams p) {
   lk::pdl_wait();  // launched to overlap the kernel ahead of it: wait for it before reading
