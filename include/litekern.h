@@ -133,8 +133,10 @@ int lk_paged_decode(void* out, int64_t out_token_stride,
  * block_size, G in {1, 2, 4, 8}. workspace: at least
  * lk_paged_decode_shared_prefix_workspace_bytes(...) bytes, 256-byte aligned,
  * zero-filled before first use (the same reuse rules as lk_paged_decode).
- * Launches three kernels (prefix, ordering, suffix) and, on the first call on a
- * stream, allocates the prefix kernel's 256-byte work counter.
+ * Launches three kernels on `stream`: the suffix units' ordering, the prefix
+ * (once for all rows, on the tensor cores) and the suffix decode, which runs
+ * beside the prefix kernel and waits for it only to merge its partials. Their
+ * counters live in the workspace; nothing is allocated.
  */
 size_t lk_paged_decode_shared_prefix_workspace_bytes(int32_t B, int32_t H, int32_t H_kv,
                                                       int32_t D, int32_t max_blocks_per_seq,
