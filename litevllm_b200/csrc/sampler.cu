@@ -788,7 +788,10 @@ LK_DEVINL void gumbel_segment(const SampleParams& p, int b, int j0, int j1, bool
       nxt = j + kSampThreads < j1 ? __ldcs(rowv + j + kSampThreads) : zero;
       const uint32_t pm = pmax_nan<T>(pmax_nan<T>(raw.x, raw.y), pmax_nan<T>(raw.z, raw.w));
       const float xm = fmax_nan(half_lo<T>(pm), half_hi<T>(pm));
-      const float qm = dv.in_range(xm) ? dv.fast(xm) : __fdiv_rn(xm, dv.t);
+      // an upper bound of fl(x_max / T) is all the bound needs: x_max RN(1/T)
+      // is within 2^-23 of the quotient, so widening it by 2^-22 covers that
+      const float q0 = xm * dv.y;
+      const float qm = fmaf(fabsf(q0), 2.384185791015625e-07f, q0);
       const float thr = fmaxf(best, ordered_to_float(*static_cast<volatile int*>(&s_best)));
       // logits alone: even the largest noise cannot lift this vector to the
       // best key, so its Philox blocks are not needed either
