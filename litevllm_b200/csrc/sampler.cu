@@ -719,8 +719,10 @@ __global__ void __launch_bounds__(kSampThreads) argmax_bulk_kernel(const SampleP
 // is at most fl(fl(x_max / T) + h(u_max) + margin), where h(u) = -ln(1 - u)
 // >= g(u) = -ln(-ln u) (as -ln u >= 1 - u; one logarithm instead of the
 // map's two and its polynomial, and within 0.05 of g for the u_max near 0.9
-// that the largest of 8 uniforms usually is). Division, h and rounding are
-// monotone, and the errors of g and h are far below the margin, so a vector
+// that the largest of 8 uniforms usually is), and x_max / T is taken as
+// x_max RN(1/T) widened by 2^-22, which is at least the IEEE quotient. That,
+// h and rounding are monotone, and the errors of g and h are far below the
+// margin, so a vector
 // whose bound is below a key already reached in this CTA cannot hold the
 // row's winner (nor tie it) and is skipped after its Philox words. x_max is
 // taken with packed 16-bit max instructions; a vector is widened to fp32
