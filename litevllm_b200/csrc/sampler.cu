@@ -722,13 +722,12 @@ __global__ void __launch_bounds__(kSampThreads) argmax_bulk_kernel(const SampleP
 // that the largest of 8 uniforms usually is), and x_max / T is taken as
 // x_max RN(1/T) widened by 2^-22, which is at least the IEEE quotient. That,
 // h and rounding are monotone, and the errors of g and h are far below the
-// margin, so a vector
-// whose bound is below a key already reached in this CTA cannot hold the
-// row's winner (nor tie it) and is skipped after its Philox words. x_max is
-// taken with packed 16-bit max instructions; a vector is widened to fp32
-// only when its keys are computed. A NaN logit makes the bound NaN: its
-// vector is always computed (a NaN key wins). With a noise dump every key
-// is computed.
+// margin, so a vector whose bound is below a key already reached in this CTA
+// cannot hold the row's winner (nor tie it) and is skipped after its Philox
+// words. x_max is taken with packed 16-bit max instructions; a vector is
+// widened to fp32 only when its keys are computed. A NaN logit makes the
+// bound NaN: its vector is always computed (a NaN key wins). With a noise
+// dump every key is computed.
 template <typename T>
 LK_DEVINL void gumbel_segment(const SampleParams& p, int b, int j0, int j1, bool tail, float temp,
                               float& best, int& besti) {
